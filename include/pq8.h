@@ -1,0 +1,190 @@
+/*
+ * pq8 - B200 (sm_100a) Q8_0-weight x FP32-activation contraction library.
+ *
+ * C ABI: plain pointers and sizes, no exceptions or aborts cross it. Every
+ * function returns 0 on success or an error code: values below 1000 are
+ * CUDA runtime error numbers, values from 1000 up are PQ8_ERR_* below.
+ * pq8_error_string() names any code.
+ *
+ * Pointers marked "device" are device addresses in the current CUDA context
+ * of the calling thread (the primary context, as the reference's ctypes
+ * driver uses it). `stream` is a cudaStream_t / CUstream; NULL is the legacy
+ * default stream, which is what the reference launches on. Work is enqueued
+ * asynchronously on that stream; the library never synchronizes except in
+ * pq8_device_status(). It never allocates device memory: scratch space is a
+ * caller-provided workspace, in the manner of cublasSetWorkspace_v2.
+ *
+ * Weights are kept resident in the "packed Q8_0" device format produced by
+ * pq8_pack_q8_0*() from GGUF Q8_0 blocks (34-byte `<f2 scale><32 x i8>`
+ * records along K, row-major [N, K]): a 256-byte header, then per tile of
+ * 128 weight rows and per 32-wide K block a 4352-byte record holding the
+ * int8 values (16-byte aligned, laid out for coalesced and tensor-memory
+ * access) followed by the 128 fp16 scales. The packed format is what makes
+ * the GGUF blocks, whose 34-byte stride breaks 16-byte TMA alignment,
+ * streamable by bulk copies.
+ *
+ * Reference interfaces replaced (mgostIH/parakeet_cuda):
+ *   - parakeet_cuda/gpu.py:169-184  GPU.load_weights -> dequant_q8 expansion
+ *   - parakeet_cuda/gpu.py:87-90    Blas.linear -> cublasSgemm_v2 (FP32)
+ *   - parakeet_cuda/kernels/runtime.cu:26-33   dequant_q8
+ *   - parakeet_cuda/kernels/runtime.cu:180-188 q8_gemv
+ *   - parakeet_cuda/kernels/runtime.cu:49-62   silu / residual / bias_act / glu epilogues
+ *   - parakeet_cuda/kernels/runtime.cu:155-179 lstm / joint_relu / argmax_tdt
+ *   - kernels/q8_gemm.cu:5-42                  q8_gemm (direct fused-dequant GEMM)
+ */
+#ifndef PQ8_H
+#define PQ8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PQ8_API __attribute__((visibility("default")))
+#else
+#define PQ8_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- error codes (>= 1000; smaller nonzero values are cudaError_t) ---- */
+#define PQ8_OK 0
+#define PQ8_ERR_INVALID_ARGUMENT 1001  /* NULL pointer, negative size, bad enum */
+#define PQ8_ERR_UNSUPPORTED_SHAPE 1002 /* K not a positive multiple of 32, N out of range, ... */
+#define PQ8_ERR_MISALIGNED 1003        /* a pointer does not meet the documented alignment */
+#define PQ8_ERR_ARCH 1004              /* current device is not compute capability 10.0 (sm_100a) */
+#define PQ8_ERR_WORKSPACE 1005         /* workspace NULL or smaller than pq8_*_workspace_size() */
+#define PQ8_ERR_LAYOUT 1006            /* device-side: packed header does not match n/k/layout */
+#define PQ8_ERR_TIMEOUT 1007           /* device-side: a bounded wait inside a kernel expired */
+#define PQ8_ERR_DRIVER 1008            /* CUDA driver entry point missing or tensor-map encode failed */
+
+/* ---- packed weight layouts ---- */
+#define PQ8_LAYOUT_ROWS 0   /* packed row p = source row p */
+#define PQ8_LAYOUT_GLU 1    /* rows j and j+N/2 paired in one warp; output width N/2 */
+#define PQ8_LAYOUT_GATES4 2 /* LSTM gates i,f,g,o of one hidden unit in one tile column; output width N/4 */
+
+/* ---- epilogues (applied to z = acc + bias; bias may be NULL) ---- */
+#define PQ8_EPI_NONE 0     /* y = z                              (Blas.linear, + bias_act relu=0) */
+#define PQ8_EPI_RELU 1     /* y = max(z, 0)                      (bias_act relu=1) */
+#define PQ8_EPI_SILU 2     /* y = z * sigmoid(z)                 (FFN linear1 + silu) */
+#define PQ8_EPI_GLU 3      /* y[:, j] = z[:, j] * sigmoid(z[:, j+N/2])   (pointwise_conv1 + glu; GLU layout) */
+#define PQ8_EPI_RESIDUAL 4 /* y = resid + alpha * z              (linear + residual; y may alias resid) */
+
+/* ---- flags ---- */
+#define PQ8_FLAG_X_TF32 1   /* x already holds TF32-rounded values: skip the in-kernel rounding pass */
+#define PQ8_FLAG_OUT_TF32 2 /* round y to TF32 (nearest) so that it can feed another GEMM with PQ8_FLAG_X_TF32 */
+
+#define PQ8_HEADER_BYTES 256
+#define PQ8_TILE_ROWS 128
+#define PQ8_RECORD_BYTES 4352 /* 128 rows x 32 int8 + 128 fp16 scales */
+#define PQ8_GEMV_MAX_M 8      /* pq8_gemv handles m <= 8; pq8_linear sends larger m to pq8_gemm */
+
+/* Name of an error code (static string; never NULL). */
+PQ8_API const char* pq8_error_string(int code);
+
+/* Library version as major*10000 + minor*100 + patch. */
+PQ8_API int pq8_version(void);
+
+/* ---- host-side packing (no GPU needed) ---------------------------------
+ * Replaces the per-layer upload + dequant_q8 expansion of GPU.load_weights
+ * (parakeet_cuda/gpu.py:169-184): the Q8_0 bytes stay Q8_0, only their order
+ * changes, and the result is uploaded once and kept resident.
+ */
+
+/* Bytes of a packed tensor of n rows x k columns in `layout`. */
+PQ8_API int pq8_packed_size(int n, int k, int layout, size_t* bytes);
+
+/* Pack GGUF Q8_0 blocks (host memory, n*k/32 records of 34 bytes, row-major
+ * [n, k] as gguf.Model.raw() returns them, parakeet_cuda/gguf.py:135-138)
+ * into `packed` (host memory, pq8_packed_size() bytes). */
+PQ8_API int pq8_pack_q8_0(const void* gguf_blocks, int n, int k, int layout, void* packed);
+
+/* Pack a [n, k_src] source into columns [k_offset, k_offset + k_src) of a
+ * packed [n, k_total] tensor (k_offset and k_src multiples of 32). Used to
+ * concatenate the LSTM input and hidden weights along K
+ * (decoder.py:58-61 computes W_ih x + W_hh h). The first call on a buffer
+ * must have k_offset == 0: it writes the header and zero-fills padding. */
+PQ8_API int pq8_pack_q8_0_part(const void* gguf_blocks, int n, int k_src, int k_total, int k_offset,
+                       int layout, void* packed);
+
+/* ---- device kernels ------------------------------------------------------ */
+
+/* Q8_0 -> FP32 expansion, bit-identical to dequant_q8 (runtime.cu:26-33).
+ * gguf_blocks: device, n_elements/32 records of 34 bytes; out: device float[n_elements]. */
+PQ8_API int pq8_dequant_q8_0(const void* gguf_blocks, float* out, long long n_elements, void* stream);
+
+/* Tensor-core GEMM (tcgen05, TF32 operands rounded to nearest, FP32 accumulate):
+ *   z[m, j] = sum_k x[m, k] * W[j, k]  (+ bias[j]),  y = epilogue(z)
+ * Replaces Blas.linear (gpu.py:87-90) + the elementwise epilogue kernels.
+ *   w      device, packed ROWS or GLU layout with n rows, k columns
+ *   x      device, float[m][k], 16-byte aligned, row stride k
+ *   y      device, float[m][out], out = n (ROWS) or n/2 (GLU); may alias resid
+ *   bias   device float[n] or NULL
+ *   resid  device float[m][out] (EPI_RESIDUAL only)
+ * Any m >= 0; k a positive multiple of 32; n >= 1. */
+PQ8_API int pq8_gemm(const void* w, const float* x, float* y, const float* bias, const float* resid,
+             int m, int n, int k, int epilogue, float alpha, int flags, void* stream);
+
+/* Workspace bytes needed by pq8_gemv / pq8_lstm_layer / pq8_joint_argmax for
+ * this shape on the current device. */
+PQ8_API int pq8_gemv_workspace_size(int m, int n, int k, size_t* bytes);
+
+/* Zero a workspace before its first use (its counters reset themselves
+ * after every call, so this is needed once per buffer). */
+PQ8_API int pq8_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* HBM-streaming GEMV for the decoder regime, 1 <= m <= PQ8_GEMV_MAX_M:
+ * y = epilogue(x @ W^T + bias). Deterministic: fixed summation order
+ * (split-K partials are combined in split order by the last CTA).
+ * Replaces q8_gemv (runtime.cu:180-188) and the M=1 Blas.linear calls of
+ * CUDADecoder (decoder.py:50-52). Arguments as pq8_gemm plus the workspace. */
+PQ8_API int pq8_gemv(const void* w, const float* x, float* y, const float* bias, const float* resid,
+             int m, int n, int k, int epilogue, float alpha, void* workspace, size_t workspace_bytes,
+             void* stream);
+
+/* Dispatch by m: pq8_gemv for m <= PQ8_GEMV_MAX_M (needs the workspace),
+ * otherwise pq8_gemm. The drop-in for Blas.linear (gpu.py:87-90). */
+PQ8_API int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid,
+               int m, int n, int k, int epilogue, float alpha, int flags, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* One LSTM layer of the TDT prediction network for m <= PQ8_GEMV_MAX_M streams:
+ *   gates = W_ih x + W_hh h + bias, c' = s(f) c + s(i) tanh(g), h' = s(o) tanh(c')
+ * W is GATES4-packed [4H, in_k + H] = [W_ih | W_hh] (pq8_pack_q8_0_part twice);
+ * bias = b_ih + b_hh (float[4H]). x: float[m][in_k], or, when embed_f16 is
+ * not NULL, rows embed_f16[tokens[i]] of an fp16 [vocab][in_k] table
+ * (decoder.py:55 looks the embedding up on the host). h, c: float[m][H];
+ * h_out, c_out: float[m][H] (must not alias h, c).
+ * Replaces 2 Blas.linear + lstm (decoder.py:58-62, runtime.cu:155-163). */
+PQ8_API int pq8_lstm_layer(const void* w, const float* x, const uint16_t* embed_f16, const int* tokens,
+                   const float* h, const float* c, const float* bias, float* h_out, float* c_out,
+                   int m, int hidden, int in_k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* TDT joint for m <= PQ8_GEMV_MAX_M streams: logits = W relu(enc + pred) + bias,
+ * then ids[i] = {argmax logits[i][0:vocab), argmax logits[i][vocab:n)} with ties
+ * to the lowest index. enc: float[R][k]; row i of the activation uses enc row
+ * enc_rows[i] (device int[m]) or, when enc_rows is NULL, row i. pred:
+ * float[m][k]; logits: float[m][n]; ids: int[m][2].
+ * Replaces joint_relu + Blas.linear + bias_act + argmax_tdt (decoder.py:66-72,
+ * runtime.cu:164-179). */
+PQ8_API int pq8_joint_argmax(const void* w, const float* enc, const int* enc_rows, const float* pred,
+                             const float* bias, float* logits, int* ids, int m, int n, int k, int vocab,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Commit the candidate LSTM state of the streams whose mask[i] != 0:
+ * h[l][i][:] = h_new[l][i][:], c[l][i][:] = c_new[l][i][:] for l < layers.
+ * State buffers are float[layers][m][hidden]. decoder.py:74-75 does this by
+ * swapping the buffers of its single stream. */
+PQ8_API int pq8_tdt_commit(float* h, float* c, const float* h_new, const float* c_new, const int* mask, int m,
+                           int layers, int hidden, void* stream);
+
+/* Read and clear the device-side status word that kernels set on a layout
+ * mismatch or an expired bounded wait. Synchronizes `stream`. *status = 0 or
+ * PQ8_ERR_LAYOUT / PQ8_ERR_TIMEOUT. */
+PQ8_API int pq8_device_status(int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PQ8_H */

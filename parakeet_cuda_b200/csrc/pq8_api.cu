@@ -1,0 +1,436 @@
+// C ABI of libpq8: argument checking, per-device state, tile-shape choice and
+// kernel launches. See include/pq8.h for the contract of each entry point.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+
+#include "pq8.h"
+#include "pq8_device.cuh"
+#include "pq8_gemm.cuh"
+#include "pq8_gemv.cuh"
+
+namespace pq8 {
+
+__device__ int g_status;  // device-side error word (PQ8_ERR_LAYOUT / PQ8_ERR_TIMEOUT)
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool ready = false;
+  int sms = 0;
+  int* status = nullptr;
+  bool attr_set[8] = {};
+};
+
+std::mutex g_mutex;
+DeviceState g_dev[kMaxDevices];
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int to_code(cudaError_t e) { return e == cudaSuccess ? PQ8_OK : static_cast<int>(e); }
+
+// Current device's state; checks compute capability 10.0 on first use.
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return to_code(e);
+  if (dev < 0 || dev >= kMaxDevices) return PQ8_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& s = g_dev[dev];
+  if (!s.ready) {
+    int major = 0, minor = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess) return to_code(e);
+    if ((e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess) return to_code(e);
+    if (major != 10 || minor != 0) return PQ8_ERR_ARCH;
+    if ((e = cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return to_code(e);
+    void* sym = nullptr;
+    if ((e = cudaGetSymbolAddress(&sym, g_status)) != cudaSuccess) return to_code(e);
+    s.status = static_cast<int*>(sym);
+    s.ready = true;
+  }
+  *out = &s;
+  return PQ8_OK;
+}
+
+int encode_fn(EncodeTiledFn* fn) {
+  std::call_once(g_encode_once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  *fn = g_encode;
+  return g_encode ? PQ8_OK : PQ8_ERR_DRIVER;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ---------------------------------------------------------------- GEMM
+template <int BN, int STAGES, int ACC>
+int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaStream_t st) {
+  using C = GemmCfg<BN, STAGES, ACC>;
+  EncodeTiledFn enc;
+  int rc = encode_fn(&enc);
+  if (rc) return rc;
+  CUtensorMap tmap;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.k), static_cast<cuuint64_t>(p.m)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.k) * sizeof(float)};
+  const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(BN)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return PQ8_ERR_DRIVER;
+  auto kernel = gemm_tc_kernel<BN, STAGES, ACC>;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!ds->attr_set[cfg_id]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+      if (e != cudaSuccess) return to_code(e);
+      ds->attr_set[cfg_id] = true;
+    }
+  }
+  p.m_tiles = (p.m + BN - 1) / BN;
+  const int tiles = p.n_tiles * p.m_tiles;
+  const int grid = std::min(tiles, ds->sms);
+  kernel<<<grid, C::kThreads, C::kSmemBytes, st>>>(tmap, p);
+  return to_code(cudaGetLastError());
+}
+
+// Activation-tile height: fewest waves x (BN + fixed per-K-block cost).
+// PQ8_GEMM_BN=64|128|256 in the environment forces one (used by the tests to
+// cover every tile configuration).
+int choose_bn(int m, int n_tiles, int sms) {
+  if (const char* force = std::getenv("PQ8_GEMM_BN")) {
+    const int v = std::atoi(force);
+    if (v == 64 || v == 128 || v == 256) return v;
+  }
+  const int options[3] = {256, 128, 64};
+  int best = 256;
+  long best_cost = -1;
+  for (int bn : options) {
+    const long tiles = static_cast<long>(n_tiles) * ((m + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    const long cost = waves * (bn + 48);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+// ---------------------------------------------------------------- GEMV
+struct GemvPlan {
+  int mt, splits, kbps;
+  size_t off_tickets, off_done, off_bval, off_bidx, off_partial, total;
+};
+
+size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
+
+GemvPlan plan_gemv(int m, int n, int k, int sms) {
+  GemvPlan g{};
+  g.mt = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+  const int n_tiles = (n + kTileRows - 1) / kTileRows;
+  const int kb = k / 32;
+  int splits = std::max(1, std::min(kb, (2 * sms + n_tiles - 1) / n_tiles));
+  int kbps = (kb + splits - 1) / splits;
+  const int max_kbps = kGemvXSmemFloats / (32 * g.mt);
+  if (kbps > max_kbps) kbps = max_kbps;
+  splits = (kb + kbps - 1) / kbps;
+  g.splits = splits;
+  g.kbps = kbps;
+  size_t off = 0;
+  g.off_tickets = off;
+  off += round256(sizeof(int) * n_tiles);
+  g.off_done = off;
+  off += 256;
+  g.off_bval = off;
+  off += round256(sizeof(float) * n_tiles * g.mt * 2);
+  g.off_bidx = off;
+  off += round256(sizeof(int) * n_tiles * g.mt * 2);
+  g.off_partial = off;
+  off += (splits > 1) ? round256(sizeof(float) * (size_t)n_tiles * splits * kTileRows * g.mt) : 0;
+  g.total = off;
+  return g;
+}
+
+int launch_gemv(DeviceState* ds, GemvParams p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const GemvPlan g = plan_gemv(p.m, p.n, p.k, ds->sms);
+  if (ws == nullptr || ws_bytes < g.total) return PQ8_ERR_WORKSPACE;
+  if (!aligned(ws, 256)) return PQ8_ERR_MISALIGNED;
+  auto* base = static_cast<unsigned char*>(ws);
+  p.splits = g.splits;
+  p.kb_per_split = g.kbps;
+  p.tickets = reinterpret_cast<int*>(base + g.off_tickets);
+  p.done_count = reinterpret_cast<int*>(base + g.off_done);
+  p.best_val = reinterpret_cast<float*>(base + g.off_bval);
+  p.best_idx = reinterpret_cast<int*>(base + g.off_bidx);
+  p.partial = reinterpret_cast<float*>(base + g.off_partial);
+  p.status = ds->status;
+  const int grid = p.n_tiles * g.splits;
+  switch (g.mt) {
+    case 1: gemv_kernel<1><<<grid, kGemvThreads, 0, st>>>(p); break;
+    case 2: gemv_kernel<2><<<grid, kGemvThreads, 0, st>>>(p); break;
+    case 4: gemv_kernel<4><<<grid, kGemvThreads, 0, st>>>(p); break;
+    default: gemv_kernel<8><<<grid, kGemvThreads, 0, st>>>(p); break;
+  }
+  return to_code(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- dequant
+__global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restrict__ out, long long blocks) {
+  const long long b = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= blocks) return;
+  const uint8_t* rec = src + b * 34;
+  const float s = __half2float(__ushort_as_half(static_cast<uint16_t>(rec[0] | (rec[1] << 8))));
+  float* o = out + b * 32;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) o[i] = s * static_cast<float>(static_cast<int8_t>(rec[2 + i]));
+}
+
+int check_linear_args(const void* w, const float* x, const float* y, const float* resid, int m, int n, int k,
+                      int epi) {
+  if (m < 0 || n < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (k <= 0 || k % 32) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (epi < PQ8_EPI_NONE || epi > PQ8_EPI_RESIDUAL) return PQ8_ERR_INVALID_ARGUMENT;
+  if (epi == PQ8_EPI_GLU && n % 2) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (m == 0) return PQ8_OK;
+  if (w == nullptr || x == nullptr || y == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (epi == PQ8_EPI_RESIDUAL && resid == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(w, 16)) return PQ8_ERR_MISALIGNED;
+  return PQ8_OK;
+}
+
+}  // namespace
+}  // namespace pq8
+
+using namespace pq8;
+
+extern "C" const char* pq8_error_string(int code) {
+  switch (code) {
+    case PQ8_OK: return "PQ8_OK";
+    case PQ8_ERR_INVALID_ARGUMENT: return "PQ8_ERR_INVALID_ARGUMENT: NULL pointer, negative size or unknown enum";
+    case PQ8_ERR_UNSUPPORTED_SHAPE: return "PQ8_ERR_UNSUPPORTED_SHAPE: K must be a positive multiple of 32";
+    case PQ8_ERR_MISALIGNED: return "PQ8_ERR_MISALIGNED: pointer alignment requirement not met";
+    case PQ8_ERR_ARCH: return "PQ8_ERR_ARCH: current device is not sm_100 (B200)";
+    case PQ8_ERR_WORKSPACE: return "PQ8_ERR_WORKSPACE: workspace missing or too small";
+    case PQ8_ERR_LAYOUT: return "PQ8_ERR_LAYOUT: packed weight header does not match n/k/layout";
+    case PQ8_ERR_TIMEOUT: return "PQ8_ERR_TIMEOUT: a bounded wait inside a kernel expired";
+    case PQ8_ERR_DRIVER: return "PQ8_ERR_DRIVER: CUDA driver entry point unavailable or tensor map rejected";
+    default:
+      if (code > 0 && code < 1000) return cudaGetErrorString(static_cast<cudaError_t>(code));
+      return "unknown pq8 error";
+  }
+}
+
+extern "C" int pq8_version(void) { return 100; }
+
+extern "C" int pq8_dequant_q8_0(const void* gguf_blocks, float* out, long long n_elements, void* stream) {
+  if (n_elements < 0 || n_elements % 32) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (n_elements == 0) return PQ8_OK;
+  if (gguf_blocks == nullptr || out == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  const long long blocks = n_elements / 32;
+  const int threads = 256;
+  const long long grid = (blocks + threads - 1) / threads;
+  dequant_kernel<<<static_cast<unsigned>(grid), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(gguf_blocks), out, blocks);
+  return to_code(cudaGetLastError());
+}
+
+extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bias, const float* resid, int m, int n,
+                        int k, int epilogue, float alpha, int flags, void* stream) {
+  int rc = check_linear_args(w, x, y, resid, m, n, k, epilogue);
+  if (rc || m == 0) return rc;
+  if (!aligned(x, 16)) return PQ8_ERR_MISALIGNED;
+  if (flags & ~(PQ8_FLAG_X_TF32 | PQ8_FLAG_OUT_TF32)) return PQ8_ERR_INVALID_ARGUMENT;
+  DeviceState* ds;
+  if ((rc = device_state(&ds))) return rc;
+  GemmParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.y = y;
+  p.bias = bias;
+  p.resid = resid;
+  p.status = ds->status;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.epi = epilogue;
+  p.alpha = alpha;
+  p.flags = flags;
+  p.layout = epilogue == PQ8_EPI_GLU ? PQ8_LAYOUT_GLU : PQ8_LAYOUT_ROWS;
+  p.out_cols = epilogue == PQ8_EPI_GLU ? n / 2 : n;
+  p.n_tiles = (n + kTileRows - 1) / kTileRows;
+  p.k_blocks = k / 32;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (choose_bn(m, p.n_tiles, ds->sms)) {
+    case 256: return launch_gemm<256, 5, 1>(ds, 0, x, p, st);
+    case 128: return launch_gemm<128, 6, 2>(ds, 1, x, p, st);
+    default: return launch_gemm<64, 8, 2>(ds, 2, x, p, st);
+  }
+}
+
+extern "C" int pq8_gemv_workspace_size(int m, int n, int k, size_t* bytes) {
+  if (bytes == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (m < 1 || m > PQ8_GEMV_MAX_M || n < 1 || k <= 0 || k % 32) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  *bytes = plan_gemv(m, n, k, ds->sms).total;
+  return PQ8_OK;
+}
+
+extern "C" int pq8_workspace_init(void* workspace, size_t bytes, void* stream) {
+  if (workspace == nullptr && bytes) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!bytes) return PQ8_OK;
+  return to_code(cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int pq8_gemv(const void* w, const float* x, float* y, const float* bias, const float* resid, int m, int n,
+                        int k, int epilogue, float alpha, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_linear_args(w, x, y, resid, m, n, k, epilogue);
+  if (rc || m == 0) return rc;
+  if (m > PQ8_GEMV_MAX_M) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  DeviceState* ds;
+  if ((rc = device_state(&ds))) return rc;
+  GemvParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.x0 = x;
+  p.x_mode = kXPlain;
+  p.y = y;
+  p.bias = bias;
+  p.resid = resid;
+  p.alpha = alpha;
+  p.epi = epilogue;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.layout = epilogue == PQ8_EPI_GLU ? PQ8_LAYOUT_GLU : PQ8_LAYOUT_ROWS;
+  p.out_cols = epilogue == PQ8_EPI_GLU ? n / 2 : n;
+  p.n_tiles = (n + kTileRows - 1) / kTileRows;
+  p.k_blocks = k / 32;
+  p.mode = kGemvLinear;
+  return launch_gemv(ds, p, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid, int m,
+                          int n, int k, int epilogue, float alpha, int flags, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  if (m >= 1 && m <= PQ8_GEMV_MAX_M)
+    return pq8_gemv(w, x, y, bias, resid, m, n, k, epilogue, alpha, workspace, workspace_bytes, stream);
+  return pq8_gemm(w, x, y, bias, resid, m, n, k, epilogue, alpha, flags, stream);
+}
+
+extern "C" int pq8_lstm_layer(const void* w, const float* x, const uint16_t* embed_f16, const int* tokens,
+                              const float* h, const float* c, const float* bias, float* h_out, float* c_out, int m,
+                              int hidden, int in_k, void* workspace, size_t workspace_bytes, void* stream) {
+  if (m < 1 || m > PQ8_GEMV_MAX_M || hidden < 1 || in_k <= 0 || in_k % 32 || hidden % 32)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (w == nullptr || h == nullptr || c == nullptr || h_out == nullptr || c_out == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  if (embed_f16 == nullptr ? x == nullptr : tokens == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (h_out == h || c_out == c) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(w, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  GemvParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.x0 = x;
+  p.x1 = h;
+  p.embed = embed_f16;
+  p.tokens = tokens;
+  p.x_mode = embed_f16 ? kXEmbedConcat : kXConcat;
+  p.k0 = in_k;
+  p.bias = bias;
+  p.m = m;
+  p.n = 4 * hidden;
+  p.k = in_k + hidden;
+  p.layout = PQ8_LAYOUT_GATES4;
+  p.out_cols = hidden;
+  p.n_tiles = (p.n + kTileRows - 1) / kTileRows;
+  p.k_blocks = p.k / 32;
+  p.c_prev = c;
+  p.h_out = h_out;
+  p.c_out = c_out;
+  p.hidden = hidden;
+  p.mode = kGemvLstm;
+  return launch_gemv(ds, p, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pq8_joint_argmax(const void* w, const float* enc, const int* enc_rows, const float* pred,
+                                const float* bias, float* logits, int* ids, int m, int n, int k, int vocab,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (m < 1 || m > PQ8_GEMV_MAX_M || n < 2 || k <= 0 || k % 32 || vocab < 1 || vocab >= n)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (w == nullptr || enc == nullptr || pred == nullptr || logits == nullptr || ids == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(w, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  GemvParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.x0 = enc;
+  p.x0_rows = enc_rows;
+  p.x1 = pred;
+  p.x_mode = kXReluSum;
+  p.y = logits;
+  p.bias = bias;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.layout = PQ8_LAYOUT_ROWS;
+  p.out_cols = n;
+  p.n_tiles = (n + kTileRows - 1) / kTileRows;
+  p.k_blocks = k / 32;
+  p.ids = ids;
+  p.vocab = vocab;
+  p.mode = kGemvJoint;
+  return launch_gemv(ds, p, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pq8_tdt_commit(float* h, float* c, const float* h_new, const float* c_new, const int* mask, int m,
+                              int layers, int hidden, void* stream) {
+  if (m < 0 || layers < 1 || hidden < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (m == 0) return PQ8_OK;
+  if (h == nullptr || c == nullptr || h_new == nullptr || c_new == nullptr || mask == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  const long long total = (long long)layers * m * hidden;
+  const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * ds->sms);
+  tdt_commit_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(h, c, h_new, c_new, mask, m, layers,
+                                                                         hidden);
+  return to_code(cudaGetLastError());
+}
+
+extern "C" int pq8_device_status(int* status, void* stream) {
+  if (status == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int value = 0;
+  cudaError_t e = cudaMemcpyAsync(&value, ds->status, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ds->status, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return to_code(e);
+  *status = value;
+  return PQ8_OK;
+}

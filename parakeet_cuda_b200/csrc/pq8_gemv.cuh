@@ -1,0 +1,306 @@
+// Decoder-regime contraction (m <= 8 activation rows): an HBM-streaming,
+// split-K GEMV over the packed Q8_0 records, with the TDT tails fused.
+//
+// One CTA of 128 threads handles one 128-row weight tile over a range of K
+// blocks; thread r owns tile row r, so the reduction over K is thread-local
+// and needs no shuffles. Each thread streams its row's 2 x 16 bytes of int8
+// values and its fp16 scale per K block with 128-bit non-allocating loads
+// (a warp reads 512 contiguous bytes per instruction). The activations of
+// the CTA's K range are staged once in shared memory and read as broadcasts.
+//
+// When a tile's K range is split over several CTAs, each writes its partial
+// sums to the workspace and the last CTA to arrive (atomic ticket) adds the
+// partials in split order and runs the epilogue, so results do not depend on
+// CTA timing. Tickets reset themselves, so a zeroed workspace stays valid
+// across calls.
+//
+// Modes: plain linear (bias / ReLU / SiLU / GLU / residual epilogues), one
+// LSTM layer (GATES4 layout: the four gates of 32 hidden units per tile are
+// combined in shared memory and the cell update runs in the epilogue), and
+// the TDT joint (ReLU(enc + pred) staged as the activation; per-tile argmax
+// partials reduced by the last tile to finish).
+#pragma once
+
+#include <float.h>
+#include <limits.h>
+
+#include "pq8_device.cuh"
+
+namespace pq8 {
+
+enum GemvMode { kGemvLinear = 0, kGemvLstm = 1, kGemvJoint = 2 };
+enum XMode { kXPlain = 0, kXConcat = 1, kXReluSum = 2, kXEmbedConcat = 3 };
+
+struct GemvParams {
+  const uint8_t* w;
+  const float* x0;
+  const float* x1;
+  const uint16_t* embed;
+  const int* tokens;
+  const int* x0_rows;  // optional row indices into x0 (joint: frame of each stream)
+  int x_mode;
+  int k0;  // width of the first segment in concat modes
+  float* y;
+  const float* bias;
+  const float* resid;
+  float alpha;
+  int epi;
+  int m, n, k, layout, out_cols, n_tiles, k_blocks, splits, kb_per_split;
+  float* partial;  // [n_tiles][splits][128][MT]
+  int* tickets;    // [n_tiles]
+  int* done_count; // joint: tiles finished
+  float* best_val; // joint: [n_tiles][m][2]
+  int* best_idx;
+  const float* c_prev;
+  float* h_out;
+  float* c_out;
+  int hidden;
+  int* ids;
+  int vocab;
+  int mode;
+  int* status;
+};
+
+constexpr int kGemvThreads = 128;
+constexpr int kGemvXSmemFloats = 10240;  // 40 KB of staged activations per CTA
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint16_t ldg_u16(const void* p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+// Activation element (row m, column kg) for the staged modes.
+__device__ __forceinline__ float load_x(const GemvParams& p, int m, int kg) {
+  switch (p.x_mode) {
+    case kXConcat:
+      return kg < p.k0 ? p.x0[(size_t)m * p.k0 + kg] : p.x1[(size_t)m * (p.k - p.k0) + (kg - p.k0)];
+    case kXReluSum: {
+      const size_t row = p.x0_rows ? (size_t)p.x0_rows[m] : (size_t)m;
+      return fmaxf(p.x0[row * p.k + kg] + p.x1[(size_t)m * p.k + kg], 0.0f);
+    }
+    case kXEmbedConcat:
+      return kg < p.k0 ? __half2float(__ushort_as_half(p.embed[(size_t)p.tokens[m] * p.k0 + kg]))
+                       : p.x1[(size_t)m * (p.k - p.k0) + (kg - p.k0)];
+    default:
+      return p.x0[(size_t)m * p.k + kg];
+  }
+}
+
+// (value, index) arg-max with ties to the lowest index.
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float ov, int oi) {
+  if (ov > v || (ov == v && oi < i)) {
+    v = ov;
+    i = oi;
+  }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) {
+  __shared__ float xs[kGemvXSmemFloats];
+  __shared__ float gate_s[MT][4][32];
+  __shared__ float red_v[4][MT][2];
+  __shared__ int red_i[4][MT][2];
+  __shared__ int ticket_s;
+
+  const int t = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
+  const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+  const int nk = (kb1 - kb0) * 32;
+
+  if (r == 0 && blockIdx.x == 0) {
+    const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
+    if (!(h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout && h->n_tiles == p.n_tiles))
+      atomicCAS(p.status, 0, PQ8_ERR_LAYOUT);
+  }
+
+  // Stage the activations of this CTA's K range: xs[m * nk + kk].
+  for (int i = r; i < MT * nk; i += kGemvThreads) {
+    const int m = i / nk, kk = i - m * nk;
+    xs[i] = (m < p.m) ? load_x(p, m, kb0 * 32 + kk) : 0.0f;
+  }
+  __syncthreads();
+
+  float acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+
+  const uint8_t* tile_base = p.w + PQ8_HEADER_BYTES + (size_t)t * p.k_blocks * kRecordBytes;
+#pragma unroll 2
+  for (int kb = kb0; kb < kb1; ++kb) {
+    const uint8_t* rec = tile_base + (size_t)kb * kRecordBytes;
+    const uint4 q0 = ldg_stream(rec + r * 16);
+    const uint4 q1 = ldg_stream(rec + 2048 + r * 16);
+    const float sc = __half2float(__ushort_as_half(ldg_u16(rec + kScaleOffset + r * 2)));
+    const uint32_t wd[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
+                            q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
+    const float* xk = xs + (kb - kb0) * 32;
+    float inner[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) inner[m] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float q_0 = i8_to_f32(wd[j >> 2], 0), q_1 = i8_to_f32(wd[j >> 2], 1);
+      const float q_2 = i8_to_f32(wd[j >> 2], 2), q_3 = i8_to_f32(wd[j >> 2], 3);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        const float4 xv = *reinterpret_cast<const float4*>(xk + m * nk + j);
+        inner[m] = fmaf(q_0, xv.x, inner[m]);
+        inner[m] = fmaf(q_1, xv.y, inner[m]);
+        inner[m] = fmaf(q_2, xv.z, inner[m]);
+        inner[m] = fmaf(q_3, xv.w, inner[m]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = fmaf(sc, inner[m], acc[m]);
+  }
+
+  if (p.splits > 1) {
+    float* mine = p.partial + (((size_t)t * p.splits + split) * kGemvThreads + r) * MT;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) __stcg(mine + m, acc[m]);
+    __threadfence();
+    __syncthreads();
+    if (r == 0) ticket_s = atomicAdd(&p.tickets[t], 1);
+    __syncthreads();
+    if (ticket_s != p.splits - 1) return;
+    __threadfence();
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float* part = p.partial + (((size_t)t * p.splits + s) * kGemvThreads + r) * MT;
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[m] += __ldcg(part + m);
+    }
+    if (r == 0) p.tickets[t] = 0;
+  }
+
+  RowMap rm;
+  const bool valid = map_row(p.layout, p.n, t * kTileRows + r, rm);
+  const float b = (p.bias != nullptr && valid) ? p.bias[rm.src] : 0.0f;
+
+  if (p.mode == kGemvLinear) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      if (m >= p.m) break;
+      const float z = acc[m] + b;
+      float out;
+      if (p.epi == PQ8_EPI_GLU) {
+        const float gate = __shfl_down_sync(0xffffffffu, z, 16);
+        out = z * sigmoidf_(gate);
+      } else if (p.epi == PQ8_EPI_RESIDUAL) {
+        out = valid ? p.resid[(size_t)m * p.out_cols + rm.col] + p.alpha * z : 0.0f;
+      } else {
+        out = apply_act(z, p.epi);
+      }
+      if (valid && (p.epi != PQ8_EPI_GLU || lane < 16)) p.y[(size_t)m * p.out_cols + rm.col] = out;
+    }
+    return;
+  }
+
+  if (p.mode == kGemvLstm) {
+    // Tile row r holds gate (r / 32) of hidden unit t*32 + r%32.
+#pragma unroll
+    for (int m = 0; m < MT; ++m) gate_s[m][warp][lane] = acc[m] + b;
+    __syncthreads();
+    if (warp == 0) {
+      const int u = t * 32 + lane;
+      if (u < p.hidden) {
+        for (int m = 0; m < p.m && m < MT; ++m) {
+          const float gi = gate_s[m][0][lane], gf = gate_s[m][1][lane];
+          const float gg = gate_s[m][2][lane], go = gate_s[m][3][lane];
+          const float si = 1.0f / (1.0f + expf(-gi)), sf = 1.0f / (1.0f + expf(-gf));
+          const float so = 1.0f / (1.0f + expf(-go));
+          const float c = sf * p.c_prev[(size_t)m * p.hidden + u] + si * tanhf(gg);
+          p.c_out[(size_t)m * p.hidden + u] = c;
+          p.h_out[(size_t)m * p.hidden + u] = so * tanhf(c);
+        }
+      }
+    }
+    return;
+  }
+
+  // Joint: logits, then per-tile arg-max partials for tokens / durations.
+  float bv[MT][2];
+  int bi[MT][2];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const float z = acc[m] + b;
+    if (valid && m < p.m) p.y[(size_t)m * p.n + rm.src] = z;
+    const bool tok = valid && rm.src < p.vocab, dur = valid && rm.src >= p.vocab;
+    bv[m][0] = tok ? z : -INFINITY;
+    bi[m][0] = tok ? rm.src : INT_MAX;
+    bv[m][1] = dur ? z : -INFINITY;
+    bi[m][1] = dur ? rm.src : INT_MAX;
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      float v = bv[m][part];
+      int i = bi[m][part];
+#pragma unroll
+      for (int off = 16; off; off >>= 1) {
+        const float ov = __shfl_down_sync(0xffffffffu, v, off);
+        const int oi = __shfl_down_sync(0xffffffffu, i, off);
+        argmax_merge(v, i, ov, oi);
+      }
+      if (lane == 0) {
+        red_v[warp][m][part] = v;
+        red_i[warp][m][part] = i;
+      }
+    }
+  __syncthreads();
+  if (r < MT * 2) {
+    const int m = r >> 1, part = r & 1;
+    float v = red_v[0][m][part];
+    int i = red_i[0][m][part];
+    for (int w = 1; w < 4; ++w) argmax_merge(v, i, red_v[w][m][part], red_i[w][m][part]);
+    __stcg(p.best_val + ((size_t)t * MT + m) * 2 + part, v);
+    __stcg(p.best_idx + ((size_t)t * MT + m) * 2 + part, i);
+  }
+  __threadfence();
+  __syncthreads();
+  if (r == 0) ticket_s = atomicAdd(p.done_count, 1);
+  __syncthreads();
+  if (ticket_s != p.n_tiles - 1) return;
+  __threadfence();
+  if (r < MT * 2) {
+    const int m = r >> 1, part = r & 1;
+    if (m < p.m) {
+      float v = -INFINITY;
+      int i = INT_MAX;
+      for (int tt = 0; tt < p.n_tiles; ++tt)
+        argmax_merge(v, i, __ldcg(p.best_val + ((size_t)tt * MT + m) * 2 + part),
+                     __ldcg(p.best_idx + ((size_t)tt * MT + m) * 2 + part));
+      p.ids[m * 2 + part] = (i == INT_MAX) ? 0 : i - (part ? p.vocab : 0);
+    }
+  }
+  if (r == 0) *p.done_count = 0;
+}
+
+// TDT commit: rows whose mask is set take the candidate LSTM state
+// (decoder.py:74-75 swaps the buffers of its single stream).
+__global__ void tdt_commit_kernel(float* __restrict__ h, float* __restrict__ c, const float* __restrict__ hn,
+                                  const float* __restrict__ cn, const int* __restrict__ mask, int m, int layers,
+                                  int hidden) {
+  const long long total = (long long)layers * m * hidden;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)((i / hidden) % m);
+    if (mask[row]) {
+      h[i] = hn[i];
+      c[i] = cn[i];
+    }
+  }
+}
+
+}  // namespace pq8

@@ -1,0 +1,116 @@
+"""ctypes binding of libpq8.so, in the style of the reference's Driver adapter.
+
+The reference drives CUDA through ctypes (``parakeet_cuda/cuda_driver.py:29-118``)
+and turns every nonzero status into ``RuntimeError`` (``cuda_driver.py:90-96``,
+``gpu.py:83-85``). This module does the same for the pq8 C ABI declared in
+``include/pq8.h``: ``Library.call(name, *args)`` raises ``PQ8Error`` (a
+``RuntimeError``) carrying the library's error string and code.
+
+Device pointers are passed as Python ints (``c_void_p``), exactly as the
+reference marshals its ``Buffer`` objects (``gpu.py:147-153``). There is no
+CPU fallback: loading fails loudly when the shared library is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+import re
+
+LIB_PATH = Path(__file__).resolve().parent / 'libpq8.so'
+HEADER = Path(__file__).resolve().parents[1] / 'include' / 'pq8.h'
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1001
+ERR_UNSUPPORTED_SHAPE = 1002
+ERR_MISALIGNED = 1003
+ERR_ARCH = 1004
+ERR_WORKSPACE = 1005
+ERR_LAYOUT = 1006
+ERR_TIMEOUT = 1007
+ERR_DRIVER = 1008
+
+LAYOUT_ROWS, LAYOUT_GLU, LAYOUT_GATES4 = 0, 1, 2
+EPI_NONE, EPI_RELU, EPI_SILU, EPI_GLU, EPI_RESIDUAL = 0, 1, 2, 3, 4
+FLAG_X_TF32, FLAG_OUT_TF32 = 1, 2
+HEADER_BYTES, TILE_ROWS, RECORD_BYTES = 256, 128, 4352
+GEMV_MAX_M = 8
+
+_P, _I, _F, _SZ, _LL = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_longlong
+
+SIGNATURES = {
+    'pq8_error_string': ([_I], C.c_char_p),
+    'pq8_version': ([], _I),
+    'pq8_packed_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
+    'pq8_pack_q8_0': ([_P, _I, _I, _I, _P], _I),
+    'pq8_pack_q8_0_part': ([_P, _I, _I, _I, _I, _I, _P], _I),
+    'pq8_dequant_q8_0': ([_P, _P, _LL, _P], _I),
+    'pq8_gemm': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P], _I),
+    'pq8_gemv_workspace_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
+    'pq8_workspace_init': ([_P, _SZ, _P], _I),
+    'pq8_gemv': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _SZ, _P], _I),
+    'pq8_linear': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P, _SZ, _P], _I),
+    'pq8_lstm_layer': ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P], _I),
+    'pq8_joint_argmax': ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P], _I),
+    'pq8_tdt_commit': ([_P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
+    'pq8_device_status': ([C.POINTER(_I), _P], _I),
+}
+
+
+def header_symbols(path: Path = HEADER):
+    """Every function the C header declares (``pq8_*(``)."""
+    text = re.sub(r'/\*.*?\*/', '', path.read_text(), flags=re.S)
+    return sorted(set(re.findall(r'\b(pq8_\w+)\s*\(', text)))
+
+
+class PQ8Error(RuntimeError):
+    def __init__(self, name: str, code: int, message: str):
+        super().__init__(f'{name}: {message} (pq8 {code})')
+        self.name, self.code = name, code
+
+
+class Library:
+    """Loaded ``libpq8.so`` with typed entry points."""
+
+    def __init__(self, path: Path | str = LIB_PATH):
+        path = Path(path)
+        if not path.is_file():
+            raise FileNotFoundError(f'{path} is missing: build it with `python -m parakeet_cuda_b200.build`')
+        self.path = path
+        self.lib = C.CDLL(str(path))
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(self.lib, name)
+            fn.argtypes, fn.restype = args, res
+
+    def error_string(self, code: int) -> str:
+        return self.lib.pq8_error_string(int(code)).decode()
+
+    def call(self, name: str, *args) -> None:
+        code = getattr(self.lib, name)(*args)
+        if code:
+            raise PQ8Error(name, code, self.error_string(code))
+
+    def packed_size(self, n: int, k: int, layout: int = LAYOUT_ROWS) -> int:
+        out = _SZ()
+        self.call('pq8_packed_size', n, k, layout, C.byref(out))
+        return out.value
+
+    def gemv_workspace_size(self, m: int, n: int, k: int) -> int:
+        out = _SZ()
+        self.call('pq8_gemv_workspace_size', m, n, k, C.byref(out))
+        return out.value
+
+    def device_status(self, stream=None) -> int:
+        out = _I()
+        self.call('pq8_device_status', C.byref(out), stream)
+        return out.value
+
+
+_default = None
+
+
+def library() -> Library:
+    """Process-wide library instance (loaded on first use)."""
+    global _default
+    if _default is None:
+        _default = Library()
+    return _default

@@ -1,0 +1,120 @@
+"""Greedy TDT token loop (host state machine) for one or many streams.
+
+The rules follow the reference's ``decode`` (``parakeet_cuda/decoder.py:78-97``):
+blank id 8192; durations from the model metadata; at most 10 symbols per
+frame; a blank with duration 0 advances one frame; the predictor runs only
+after an emitted token; an emitted token commits the candidate LSTM state.
+
+``greedy_decode`` drives any decoder with the reference protocol
+(``predict``/``joint``/``commit``). ``greedy_decode_batch`` drives a
+``PQ8Decoder`` over B independent streams in lock-step: one fused joint launch
+per step for all streams, one predict for all streams whenever any stream
+needs it (a stream whose inputs did not change gets bit-identical candidates
+again, so this is equivalent to predicting it alone), and a masked commit.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+BLANK = 8192
+MAX_SYMBOLS = 10
+FRAME_SECONDS = 0.08
+
+
+@dataclass
+class Stream:
+    """State of one stream's greedy loop between joint calls."""
+    frames: int
+    t: int = 0
+    symbols: int = 0
+    previous: int = BLANK
+    needs_predict: bool = True
+    tokens: list = field(default_factory=list)
+    token_times: list = field(default_factory=list)
+    trace: list = field(default_factory=list)
+    calls: int = 0
+
+    @property
+    def done(self) -> bool:
+        return self.t >= self.frames
+
+    def advance(self, token: int, dur_index: int, durations) -> bool:
+        """Apply one joint result; returns True when the candidate state must be committed."""
+        self.calls += 1
+        skip = durations[dur_index]
+        if token == BLANK and skip == 0:
+            skip = 1
+        self.trace.append([self.t, token, skip])
+        commit = token != BLANK
+        if commit:
+            self.tokens.append(token)
+            self.token_times.append([self.t * FRAME_SECONDS, (self.t + max(1, skip)) * FRAME_SECONDS])
+            self.previous = token
+            self.needs_predict = True
+        self.symbols += 1
+        self.t += skip
+        if skip:
+            self.symbols = 0
+        elif self.symbols == MAX_SYMBOLS:
+            self.t += 1
+            self.symbols = 0
+        return commit
+
+    def result(self) -> dict:
+        return {'tokens': self.tokens, 'token_times': self.token_times, 'decode_trace': self.trace,
+                'joint_calls': self.calls}
+
+
+def greedy_decode(projected, decoder, durations) -> dict:
+    """One stream through any decoder with the reference's predict/joint/commit protocol."""
+    s = Stream(len(projected))
+    while not s.done:
+        if s.needs_predict:
+            decoder.predict(s.previous)
+            s.needs_predict = False
+        token, dur = decoder.joint(projected[s.t])
+        if s.advance(token, dur, durations):
+            decoder.commit()
+    return s.result()
+
+
+def greedy_decode_batch(projected, decoder, durations, max_steps: int | None = None) -> list:
+    """B streams (``projected[b]`` = frames of stream b, [T_b, 640]) on a batched PQ8Decoder."""
+    b = decoder.batch
+    if len(projected) != b:
+        raise ValueError(f'decoder has {b} rows, got {len(projected)} streams')
+    t_max = max(len(p) for p in projected)
+    table = np.zeros((b * max(t_max, 1), projected[0].shape[1]), np.float32)
+    for i, p in enumerate(projected):
+        table[i * t_max:i * t_max + len(p)] = p
+    dev = decoder.rt.device
+    enc = torch.from_numpy(table).to(dev)
+    streams = [Stream(len(p)) for p in projected]
+    tokens_h = torch.zeros(b, dtype=torch.int32).pin_memory()
+    rows_h = torch.zeros(b, dtype=torch.int32).pin_memory()
+    mask_h = torch.zeros(b, dtype=torch.int32).pin_memory()
+    steps = 0
+    while any(not s.done for s in streams):
+        if max_steps is not None and steps >= max_steps:
+            break
+        if any(s.needs_predict and not s.done for s in streams):
+            tokens_h.copy_(torch.tensor([s.previous for s in streams], dtype=torch.int32))
+            decoder.predict_device(tokens_h)
+            for s in streams:
+                s.needs_predict = False
+        rows_h.copy_(torch.tensor([i * t_max + min(s.t, s.frames - 1) for i, s in enumerate(streams)],
+                                  dtype=torch.int32))
+        decoder.joint_device(enc, rows_h)
+        ids = decoder.read_ids()
+        commit = [0] * b
+        for i, s in enumerate(streams):
+            if not s.done:
+                commit[i] = int(s.advance(int(ids[i, 0]), int(ids[i, 1]), durations))
+        if any(commit):
+            mask_h.copy_(torch.tensor(commit, dtype=torch.int32))
+            decoder.commit_rows(mask_h)
+        steps += 1
+    return [s.result() for s in streams]

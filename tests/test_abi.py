@@ -1,0 +1,103 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, rejects bad arguments before touching a device, and its
+host-side packer produces the documented layout."""
+import ctypes as C
+import subprocess
+
+import numpy as np
+import pytest
+
+from parakeet_cuda_b200 import pq8
+from parakeet_cuda_b200.runtime import pack_concat_host, pack_host
+from parakeet_cuda_b200.synthetic import q8_0_blocks
+
+
+@pytest.fixture(scope='module')
+def lib():
+    return pq8.library()
+
+
+def test_library_exports_every_header_symbol(lib):
+    declared = pq8.header_symbols()
+    assert len(declared) >= 14
+    for name in declared:
+        assert hasattr(lib.lib, name), name
+    out = subprocess.run(['nm', '-D', '--defined-only', str(lib.path)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if ' T ' in line}
+    assert set(declared) <= exported
+    # nothing but the C ABI is exported
+    assert {s for s in exported if s.startswith('pq8_')} == set(declared)
+    assert set(pq8.SIGNATURES) == set(declared)
+
+
+def test_error_strings(lib):
+    assert lib.error_string(0) == 'PQ8_OK'
+    for code in range(1001, 1009):
+        assert lib.error_string(code).startswith('PQ8_ERR_')
+    assert 'unknown' in lib.error_string(4242)
+
+
+def test_argument_validation_without_device(lib):
+    with pytest.raises(pq8.PQ8Error) as e:
+        lib.call('pq8_gemm', None, None, None, None, None, 4, 128, 33, 0, 1.0, 0, None)
+    assert e.value.code == pq8.ERR_UNSUPPORTED_SHAPE
+    with pytest.raises(pq8.PQ8Error) as e:
+        lib.call('pq8_gemm', None, None, None, None, None, 4, 128, 64, 9, 1.0, 0, None)
+    assert e.value.code == pq8.ERR_INVALID_ARGUMENT
+    with pytest.raises(pq8.PQ8Error) as e:
+        lib.call('pq8_gemm', None, None, None, None, None, 4, 128, 64, 0, 1.0, 0, None)
+    assert e.value.code == pq8.ERR_INVALID_ARGUMENT
+    # m == 0 is a no-op that needs no device
+    lib.call('pq8_gemm', None, None, None, None, None, 0, 128, 64, 0, 1.0, 0, None)
+    with pytest.raises(pq8.PQ8Error) as e:
+        lib.call('pq8_packed_size', 10, 48, 0, C.byref(C.c_size_t()))
+    assert e.value.code == pq8.ERR_UNSUPPORTED_SHAPE
+    with pytest.raises(pq8.PQ8Error):
+        lib.packed_size(3, 64, pq8.LAYOUT_GLU)
+
+
+def reference_pack(raw, n, k, layout):
+    """Restatement of the packed layout documented in include/pq8.h / pq8_pack.cpp."""
+    blocks = np.asarray(raw, np.uint8).reshape(n, k // 32, 34)
+    tiles = (n + 127) // 128
+    kb = k // 32
+    data = np.zeros((tiles, kb, 4352), np.uint8)
+    for t in range(tiles):
+        for r in range(128):
+            p = t * 128 + r
+            if layout == pq8.LAYOUT_ROWS:
+                src = p if p < n else -1
+            elif layout == pq8.LAYOUT_GLU:
+                h, w, l = n // 2, r // 32, r % 32
+                j = t * 64 + w * 16 + l % 16
+                src = -1 if j >= h else (j if l < 16 else h + j)
+            else:
+                h, g, u = n // 4, r // 32, t * 32 + r % 32
+                src = g * h + u if u < h else -1
+            if src < 0:
+                continue
+            data[t, :, r * 16:r * 16 + 16] = blocks[src, :, 2:18]
+            data[t, :, 2048 + r * 16:2048 + r * 16 + 16] = blocks[src, :, 18:34]
+            data[t, :, 4096 + 2 * r:4096 + 2 * r + 2] = blocks[src, :, 0:2]
+    return data.reshape(-1)
+
+
+@pytest.mark.parametrize('n,k,layout', [(3, 32, 0), (129, 64, 0), (256, 96, 1), (130, 32, 1), (2560, 64, 2),
+                                        (640, 32, 2)])
+def test_host_packer_layout(lib, n, k, layout):
+    raw = q8_0_blocks(np.random.default_rng(n + k), n, k, qmin=-128)
+    packed = pack_host(raw, n, k, layout)
+    assert packed.size == lib.packed_size(n, k, layout)
+    hdr = packed[:32].view(np.int32)
+    assert packed[:4].tobytes() == b'PQ8P'
+    assert list(hdr[2:8]) == [n, k, layout, (n + 127) // 128, k // 32,
+                              n // 2 if layout == 1 else n // 4 if layout == 2 else n]
+    np.testing.assert_array_equal(packed[256:], reference_pack(raw, n, k, layout))
+
+
+def test_host_packer_k_concat(lib):
+    rng = np.random.default_rng(5)
+    a, b = q8_0_blocks(rng, 256, 64), q8_0_blocks(rng, 256, 96)
+    both = np.concatenate([a.reshape(256, 2, 34), b.reshape(256, 3, 34)], axis=1).reshape(-1, 34)
+    np.testing.assert_array_equal(pack_concat_host([(a, 64), (b, 96)], 256, pq8.LAYOUT_GATES4),
+                                  pack_host(both, 256, 160, pq8.LAYOUT_GATES4))

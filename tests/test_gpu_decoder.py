@@ -1,0 +1,139 @@
+"""GPU parity of the decoder regime: fused LSTM layer, fused joint + arg-max,
+and the greedy TDT loop against the reference's golden token ids."""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import q8, tdt as otdt
+from parakeet_cuda_b200 import pq8
+from parakeet_cuda_b200.decoder import PQ8Decoder
+from parakeet_cuda_b200.runtime import Runtime, pack_concat_host
+from parakeet_cuda_b200.synthetic import SyntheticParakeet, q8_0_blocks
+from parakeet_cuda_b200.tdt import greedy_decode, greedy_decode_batch
+
+pytestmark = pytest.mark.gpu
+
+DURATIONS = [0, 1, 2, 3, 4]
+
+
+@pytest.fixture(scope='module')
+def rt():
+    return Runtime(0)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize('m', [1, 3, 8])
+def test_lstm_layer_matches_oracle(rt, m):
+    rng = np.random.default_rng(20 + m)
+    hid, k_in = 640, 640
+    w_ih, w_hh = q8_0_blocks(rng, 4 * hid, k_in, 2e-4, 1.2e-3), q8_0_blocks(rng, 4 * hid, hid, 2e-4, 1.2e-3)
+    packed = pack_concat_host([(w_ih, k_in), (w_hh, hid)], 4 * hid, pq8.LAYOUT_GATES4)
+    w = rt.upload_packed(packed, 4 * hid, k_in + hid, pq8.LAYOUT_GATES4)
+    x = rng.normal(size=(m, k_in)).astype(np.float32)
+    h = np.tanh(rng.normal(size=(m, hid))).astype(np.float32)
+    c = rng.normal(size=(m, hid)).astype(np.float32)
+    bias = (0.1 * rng.normal(size=4 * hid)).astype(np.float32)
+    h_out, c_out = torch.empty(m, hid, device='cuda'), torch.empty(m, hid, device='cuda')
+    rt.ensure_workspace(m, 4 * hid, k_in + hid)
+    ws = rt.workspace
+    rt.lib.call('pq8_lstm_layer', w.pointer, dev(x).data_ptr(), None, None, dev(h).data_ptr(), dev(c).data_ptr(),
+                dev(bias).data_ptr(), h_out.data_ptr(), c_out.data_ptr(), m, hid, k_in, ws.data_ptr(), ws.numel(),
+                rt.stream())
+    gates = q8.gemm(x, w_ih, 4 * hid, k_in) + q8.gemm(h, w_hh, 4 * hid, hid) + bias
+    for i in range(m):
+        hr, cr = otdt.lstm_cell(gates[i], c[i])
+        np.testing.assert_allclose(h_out[i].cpu().numpy(), hr, atol=2e-5, rtol=1e-4)
+        np.testing.assert_allclose(c_out[i].cpu().numpy(), cr, atol=2e-5, rtol=1e-4)
+
+
+def test_lstm_layer_embedding_input(rt):
+    model = SyntheticParakeet(seed=3, encoder_layers=0)
+    d = PQ8Decoder(model, rt, batch=2)
+    o = otdt.Decoder64(model)
+    for tok in (8192, 17):
+        d.predict_device(torch.tensor([tok, tok], dtype=torch.int32))
+        o.predict(tok)
+        np.testing.assert_allclose(d.pred[0].cpu().numpy(), o.pred, atol=1e-4, rtol=1e-4)
+        np.testing.assert_allclose(d.pred[1].cpu().numpy(), o.pred, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize('m', [1, 5])
+def test_joint_argmax_matches_oracle(rt, m):
+    rng = np.random.default_rng(30 + m)
+    n, k = 8198, 640
+    raw = q8_0_blocks(rng, n, k, 2e-4, 1.2e-3)
+    w = rt.pack(raw, n, k)
+    enc = rng.normal(size=(3 * m, k)).astype(np.float32)
+    rows = np.array([(2 * i + 1) % (3 * m) for i in range(m)], np.int32)
+    pred = rng.normal(size=(m, k)).astype(np.float32)
+    bias = (0.1 * rng.normal(size=n)).astype(np.float32)
+    logits = torch.empty(m, n, device='cuda')
+    ids = torch.empty(m, 2, dtype=torch.int32, device='cuda')
+    rt.ensure_workspace(m, n, k)
+    ws = rt.workspace
+    for _ in range(2):  # second call checks the self-resetting tickets
+        rt.lib.call('pq8_joint_argmax', w.pointer, dev(enc).data_ptr(), dev(rows).data_ptr(), dev(pred).data_ptr(),
+                    dev(bias).data_ptr(), logits.data_ptr(), ids.data_ptr(), m, n, k, 8193, ws.data_ptr(),
+                    ws.numel(), rt.stream())
+        act = np.maximum(enc[rows] + pred, 0)
+        gold = q8.gemm(act, raw, n, k) + bias
+        np.testing.assert_allclose(logits.cpu().numpy(), gold, atol=2e-4, rtol=2e-4)
+        got = ids.cpu().numpy()
+        for i in range(m):
+            assert tuple(got[i]) == otdt.argmax_tdt(gold[i]), (i, otdt.top2_margin(gold[i]))
+
+
+def test_joint_argmax_ties_lowest_index(rt):
+    """runtime.cu:167-179 / tests/test_cuda.py:78-82: ties resolve to the lowest index."""
+    n, k = 8198, 32
+    raw = np.zeros((n * k // 32, 34), np.uint8)  # all-zero weights: logits == bias
+    w = rt.pack(raw, n, k)
+    bias = np.zeros(n, np.float32)
+    bias[19] = bias[37] = 2
+    bias[8195] = bias[8197] = 3
+    ids = torch.empty(1, 2, dtype=torch.int32, device='cuda')
+    logits = torch.empty(1, n, device='cuda')
+    z = dev(np.zeros((1, k), np.float32))
+    rt.ensure_workspace(1, n, k)
+    rt.lib.call('pq8_joint_argmax', w.pointer, z.data_ptr(), None, z.data_ptr(), dev(bias).data_ptr(),
+                logits.data_ptr(), ids.data_ptr(), 1, n, k, 8193, rt.workspace.data_ptr(), rt.workspace.numel(),
+                rt.stream())
+    assert ids.cpu().numpy().tolist() == [[19, 2]]
+
+
+def test_tdt_decode_matches_reference_golden(rt, golden_dir):
+    meta = json.loads((golden_dir / 'golden_meta.json').read_text())
+    data = np.load(golden_dir / 'tdt_decode.npz')
+    for case in meta['tdt_random']:
+        seed = case['seed']
+        model = SyntheticParakeet(seed=seed, encoder_layers=0, blank_bias=case['blank_bias'],
+                                  duration0_bias=case['duration0_bias'])
+        d = PQ8Decoder(model, rt, batch=1)
+        r = greedy_decode(data[f'seed{seed}_projected'], d, DURATIONS)
+        np.testing.assert_array_equal(np.asarray(r['tokens'], np.int32), data[f'seed{seed}_tokens'])
+        np.testing.assert_array_equal(np.asarray(r['decode_trace'], np.int32).reshape(-1, 3),
+                                      data[f'seed{seed}_trace'])
+        assert r['joint_calls'] == case['joint_calls']
+
+
+@pytest.mark.parametrize('batch', [1, 4, 8])
+def test_tdt_batched_decode_matches_oracle(rt, batch):
+    model = SyntheticParakeet(seed=12, encoder_layers=0, blank_bias=3.0)
+    rng = np.random.default_rng(40 + batch)
+    projected = [rng.normal(size=(int(rng.integers(20, 40)), 640)).astype(np.float32) for _ in range(batch)]
+    d = PQ8Decoder(model, rt, batch=batch)
+    got = greedy_decode_batch(projected, d, DURATIONS)
+    for p, g in zip(projected, got):
+        ref = otdt.greedy_decode(p, otdt.Decoder64(model), DURATIONS)
+        assert g['tokens'] == ref['tokens']
+        assert g['decode_trace'] == ref['decode_trace']
+
+
+def test_status_clean(rt):
+    torch.cuda.synchronize()
+    assert rt.device_status() == 0

@@ -1,0 +1,226 @@
+"""GPU parity of the Q8_0 contraction kernels against the CPU oracle.
+
+Tolerances:
+* GEMM (tensor cores, TF32 operands rounded to nearest)
+  ``max|y - golden| <= 2e-3 * rms(golden)`` against the float64 golden, and
+  ``<= 2e-5 * rms`` against ``oracle.q8.gemm_tf32`` (the same TF32-rounded
+  operands summed in float64), which pins the operand rounding exactly.
+* GEMV (FP32 FMA): ``atol = rtol = 2e-4`` as ``tests/test_cuda.py:34-50`` of
+  the reference.
+* Q8_0 expansion: bit-exact.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import q8
+from parakeet_cuda_b200 import pq8
+from parakeet_cuda_b200.pq8 import EPI_GLU, EPI_NONE, EPI_RELU, EPI_RESIDUAL, EPI_SILU, LAYOUT_GLU, LAYOUT_ROWS
+from parakeet_cuda_b200.runtime import Runtime
+from parakeet_cuda_b200.synthetic import q8_0_blocks
+
+pytestmark = pytest.mark.gpu
+
+NORTH_STAR = 2e-3
+TF32_EXACT = 2e-5
+
+
+@pytest.fixture(scope='module')
+def rt():
+    return Runtime(0)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def contract_cases():
+    """workloads/q8_gemm.py:cases() inputs (seed 903), regenerated in draw order."""
+    rng = np.random.default_rng(903)
+    for m, k, n in ((1, 32, 3), (17, 640, 65), (33, 1024, 129), (441, 1024, 4096)):
+        raw = q8_0_blocks(rng, n, k, scale_lo=1e-4, scale_hi=2e-2)
+        x = rng.normal(size=(m, k)).astype(np.float32)
+        yield m, k, n, raw, x
+
+
+# Lipschitz factor of each epilogue with respect to the GEMM output z: the
+# north-star bar applies to z, so an epilogue may scale the error by this much.
+LIPSCHITZ = {EPI_NONE: 1.0, EPI_RELU: 1.0, EPI_SILU: 1.1, EPI_RESIDUAL: 1.0, EPI_GLU: None}
+
+
+def check_gemm(y, x, raw, n, k, epi=EPI_NONE, bias=None, resid=None, alpha=1.0):
+    """North-star bar on the GEMM output (scaled through the epilogue) and an
+    exact-numerics bar against the TF32-rounded-operand model."""
+    y = y.cpu().numpy().astype(np.float64)
+    z_gold, z_tf = q8.gemm(x, raw, n, k), q8.gemm_tf32(x, raw, n, k)
+    if bias is not None:
+        z_gold, z_tf = z_gold + bias, z_tf + bias
+    gold = q8.epilogue(z_gold, epi, None, resid, alpha)
+    tf = q8.epilogue(z_tf, epi, None, resid, alpha)
+    assert np.isfinite(y).all()
+    e_gold = float(np.max(np.abs(y - gold))) / q8.rms(z_gold)
+    e_tf = float(np.max(np.abs(y - tf))) / q8.rms(z_tf)
+    assert e_tf <= TF32_EXACT, (e_gold, e_tf)
+    if LIPSCHITZ[epi] is not None:
+        assert e_gold <= NORTH_STAR * LIPSCHITZ[epi] * (alpha if epi == EPI_RESIDUAL else 1.0), (e_gold, e_tf)
+    return e_gold, e_tf
+
+
+def test_dequant_bit_exact(rt, golden_dir):
+    data = np.load(golden_dir / 'q8_decode_gemv.npz')
+    for n, k in ((3, 32), (7, 640), (5, 1024)):
+        raw = dev(data[f'n{n}_k{k}_raw'].reshape(-1))
+        out = torch.empty(n * k, dtype=torch.float32, device='cuda')
+        rt.lib.call('pq8_dequant_q8_0', raw.data_ptr(), out.data_ptr(), n * k, rt.stream())
+        np.testing.assert_array_equal(out.cpu().numpy(), data[f'n{n}_k{k}_decoded'])
+
+
+def test_gemv_reference_cases(rt, golden_dir):
+    data = np.load(golden_dir / 'q8_decode_gemv.npz')
+    for n, k in ((3, 32), (7, 640), (5, 1024)):
+        w = rt.pack(data[f'n{n}_k{k}_raw'], n, k)
+        x = dev(data[f'n{n}_k{k}_x'][None, :])
+        y = rt.linear(x, w)
+        np.testing.assert_allclose(y.cpu().numpy()[0], data[f'n{n}_k{k}_gemv'], atol=2e-4, rtol=2e-4)
+
+
+@pytest.mark.parametrize('bn', ['64', '128', '256'])
+def test_gemm_reference_contract(rt, golden_dir, bn, monkeypatch):
+    monkeypatch.setenv('PQ8_GEMM_BN', bn)
+    data = np.load(golden_dir / 'q8_gemm_contract.npz')
+    for m, k, n, raw, x in contract_cases():
+        w = rt.pack(raw, n, k)
+        y = rt.gemm(dev(x), w)
+        check_gemm(y, x, raw, n, k)
+        tag = f'm{m}_k{k}_n{n}'
+        gold = data[tag + '_golden'] if tag + '_golden' in data else None
+        if gold is not None:
+            assert q8.max_err_over_rms(y.cpu().numpy(), gold) <= NORTH_STAR
+        else:
+            idx, val = data[tag + '_sample_idx'], data[tag + '_sample_val']
+            got = y.cpu().numpy().reshape(-1)[idx]
+            assert np.max(np.abs(got - val)) <= NORTH_STAR * q8.rms(val)
+
+
+def test_gemm_config0(rt):
+    """X [128, 1024] ~ N(0, 1), W [4096, 1024] Q8_0, scales U[1e-3, 2e-2]."""
+    rng = np.random.default_rng(0)
+    raw = q8_0_blocks(rng, 4096, 1024)
+    x = rng.normal(size=(128, 1024)).astype(np.float32)
+    y = rt.gemm(dev(x), rt.pack(raw, 4096, 1024))
+    e_gold, _ = check_gemm(y, x, raw, 4096, 1024)
+    assert e_gold < 1.8e-3
+
+
+@pytest.mark.parametrize('bn', ['64', '128', '256'])
+@pytest.mark.parametrize('m,n,k', [(1, 3, 32), (31, 200, 64), (65, 128, 96), (200, 385, 160), (257, 64, 32),
+                                   (300, 1000, 640)])
+def test_gemm_tails(rt, bn, m, n, k, monkeypatch):
+    monkeypatch.setenv('PQ8_GEMM_BN', bn)
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    raw = q8_0_blocks(rng, n, k, qmin=-128)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    check_gemm(rt.gemm(dev(x), rt.pack(raw, n, k)), x, raw, n, k)
+
+
+@pytest.mark.parametrize('bn', ['64', '256'])
+@pytest.mark.parametrize('epi', [EPI_NONE, EPI_RELU, EPI_SILU, EPI_RESIDUAL, EPI_GLU])
+def test_gemm_epilogues(rt, epi, bn, monkeypatch):
+    monkeypatch.setenv('PQ8_GEMM_BN', bn)
+    rng = np.random.default_rng(epi + 10)
+    m, n, k = 150, 384, 256
+    raw = q8_0_blocks(rng, n, k)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    out_n = n // 2 if epi == EPI_GLU else n
+    resid = rng.normal(size=(m, out_n)).astype(np.float32)
+    w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
+    y = dev(resid) if epi == EPI_RESIDUAL else None
+    y = rt.gemm(dev(x), w, out=y, bias=dev(bias), resid=y, epilogue=epi, alpha=0.5)
+    check_gemm(y, x, raw, n, k, epi, bias, resid, 0.5)
+
+
+def test_gemm_tf32_flags(rt):
+    rng = np.random.default_rng(3)
+    m, n, k = 256, 512, 512
+    raw1, raw2 = q8_0_blocks(rng, n, k), q8_0_blocks(rng, k, n)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    w1, w2 = rt.pack(raw1, n, k), rt.pack(raw2, k, n)
+    h = rt.gemm(dev(x), w1, epilogue=EPI_SILU, flags=pq8.FLAG_OUT_TF32)
+    hn = h.cpu().numpy()
+    assert np.all((hn.view(np.uint32) & 0x1FFF) == 0)
+    y_pre = rt.gemm(h, w2, flags=pq8.FLAG_X_TF32).cpu().numpy()
+    y_in = rt.gemm(h, w2).cpu().numpy()
+    np.testing.assert_array_equal(y_pre, y_in)  # rounding an already-rounded X is the identity
+
+
+def test_linear_dispatch_gemv_matches_gemm(rt):
+    rng = np.random.default_rng(4)
+    n, k = 2560, 640
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k)
+    for m in (1, 2, 3, 5, 8):
+        x = rng.normal(size=(m, k)).astype(np.float32)
+        bias = rng.normal(size=n).astype(np.float32)
+        y = rt.linear(dev(x), w, bias=dev(bias)).cpu().numpy()
+        gold = q8.epilogue(q8.gemm(x, raw, n, k), EPI_NONE, bias)
+        np.testing.assert_allclose(y, gold, atol=2e-4, rtol=2e-4)
+
+
+def test_gemv_epilogues(rt):
+    rng = np.random.default_rng(6)
+    m, n, k = 4, 1280, 640
+    raw = q8_0_blocks(rng, n, k)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    for epi in (EPI_RELU, EPI_SILU, EPI_GLU, EPI_RESIDUAL):
+        out_n = n // 2 if epi == EPI_GLU else n
+        resid = rng.normal(size=(m, out_n)).astype(np.float32)
+        w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
+        y = dev(resid) if epi == EPI_RESIDUAL else None
+        y = rt.linear(dev(x), w, out=y, bias=dev(bias), resid=y, epilogue=epi, alpha=0.5).cpu().numpy()
+        gold = q8.epilogue(q8.gemm(x, raw, n, k), epi, bias, resid, 0.5)
+        np.testing.assert_allclose(y, gold, atol=2e-4 * max(1.0, q8.rms(gold)), rtol=2e-4)
+
+
+def test_gemv_deterministic(rt):
+    rng = np.random.default_rng(8)
+    n, k = 8198, 640
+    w = rt.pack(q8_0_blocks(rng, n, k), n, k)
+    x = dev(rng.normal(size=(1, k)).astype(np.float32))
+    ys = [rt.linear(x, w).cpu().numpy() for _ in range(5)]
+    for y in ys[1:]:
+        np.testing.assert_array_equal(y, ys[0])
+
+
+def test_layout_mismatch_reports_status(rt):
+    rng = np.random.default_rng(9)
+    raw = q8_0_blocks(rng, 256, 64)
+    glu = rt.pack(raw, 256, 64, LAYOUT_GLU)
+    x = dev(rng.normal(size=(40, 64)).astype(np.float32))
+    assert rt.device_status() == 0
+    rt.gemm(x, glu)  # GLU-packed weights used without the GLU epilogue
+    assert rt.device_status() == pq8.ERR_LAYOUT
+    rt.linear(x[:2], glu)
+    assert rt.device_status() == pq8.ERR_LAYOUT
+    assert rt.device_status() == 0
+
+
+def test_large_shape_rows_sampled(rt):
+    """Full-size FFN down projection (M=3000, K=4096, N=1024), sampled rows vs float64."""
+    rng = np.random.default_rng(12)
+    m, n, k = 3000, 1024, 4096
+    raw = q8_0_blocks(rng, n, k)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    y = rt.gemm(dev(x), rt.pack(raw, n, k)).cpu().numpy()
+    rows = rng.choice(m, 96, replace=False)
+    gold = q8.gemm(x[rows], raw, n, k)
+    assert q8.max_err_over_rms(y[rows], gold) <= NORTH_STAR
+    assert q8.max_err_over_rms(y[rows], q8.gemm_tf32(x[rows], raw, n, k)) <= TF32_EXACT
+
+
+def test_status_clean_at_end(rt):
+    torch.cuda.synchronize()
+    assert rt.device_status() == 0
