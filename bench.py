@@ -1,0 +1,370 @@
+"""Benchmark: Q8_0 encoder GEMM stack on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl pq8|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N ...
+
+One step = every Q8_0 linear of the 24 FastConformer layers (9 fused GEMM
+launches per layer) over this GPU's windows: 8 windows x 375 frames = 3000
+activation rows per GPU, weights replicated, no collective on the data path
+(weak scaling: 8/16/32/64 windows on 1/2/4/8 GPUs). Rank 0 prints one JSON
+line. The metric is encoder frames per second for the whole job.
+
+Extra keys on the line: ``roofline`` (the GEMM kernel against the TF32 tensor
+peak derived from MEASURED_PEAKS.json), ``gemv`` (the M = 1 decoder-regime
+kernel streaming all 642 MB of encoder weights, against HBM bandwidth),
+``cpu_baseline`` (the reference's NumPy path on this host), ``e2e`` (the same
+metric through the public host API with H2D/D2H copies in the timed region),
+``clocks`` (nvidia-smi samples during the timed region) and ``gpu_launches``.
+
+``--impl reference`` times the reference's CPU implementation (NumPy: Q8_0
+decode + FP32 matmul) on the host cores instead; under torchrun only rank 0
+runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from pathlib import Path
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WINDOW_FRAMES = 375
+METRIC = 'encoder_frames_per_s'
+UNIT = 'frames/s'
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', choices=('pq8', 'reference'), default='pq8')
+    ap.add_argument('--windows-per-gpu', type=int, default=8)
+    ap.add_argument('--layers', type=int, default=24)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
+    return ap.parse_args()
+
+
+def config(args, n_gpus):
+    return {
+        'workload': (f'config 2: {args.layers}-layer FastConformer Q8_0 linear stack (FFN x2, QKV, pos, out, '
+                     f'pointwise GLU, pointwise) over {args.windows_per_gpu} windows x {WINDOW_FRAMES} frames '
+                     f'per GPU'),
+        'rows_per_gpu': args.windows_per_gpu * WINDOW_FRAMES,
+        'windows_total': args.windows_per_gpu * n_gpus,
+        'layers': args.layers,
+        'parallelism': f'windows sharded over {n_gpus} GPU(s), weights replicated, no data-path collective',
+        'l2': 'weights streamed per step (642 MB packed Q8_0 > 126 MB L2); no flush needed',
+        'weights': 'random Q8_0, int8 U[-127,127], fp16 scales U[1e-3,2e-2]; activations N(0,1)',
+    }
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    def __init__(self, gpus: int):
+        self.proc = None
+        self.path = Path(os.environ.get('TMPDIR', '/tmp')) / f'pq8_clocks_{os.getpid()}.csv'
+        q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+        try:
+            self.f = open(self.path, 'w')
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={q}', '--format=csv,noheader,nounits',
+                                          '-i', ','.join(str(i) for i in range(gpus)), '-lms', '100'],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def measured_peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return d, 'measured'
+    return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'bf16_tflops_sustained': 1400.0}, 'fallback'
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the GEMM kernel from the committed ncu summary, if any."""
+    p = ROOT / 'profiles' / 'gemm_traffic.json'
+    if p.is_file():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_sample(model, rows=WINDOW_FRAMES, repeats=3):
+    from oracle.cpu_path import blas_threads, time_layer_window
+    times = [time_layer_window(model, rows, layer=0, seed=i) for i in range(repeats)]
+    t = min(times)
+    return {'value': rows / (t * 24), 'unit': UNIT, 'cores': blas_threads(), 'kind': 'port',
+            'sample': (f'NumPy restatement of the reference CPU path (gguf.array Q8_0 decode + FP32 x @ W.T, '
+                       f'reference.py:37): one layer x one {rows}-frame window, best of {repeats} '
+                       f'({t:.3f} s), scaled to 24 layers')}
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', 0))
+    if rank != 0:
+        return
+    from parakeet_cuda_b200.synthetic import SyntheticParakeet
+    model = SyntheticParakeet(seed=0, encoder_layers=1, decoder=False)
+    from oracle.cpu_path import blas_threads, time_layer_window
+    for i in range(args.warmup):
+        time_layer_window(model, WINDOW_FRAMES, 0, seed=i)
+    times = [time_layer_window(model, WINDOW_FRAMES, 0, seed=100 + i) for i in range(args.steps)]
+    t = sum(times) / len(times)
+    value = WINDOW_FRAMES / (t * 24)
+    n = args.gpus
+    line = {'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': n,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': t * 1000, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+            'config': config(args, n),
+            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': blas_threads(), 'kind': 'port',
+                             'sample': (f'each step: one encoder layer (Q8_0 decode + 9 FP32 linears) over one '
+                                        f'{WINDOW_FRAMES}-frame window; frames/s = {WINDOW_FRAMES} / '
+                                        f'(24 x step time)')},
+            'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm
+class LaunchTimer:
+    """CUDA events around each launch on the launching stream, grouped by name."""
+
+    def __init__(self, torch):
+        self.torch = torch
+        self.pairs = []
+        self.open = None
+
+    def start(self, name):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.open = (name, e)
+
+    def stop(self, name):
+        e = self.torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.pairs.append((self.open[0], self.open[1], e))
+
+    def totals(self):
+        out = {}
+        for name, a, b in self.pairs:
+            ms = a.elapsed_time(b)
+            c, t = out.get(name, (0, 0.0))
+            out[name] = (c + 1, t + ms)
+        return out
+
+
+def run_gpu(args):
+    import torch
+    from parakeet_cuda_b200.encoder import LAYER_PLAN, EncoderStack
+    from parakeet_cuda_b200.runtime import Runtime
+    from parakeet_cuda_b200.scheduler import WindowScheduler
+    from parakeet_cuda_b200.synthetic import SyntheticParakeet
+
+    sched = WindowScheduler(timeout_s=300)
+    n = sched.world
+    if n != args.gpus:
+        print(f'warning: --gpus {args.gpus} but WORLD_SIZE {n}; using {n}', file=sys.stderr)
+    dev = sched.local_rank if n > 1 else 0
+    torch.cuda.set_device(dev)
+    rows = args.windows_per_gpu * WINDOW_FRAMES
+    model = SyntheticParakeet(seed=0, encoder_layers=args.layers, decoder=False)
+    rt = Runtime(dev)
+    stack = EncoderStack(model, rt, rows, layers=args.layers, seed=1 + sched.rank)
+    del model
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        stack.step()
+    torch.cuda.synchronize()
+    sched.barrier()
+
+    clocks = ClockSampler(n) if sched.rank == 0 else None
+    timer = LaunchTimer(torch)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    sched.barrier()
+    start.record()
+    for _ in range(args.steps):
+        stack.step(timer)
+    end.record()
+    torch.cuda.synchronize()
+    sched.barrier()
+    clock_info = clocks.stop() if clocks else None
+    ms = start.elapsed_time(end) / args.steps
+    ms_max = sched.max_over_ranks(ms)
+    per_name = timer.totals()
+    kernel_ms_step = sum(t for _, t in per_name.values()) / args.steps
+    status = rt.device_status()
+
+    # e2e: public host API, pinned H2D of the step input and D2H of its result in the timed region
+    x_host = torch.randn(rows, 1024).pin_memory()
+    out_host = torch.empty(rows, 1024).pin_memory()
+    for _ in range(2):
+        stack.run_host(x_host, out_host)
+    torch.cuda.synchronize()
+    sched.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        stack.run_host(x_host, out_host)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = sched.max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    extras = {}
+    if not args.no_extras:
+        extras['gemv'] = gemv_measure(torch, rt, stack)
+        extras['tf32_cublas_tflops'] = cublas_tf32(torch)
+    sched.barrier()
+
+    if sched.rank == 0:
+        peaks, peak_src = measured_peaks()
+        flops_step = stack.flops_per_step()
+        achieved = flops_step / (kernel_ms_step / 1e3) / 1e12
+        peak = peaks['bf16_tflops_sustained'] / 2
+        shapes = {}
+        for entry in LAYER_PLAN:
+            name, _, nn, kk = entry[:4]
+            cnt, tot = per_name.get(name, (0, 0.0))
+            if cnt:
+                shapes[name] = {'n': nn, 'k': kk, 'ms': tot / cnt,
+                                'tflops': 2 * rows * nn * kk / (tot / cnt / 1e3) / 1e12}
+        traffic = ncu_traffic()
+        frames = rows * n
+        line = {
+            'metric': METRIC, 'value': frames / (ms_max / 1e3), 'unit': UNIT, 'n_gpus': n, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': ms_max, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'tf32', 'data': 'synthetic (random Q8_0 weights, N(0,1) activations)',
+            'config': config(args, n),
+            'roofline': {
+                'bound': 'tensor', 'achieved': achieved,
+                'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved / peak,
+                'traffic': traffic.get('bytes_per_launch') if traffic else None,
+                'peak_source': (f'{peak_src}: MEASURED_PEAKS.json bf16_tflops_sustained / 2 (dense TF32 is half '
+                                f'the BF16 rate); kernel timed inside a long step'),
+                'frac_of_burst': achieved / (peaks['bf16_tflops'] / 2),
+                'kernel': 'pq8::gemm_tc_kernel (all 9 encoder linears)',
+                'flops_per_step': flops_step, 'kernel_ms_per_step': kernel_ms_step,
+                'per_shape': shapes,
+                'traffic_source': traffic.get('source') if traffic else None,
+            },
+            'e2e': {'value': frames / (e2e_ms / 1e3), 'unit': UNIT, 'h2d_bytes_per_step': rows * 1024 * 4,
+                    'd2h_bytes_per_step': rows * 1024 * 4,
+                    'api': 'parakeet_cuda_b200.encoder.EncoderStack.run_host (pinned host in/out)'},
+            'gpu_launches': stack.launches_per_step * args.steps,
+            'device_status': status,
+        }
+        if clock_info:
+            line['clocks'] = clock_info
+        line.update(extras)
+        if n == 1 and not args.no_cpu_baseline:
+            from parakeet_cuda_b200.synthetic import SyntheticParakeet as SP
+            line['cpu_baseline'] = cpu_sample(SP(seed=0, encoder_layers=1, decoder=False))
+        print(json.dumps(line), flush=True)
+    sched.close()
+
+
+def gemv_measure(torch, rt, stack):
+    """M = 1 GEMV over every packed encoder weight (216 launches, 642 MB > L2): HBM GB/s."""
+    from parakeet_cuda_b200.encoder import LAYER_PLAN
+    x = {k: torch.randn(1, k, device=rt.device) for k in (1024, 4096)}
+    y = torch.empty(1, 4096, device=rt.device)
+    ws = None
+    for layer in stack.weights:
+        for w in layer.values():
+            rt.ensure_workspace(1, w.n, w.k)
+    ws = rt.workspace
+
+    def run():
+        for layer in stack.weights:
+            for name, w in layer.items():
+                rt.lib.call('pq8_gemv', w.pointer, x[w.k].data_ptr(), y.data_ptr(), None, None, 1, w.n, w.k,
+                            3 if name == 'pw1_glu' else 0, 1.0, ws.data_ptr(), ws.numel(), rt.stream())
+    run()
+    torch.cuda.synchronize()
+    reps = 5
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        run()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    nbytes = stack.weight_bytes
+    peaks, src = measured_peaks()
+    gbs = nbytes / (ms / 1e3) / 1e9
+    return {'m': 1, 'bytes_per_pass': nbytes, 'ms_per_pass': ms, 'launches_per_pass': stack.launches_per_step,
+            'achieved_gbs': gbs, 'peak_gbs': peaks['hbm_gbs'], 'frac': gbs / peaks['hbm_gbs'],
+            'peak_source': f'{src}: MEASURED_PEAKS.json hbm_gbs'}
+
+
+def cublas_tf32(torch):
+    """Context only: cuBLAS FP32 GEMM with TF32 tensor cores, 8192^3, best of 5."""
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(8192, 8192, device='cuda')
+    b = torch.randn(8192, 8192, device='cuda')
+    best = None
+    for _ in range(6):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch.matmul(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1)
+        best = t if best is None else min(best, t)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    return 2 * 8192 ** 3 / (best / 1e3) / 1e12
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == '__main__':
+    main()

@@ -121,8 +121,8 @@ class PQ8Decoder:
         self.predict_device(torch.full((self.batch,), int(token), dtype=torch.int32))
 
     def joint(self, frame):
-        self.enc.copy_(torch.as_tensor(np.broadcast_to(np.asarray(frame, np.float32), (self.batch, HIDDEN))),
-                       non_blocking=False)
+        row = torch.from_numpy(np.array(frame, np.float32).reshape(1, HIDDEN))
+        self.enc.copy_(row.expand(self.batch, HIDDEN))
         self.joint_device(self.enc)
         ids = self.read_ids()
         return int(ids[0, 0]), int(ids[0, 1])

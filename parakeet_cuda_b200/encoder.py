@@ -1,0 +1,133 @@
+"""FastConformer encoder GEMM stack on resident packed Q8_0 weights (encoder regime).
+
+Each encoder layer of the reference issues these Q8_0 linears
+(``parakeet_cuda/encoder.py``; all ``use_bias=False``, ``gguf.py:91``):
+
+====================  ==============  =========================================
+linear                shape (N x K)   reference epilogue (call site)
+====================  ==============  =========================================
+FFN1 linear1          4096 x 1024     + SiLU            (``encoder.py:31-33``)
+FFN1 linear2          1024 x 4096     x += 0.5 * y      (``encoder.py:34-35``)
+Q/K/V (packed)        3072 x 1024     -                 (``encoder.py:75-84``)
+linear_pos            1024 x 1024     -                 (``encoder.py:103``)
+linear_out            1024 x 1024     x += y            (``encoder.py:111-112``)
+pointwise_conv1       2048 x 1024     GLU -> 1024       (``encoder.py:117-119``)
+pointwise_conv2       1024 x 1024     x += y            (``encoder.py:125-126``)
+FFN2 linear1/linear2  as FFN1         as FFN1           (``encoder.py:132``)
+====================  ==============  =========================================
+
+Here every epilogue is fused into the GEMM launch (the reference runs one
+SGEMM plus one elementwise kernel per linear, after a ``dequant_q8`` of the
+layer). LayerNorm, attention, the depthwise convolution and the stem are not
+part of the contraction path: their outputs are represented by fixed input
+buffers (``norm`` for every LayerNorm output, ``ctx`` for the attention
+context, ``pos`` for the positional embeddings), so the stack performs
+exactly the linears of the encoder on realistic shapes. Intermediate
+activations that feed another GEMM (FFN hidden, GLU output) are written
+TF32-rounded and consumed without re-rounding (``PQ8_FLAG_OUT_TF32`` /
+``PQ8_FLAG_X_TF32``), which is value-identical to rounding them in the
+consumer.
+
+Config 1 of the benchmark is one layer at T = 375 frames; config 2 is 24
+layers over ``windows x 375`` rows, with windows independent (``recording.py``
+segments) so that rows from several windows share one launch.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .pq8 import EPI_GLU, EPI_NONE, EPI_RESIDUAL, EPI_SILU, FLAG_OUT_TF32, FLAG_X_TF32, LAYOUT_GLU
+from .runtime import PackedWeight, Runtime, pack_host
+
+D_MODEL, D_FF, D_CONV = 1024, 4096, 2048
+FRAMES_PER_WINDOW = 375   # 30 s at 80 ms per encoder frame
+
+
+def flops_per_row_per_layer(pos_rows_per_row: float = 1.0) -> int:
+    """Algorithmic FLOPs (2 N K per linear) per activation row per layer."""
+    nk = (2 * D_FF * D_MODEL * 2 + 3 * D_MODEL * D_MODEL + D_MODEL * D_MODEL + D_CONV * D_MODEL
+          + D_MODEL * D_MODEL)
+    return int(2 * (nk + pos_rows_per_row * D_MODEL * D_MODEL))
+
+
+# (name, weight key(s), N, K, epilogue, alpha, input buffer, output buffer, flags)
+LAYER_PLAN = (
+    ('ffn1_up', ('feed_forward1.linear1',), D_FF, D_MODEL, EPI_SILU, 1.0, 'norm', 'hidden', FLAG_OUT_TF32),
+    ('ffn1_down', ('feed_forward1.linear2',), D_MODEL, D_FF, EPI_RESIDUAL, 0.5, 'hidden', 'resid', FLAG_X_TF32),
+    ('qkv', ('self_attn.linear_q', 'self_attn.linear_k', 'self_attn.linear_v'), 3 * D_MODEL, D_MODEL, EPI_NONE,
+     1.0, 'norm', 'qkv', 0),
+    ('pos', ('self_attn.linear_pos',), D_MODEL, D_MODEL, EPI_NONE, 1.0, 'pos', 'pos_out', 0),
+    ('out', ('self_attn.linear_out',), D_MODEL, D_MODEL, EPI_RESIDUAL, 1.0, 'ctx', 'resid', 0),
+    ('pw1_glu', ('conv.pointwise_conv1',), D_CONV, D_MODEL, EPI_GLU, 1.0, 'norm', 'gate', FLAG_OUT_TF32),
+    ('pw2', ('conv.pointwise_conv2',), D_MODEL, D_MODEL, EPI_RESIDUAL, 1.0, 'gate', 'resid', FLAG_X_TF32),
+    ('ffn2_up', ('feed_forward2.linear1',), D_FF, D_MODEL, EPI_SILU, 1.0, 'norm', 'hidden', FLAG_OUT_TF32),
+    ('ffn2_down', ('feed_forward2.linear2',), D_MODEL, D_FF, EPI_RESIDUAL, 0.5, 'hidden', 'resid', FLAG_X_TF32),
+)
+
+
+class EncoderStack:
+    """All Q8_0 linears of ``layers`` encoder layers over ``rows`` activation rows on one device."""
+
+    def __init__(self, model, runtime: Runtime, rows: int, layers: int = 24, seed: int = 0):
+        self.rt, self.rows, self.layers = runtime, rows, layers
+        dev = runtime.device
+        self.weights: list[dict[str, PackedWeight]] = []
+        for l in range(layers):
+            base = f'encoder.layers.{l}.'
+            packed = {}
+            for name, keys, n, k, epi, _, _, _, _ in LAYER_PLAN:
+                raw = np.concatenate([np.asarray(model.raw(base + key + '.weight'), np.uint8).reshape(-1)
+                                      for key in keys])
+                layout = LAYOUT_GLU if epi == EPI_GLU else 0
+                packed[name] = runtime.upload_packed(pack_host(raw, n, k, layout, runtime.lib), n, k, layout)
+            self.weights.append(packed)
+        self.weight_bytes = sum(w.data.numel() for layer in self.weights for w in layer.values())
+        g = torch.Generator(device='cpu').manual_seed(seed)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.buffers = {
+            'norm': torch.randn(rows, D_MODEL, generator=g).to(dev),
+            'ctx': torch.randn(rows, D_MODEL, generator=g).to(dev),
+            'pos': torch.randn(rows, D_MODEL, generator=g).to(dev),
+            'resid': torch.zeros(rows, D_MODEL, **f32),
+            'hidden': torch.empty(rows, D_FF, **f32),
+            'qkv': torch.empty(rows, 3 * D_MODEL, **f32),
+            'pos_out': torch.empty(rows, D_MODEL, **f32),
+            'gate': torch.empty(rows, D_MODEL, **f32),
+        }
+
+    @property
+    def launches_per_step(self) -> int:
+        return self.layers * len(LAYER_PLAN)
+
+    def flops_per_step(self) -> int:
+        return self.rows * self.layers * flops_per_row_per_layer()
+
+    def launch(self, layer: int, entry) -> None:
+        name, _, n, k, epi, alpha, src, dst, flags = entry
+        w = self.weights[layer][name]
+        b = self.buffers
+        resid = b['resid'] if epi == EPI_RESIDUAL else None
+        self.rt.gemm(b[src], w, out=b[dst], resid=resid, epilogue=epi, alpha=alpha, flags=flags)
+
+    def step(self, timer=None) -> None:
+        """Enqueue every linear of every layer on the current stream."""
+        for l in range(self.layers):
+            for entry in LAYER_PLAN:
+                if timer is not None:
+                    timer.start(entry[0])
+                self.launch(l, entry)
+                if timer is not None:
+                    timer.stop(entry[0])
+
+    def run_host(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
+        """Public end-to-end call on host buffers (pinned for asynchronous copies):
+        ``x_host`` [rows, 1024] is the windows' encoder input, which starts the
+        residual stream and stands in for every LayerNorm output; the final
+        residual stream is copied back into ``out_host``. All work is on the
+        current stream; the caller synchronizes."""
+        self.buffers['norm'].copy_(x_host, non_blocking=True)
+        self.buffers['resid'].copy_(self.buffers['norm'], non_blocking=True)
+        self.step()
+        out_host.copy_(self.buffers['resid'], non_blocking=True)
+        return out_host

@@ -41,8 +41,9 @@ def test_lstm_layer_matches_oracle(rt, m):
     h_out, c_out = torch.empty(m, hid, device='cuda'), torch.empty(m, hid, device='cuda')
     rt.ensure_workspace(m, 4 * hid, k_in + hid)
     ws = rt.workspace
-    rt.lib.call('pq8_lstm_layer', w.pointer, dev(x).data_ptr(), None, None, dev(h).data_ptr(), dev(c).data_ptr(),
-                dev(bias).data_ptr(), h_out.data_ptr(), c_out.data_ptr(), m, hid, k_in, ws.data_ptr(), ws.numel(),
+    xd, hd, cd, bd = dev(x), dev(h), dev(c), dev(bias)  # keep the device copies alive across the launch
+    rt.lib.call('pq8_lstm_layer', w.pointer, xd.data_ptr(), None, None, hd.data_ptr(), cd.data_ptr(),
+                bd.data_ptr(), h_out.data_ptr(), c_out.data_ptr(), m, hid, k_in, ws.data_ptr(), ws.numel(),
                 rt.stream())
     gates = q8.gemm(x, w_ih, 4 * hid, k_in) + q8.gemm(h, w_hh, 4 * hid, hid) + bias
     for i in range(m):
@@ -76,9 +77,10 @@ def test_joint_argmax_matches_oracle(rt, m):
     ids = torch.empty(m, 2, dtype=torch.int32, device='cuda')
     rt.ensure_workspace(m, n, k)
     ws = rt.workspace
+    ed, rd, pd, bd = dev(enc), dev(rows), dev(pred), dev(bias)
     for _ in range(2):  # second call checks the self-resetting tickets
-        rt.lib.call('pq8_joint_argmax', w.pointer, dev(enc).data_ptr(), dev(rows).data_ptr(), dev(pred).data_ptr(),
-                    dev(bias).data_ptr(), logits.data_ptr(), ids.data_ptr(), m, n, k, 8193, ws.data_ptr(),
+        rt.lib.call('pq8_joint_argmax', w.pointer, ed.data_ptr(), rd.data_ptr(), pd.data_ptr(),
+                    bd.data_ptr(), logits.data_ptr(), ids.data_ptr(), m, n, k, 8193, ws.data_ptr(),
                     ws.numel(), rt.stream())
         act = np.maximum(enc[rows] + pred, 0)
         gold = q8.gemm(act, raw, n, k) + bias
@@ -99,8 +101,9 @@ def test_joint_argmax_ties_lowest_index(rt):
     ids = torch.empty(1, 2, dtype=torch.int32, device='cuda')
     logits = torch.empty(1, n, device='cuda')
     z = dev(np.zeros((1, k), np.float32))
+    bd = dev(bias)
     rt.ensure_workspace(1, n, k)
-    rt.lib.call('pq8_joint_argmax', w.pointer, z.data_ptr(), None, z.data_ptr(), dev(bias).data_ptr(),
+    rt.lib.call('pq8_joint_argmax', w.pointer, z.data_ptr(), None, z.data_ptr(), bd.data_ptr(),
                 logits.data_ptr(), ids.data_ptr(), 1, n, k, 8193, rt.workspace.data_ptr(), rt.workspace.numel(),
                 rt.stream())
     assert ids.cpu().numpy().tolist() == [[19, 2]]

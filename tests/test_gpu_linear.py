@@ -3,8 +3,9 @@
 Tolerances:
 * GEMM (tensor cores, TF32 operands rounded to nearest)
   ``max|y - golden| <= 2e-3 * rms(golden)`` against the float64 golden, and
-  ``<= 2e-5 * rms`` against ``oracle.q8.gemm_tf32`` (the same TF32-rounded
-  operands summed in float64), which pins the operand rounding exactly.
+  ``<= 1e-4 * rms`` against ``oracle.q8.gemm_tf32`` (the same TF32-rounded
+  operands summed in float64): what remains is FP32 accumulation order, while
+  truncating instead of rounding an operand would show up at the 1e-3 level.
 * GEMV (FP32 FMA): ``atol = rtol = 2e-4`` as ``tests/test_cuda.py:34-50`` of
   the reference.
 * Q8_0 expansion: bit-exact.
@@ -24,7 +25,7 @@ from parakeet_cuda_b200.synthetic import q8_0_blocks
 pytestmark = pytest.mark.gpu
 
 NORTH_STAR = 2e-3
-TF32_EXACT = 2e-5
+TF32_EXACT = 1e-4
 
 
 @pytest.fixture(scope='module')
