@@ -215,43 +215,70 @@ def run_gpu(args):
     del model
     torch.cuda.synchronize()
 
+    # The timed step is one CUDA-graph replay of all 216 GEMM launches.
+    stack.step()
+    torch.cuda.synchronize()
+    graph = stack.capture()
     for _ in range(args.warmup):
-        stack.step()
+        graph.replay()
     torch.cuda.synchronize()
     sched.barrier()
 
     clocks = ClockSampler(n) if sched.rank == 0 else None
-    timer = LaunchTimer(torch)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     sched.barrier()
     start.record()
     for _ in range(args.steps):
-        stack.step(timer)
+        graph.replay()
     end.record()
     torch.cuda.synchronize()
     sched.barrier()
     clock_info = clocks.stop() if clocks else None
     ms = start.elapsed_time(end) / args.steps
     ms_max = sched.max_over_ranks(ms)
+
+    # Per-launch kernel durations (roofline): the same launches issued eagerly,
+    # each bracketed by CUDA events on the launching stream.
+    timer = LaunchTimer(torch)
+    for _ in range(args.steps):
+        stack.step(timer)
+    torch.cuda.synchronize()
     per_name = timer.totals()
     kernel_ms_step = sum(t for _, t in per_name.values()) / args.steps
+
+    # same stack with every GEMM rounding its activation tile in shared memory
+    stack.producer_tf32 = False
+    graph_rnd = stack.capture()
+    graph_rnd.replay()
+    torch.cuda.synchronize()
+    sched.barrier()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    for _ in range(args.steps):
+        graph_rnd.replay()
+    k1.record()
+    torch.cuda.synchronize()
+    ms_kernel_rounding = sched.max_over_ranks(k0.elapsed_time(k1) / args.steps)
+    stack.producer_tf32 = True
+    del graph_rnd
     status = rt.device_status()
 
     # e2e: public host API, pinned H2D of the step input and D2H of its result in the timed region
     x_host = torch.randn(rows, 1024).pin_memory()
     out_host = torch.empty(rows, 1024).pin_memory()
     for _ in range(2):
-        stack.run_host(x_host, out_host)
+        stack.run_host(x_host, out_host, graph)
     torch.cuda.synchronize()
     sched.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        stack.run_host(x_host, out_host)
+        stack.run_host(x_host, out_host, graph)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = sched.max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    del graph
 
     extras = {}
     if not args.no_extras:
@@ -291,10 +318,16 @@ def run_gpu(args):
                 'traffic_source': traffic.get('source') if traffic else None,
             },
             'e2e': {'value': frames / (e2e_ms / 1e3), 'unit': UNIT, 'h2d_bytes_per_step': rows * 1024 * 4,
-                    'd2h_bytes_per_step': rows * 1024 * 4,
+                    'd2h_bytes_per_step': rows * 1024 * 4, 'gpu_launches_per_step': stack.launches_per_step + 1,
                     'api': 'parakeet_cuda_b200.encoder.EncoderStack.run_host (pinned host in/out)'},
             'gpu_launches': stack.launches_per_step * args.steps,
             'device_status': status,
+            'x_rounding': ('GEMM inputs from outside the path (LayerNorm output, attention context, positional '
+                           'table stand-ins) are produced TF32-rounded; SiLU/GLU outputs are rounded by the fused '
+                           'epilogue; e2e rounds its uploaded input with one pq8_round_tf32 launch per step'),
+            'in_kernel_rounding': {'ms_per_step': ms_kernel_rounding,
+                                   'value': frames / (ms_kernel_rounding / 1e3),
+                                   'note': 'same step with every GEMM rounding its own X tile (no producer help)'},
         }
         if clock_info:
             line['clocks'] = clock_info
@@ -307,37 +340,62 @@ def run_gpu(args):
 
 
 def gemv_measure(torch, rt, stack):
-    """M = 1 GEMV over every packed encoder weight (216 launches, 642 MB > L2): HBM GB/s."""
-    from parakeet_cuda_b200.encoder import LAYER_PLAN
-    x = {k: torch.randn(1, k, device=rt.device) for k in (1024, 4096)}
-    y = torch.empty(1, 4096, device=rt.device)
-    ws = None
+    """M = 1 GEMV (decoder-regime kernel) against HBM bandwidth.
+
+    ``stack``: one CUDA-graph replay of a GEMV over every packed encoder weight
+    (216 launches, 642 MB > L2, so every byte comes from HBM).
+    ``single``: one launch over a [32768, 8192] Q8_0 matrix (285 MB)."""
+    from parakeet_cuda_b200.runtime import pack_host
+    from parakeet_cuda_b200.synthetic import q8_0_blocks
+    import numpy as np
+    x = {k: torch.randn(1, k, device=rt.device) for k in (1024, 4096, 8192)}
+    y = torch.empty(1, 32768, device=rt.device)
     for layer in stack.weights:
         for w in layer.values():
             rt.ensure_workspace(1, w.n, w.k)
+    big_n, big_k = 32768, 8192
+    big = rt.upload_packed(pack_host(q8_0_blocks(np.random.default_rng(5), big_n, big_k), big_n, big_k, 0,
+                                     rt.lib), big_n, big_k, 0)
+    rt.ensure_workspace(1, big_n, big_k)
     ws = rt.workspace
 
-    def run():
+    def one(w, glu=False):
+        rt.lib.call('pq8_gemv', w.pointer, x[w.k].data_ptr(), y.data_ptr(), None, None, 1, w.n, w.k,
+                    3 if glu else 0, 1.0, ws.data_ptr(), ws.numel(), rt.stream())
+
+    def sweep():
         for layer in stack.weights:
             for name, w in layer.items():
-                rt.lib.call('pq8_gemv', w.pointer, x[w.k].data_ptr(), y.data_ptr(), None, None, 1, w.n, w.k,
-                            3 if name == 'pw1_glu' else 0, 1.0, ws.data_ptr(), ws.numel(), rt.stream())
-    run()
+                one(w, name == 'pw1_glu')
+
+    sweep()
+    one(big)
     torch.cuda.synchronize()
-    reps = 5
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(reps):
-        run()
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
-    nbytes = stack.weight_bytes
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+        sweep()
+    torch.cuda.current_stream().wait_stream(side)
     peaks, src = measured_peaks()
-    gbs = nbytes / (ms / 1e3) / 1e9
-    return {'m': 1, 'bytes_per_pass': nbytes, 'ms_per_pass': ms, 'launches_per_pass': stack.launches_per_step,
-            'achieved_gbs': gbs, 'peak_gbs': peaks['hbm_gbs'], 'frac': gbs / peaks['hbm_gbs'],
-            'peak_source': f'{src}: MEASURED_PEAKS.json hbm_gbs'}
+    out = {'m': 1, 'peak_gbs': peaks['hbm_gbs'], 'peak_source': f'{src}: MEASURED_PEAKS.json hbm_gbs'}
+    reps = 5
+    for key, fn, nbytes in (('stack', g.replay, stack.weight_bytes), ('single', lambda: one(big), big.data.numel())):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / reps
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[key] = {'bytes': nbytes, 'ms': ms, 'achieved_gbs': gbs, 'frac': gbs / peaks['hbm_gbs']}
+    out['stack']['launches'] = stack.launches_per_step
+    out['single']['shape'] = [big_n, big_k]
+    del g, big
+    return out
 
 
 def cublas_tf32(torch):

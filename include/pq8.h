@@ -114,6 +114,12 @@ PQ8_API int pq8_pack_q8_0_part(const void* gguf_blocks, int n, int k_src, int k_
  * gguf_blocks: device, n_elements/32 records of 34 bytes; out: device float[n_elements]. */
 PQ8_API int pq8_dequant_q8_0(const void* gguf_blocks, float* out, long long n_elements, void* stream);
 
+/* Round n floats (device, 16-byte aligned) to TF32 in place, to nearest with
+ * ties away from zero, as the GEMM rounds its operands. A producer that writes
+ * activations this way (or a caller that rounds once an input several GEMMs
+ * read) lets those GEMMs skip their rounding pass with PQ8_FLAG_X_TF32. */
+PQ8_API int pq8_round_tf32(float* x, long long n, void* stream);
+
 /* Tensor-core GEMM (tcgen05, TF32 operands rounded to nearest, FP32 accumulate):
  *   z[m, j] = sum_k x[m, k] * W[j, k]  (+ bias[j]),  y = epilogue(z)
  * Replaces Blas.linear (gpu.py:87-90) + the elementwise epilogue kernels.

@@ -24,7 +24,7 @@ struct DeviceState {
   bool ready = false;
   int sms = 0;
   int* status = nullptr;
-  bool attr_set[8] = {};
+  bool attr_set[16] = {};
 };
 
 std::mutex g_mutex;
@@ -76,22 +76,22 @@ int encode_fn(EncodeTiledFn* fn) {
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // ---------------------------------------------------------------- GEMM
-template <int BN, int STAGES, int ACC>
+template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS>
 int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaStream_t st) {
-  using C = GemmCfg<BN, STAGES, ACC>;
+  using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS>;
   EncodeTiledFn enc;
   int rc = encode_fn(&enc);
   if (rc) return rc;
   CUtensorMap tmap;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.k), static_cast<cuuint64_t>(p.m)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.k) * sizeof(float)};
-  const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(BN)};
+  const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(C::kRowsPerCta)};
   const cuuint32_t estr[2] = {1, 1};
   CUresult cr = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return PQ8_ERR_DRIVER;
-  auto kernel = gemm_tc_kernel<BN, STAGES, ACC>;
+  auto kernel = gemm_tc_kernel<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS>;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
     if (!ds->attr_set[cfg_id]) {
@@ -101,30 +101,68 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
     }
   }
   p.m_tiles = (p.m + BN - 1) / BN;
-  const int tiles = p.n_tiles * p.m_tiles;
-  const int grid = std::min(tiles, ds->sms);
-  kernel<<<grid, C::kThreads, C::kSmemBytes, st>>>(tmap, p);
+  const int units = (PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles) * p.m_tiles;
+  const int slots = PAIR ? ds->sms / 2 : ds->sms;
+  const int grid = std::min(units, slots) * C::kCtas;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C::kCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap, p);
+  if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }
 
-// Activation-tile height: fewest waves x (BN + fixed per-K-block cost).
-// PQ8_GEMM_BN=64|128|256 in the environment forces one (used by the tests to
-// cover every tile configuration).
-int choose_bn(int m, int n_tiles, int sms) {
-  if (const char* force = std::getenv("PQ8_GEMM_BN")) {
+// GEMM configurations: activation rows per tile (the MMA N), single CTA or a
+// pair of CTAs sharing one MMA, accumulator buffers.
+enum GemmConfig { kG256 = 0, kG192, kG128, kG64, kP256, kP192, kP128, kNumGemmConfigs };
+struct GemmShape {
+  int bn, pair, acc;
+};
+constexpr GemmShape kGemmShapes[kNumGemmConfigs] = {{256, 0, 1}, {192, 0, 2}, {128, 0, 2}, {64, 0, 2},
+                                                    {256, 1, 1}, {192, 1, 2}, {128, 1, 2}};
+
+// Fewest estimated cycles: waves x per-tile cost, where a tile costs its MMA
+// work (bn) plus a fixed weight-conversion share. Measured on B200 at
+// M = 3000, CTA pairs run slightly slower per SM than single CTAs (their
+// cross-CTA handoffs add latency while shared-memory traffic is not the
+// limit), hence their small penalty.
+// PQ8_GEMM_CONFIG=<index> or PQ8_GEMM_BN=64|128|192|256 (single CTA) in the
+// environment force a configuration; the tests use this to cover all of them.
+int choose_gemm(int m, int n_tiles, int sms) {
+  if (const char* force = std::getenv("PQ8_GEMM_CONFIG")) {
     const int v = std::atoi(force);
-    if (v == 64 || v == 128 || v == 256) return v;
+    if (v >= 0 && v < kNumGemmConfigs) return v;
   }
-  const int options[3] = {256, 128, 64};
-  int best = 256;
-  long best_cost = -1;
-  for (int bn : options) {
-    const long tiles = static_cast<long>(n_tiles) * ((m + bn - 1) / bn);
-    const long waves = (tiles + sms - 1) / sms;
-    const long cost = waves * (bn + 48);
+  if (const char* force = std::getenv("PQ8_GEMM_BN")) {
+    switch (std::atoi(force)) {
+      case 256: return kG256;
+      case 192: return kG192;
+      case 128: return kG128;
+      case 64: return kG64;
+      default: break;
+    }
+  }
+  int best = kG256;
+  double best_cost = -1;
+  for (int c = 0; c < kNumGemmConfigs; ++c) {
+    const GemmShape g = kGemmShapes[c];
+    const long units = static_cast<long>(g.pair ? (n_tiles + 1) / 2 : n_tiles) * ((m + g.bn - 1) / g.bn);
+    const long slots = g.pair ? sms / 2 : sms;
+    const long waves = (units + slots - 1) / slots;
+    const double per_tile = (g.bn + 48) * (g.pair ? 1.05 : 1.0);
+    const double cost = waves * per_tile;
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
-      best = bn;
+      best = c;
     }
   }
   return best;
@@ -199,6 +237,22 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restric
   for (int i = 0; i < 32; ++i) o[i] = s * static_cast<float>(static_cast<int8_t>(rec[2 + i]));
 }
 
+__global__ void round_tf32_kernel(uint32_t* __restrict__ x, long long n) {
+  const long long n4 = n >> 2;
+  uint4* x4 = reinterpret_cast<uint4*>(x);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    uint4 v = x4[i];
+    v.x = tf32_round_bits(v.x);
+    v.y = tf32_round_bits(v.y);
+    v.z = tf32_round_bits(v.z);
+    v.w = tf32_round_bits(v.w);
+    x4[i] = v;
+  }
+  for (long long i = (n4 << 2) + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    x[i] = tf32_round_bits(x[i]);
+}
+
 int check_linear_args(const void* w, const float* x, const float* y, const float* resid, int m, int n, int k,
                       int epi) {
   if (m < 0 || n < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
@@ -251,6 +305,20 @@ extern "C" int pq8_dequant_q8_0(const void* gguf_blocks, float* out, long long n
   return to_code(cudaGetLastError());
 }
 
+extern "C" int pq8_round_tf32(float* x, long long n, void* stream) {
+  if (n < 0) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (n == 0) return PQ8_OK;
+  if (x == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(x, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  const long long blocks = std::min<long long>((n / 4 + 255) / 256 + 1, 8LL * ds->sms);
+  round_tf32_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<uint32_t*>(x), n);
+  return to_code(cudaGetLastError());
+}
+
 extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bias, const float* resid, int m, int n,
                         int k, int epilogue, float alpha, int flags, void* stream) {
   int rc = check_linear_args(w, x, y, resid, m, n, k, epilogue);
@@ -276,10 +344,14 @@ extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bi
   p.n_tiles = (n + kTileRows - 1) / kTileRows;
   p.k_blocks = k / 32;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (choose_bn(m, p.n_tiles, ds->sms)) {
-    case 256: return launch_gemm<256, 5, 1>(ds, 0, x, p, st);
-    case 128: return launch_gemm<128, 6, 2>(ds, 1, x, p, st);
-    default: return launch_gemm<64, 8, 2>(ds, 2, x, p, st);
+  switch (choose_gemm(m, p.n_tiles, ds->sms)) {
+    case kG256: return launch_gemm<256, 6, 6, 1, false, 3>(ds, kG256, x, p, st);
+    case kG192: return launch_gemm<192, 7, 4, 2, false, 2>(ds, kG192, x, p, st);
+    case kG128: return launch_gemm<128, 10, 4, 2, false, 2>(ds, kG128, x, p, st);
+    case kG64: return launch_gemm<64, 12, 4, 2, false, 2>(ds, kG64, x, p, st);
+    case kP256: return launch_gemm<256, 10, 4, 1, true, 2>(ds, kP256, x, p, st);
+    case kP192: return launch_gemm<192, 12, 4, 2, true, 2>(ds, kP192, x, p, st);
+    default: return launch_gemm<128, 14, 4, 2, true, 2>(ds, kP128, x, p, st);
   }
 }
 

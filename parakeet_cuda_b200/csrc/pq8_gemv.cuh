@@ -102,6 +102,33 @@ __device__ __forceinline__ void argmax_merge(float& v, int& i, float ov, int oi)
   }
 }
 
+// acc[m] += scale * sum_j q_j * x[m][j] over one 32-wide K block of this thread's row.
+template <int MT>
+__device__ __forceinline__ void gemv_block(const uint4 q0, const uint4 q1, uint16_t scale_bits, const float* xk,
+                                           int nk, float (&acc)[MT]) {
+  const float sc = __half2float(__ushort_as_half(scale_bits));
+  const uint32_t wd[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
+                          q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
+  float inner[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) inner[m] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float q_0 = i8_to_f32(wd[j >> 2], 0), q_1 = i8_to_f32(wd[j >> 2], 1);
+    const float q_2 = i8_to_f32(wd[j >> 2], 2), q_3 = i8_to_f32(wd[j >> 2], 3);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const float4 xv = *reinterpret_cast<const float4*>(xk + m * nk + j);
+      inner[m] = fmaf(q_0, xv.x, inner[m]);
+      inner[m] = fmaf(q_1, xv.y, inner[m]);
+      inner[m] = fmaf(q_2, xv.z, inner[m]);
+      inner[m] = fmaf(q_3, xv.w, inner[m]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = fmaf(sc, inner[m], acc[m]);
+}
+
 template <int MT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) {
   __shared__ float xs[kGemvXSmemFloats];
@@ -134,33 +161,27 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
   for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
 
   const uint8_t* tile_base = p.w + PQ8_HEADER_BYTES + (size_t)t * p.k_blocks * kRecordBytes;
-#pragma unroll 2
-  for (int kb = kb0; kb < kb1; ++kb) {
-    const uint8_t* rec = tile_base + (size_t)kb * kRecordBytes;
-    const uint4 q0 = ldg_stream(rec + r * 16);
-    const uint4 q1 = ldg_stream(rec + 2048 + r * 16);
-    const float sc = __half2float(__ushort_as_half(ldg_u16(rec + kScaleOffset + r * 2)));
-    const uint32_t wd[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
-                            q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
-    const float* xk = xs + (kb - kb0) * 32;
-    float inner[MT];
+  // Loads for U consecutive K blocks are issued before any of them is used, so
+  // each thread keeps U x 34 bytes of weights in flight.
+  constexpr int U = MT <= 2 ? 4 : 2;
+  int kb = kb0;
+  for (; kb + U <= kb1; kb += U) {
+    uint4 qa[U], qb[U];
+    uint16_t sh[U];
 #pragma unroll
-    for (int m = 0; m < MT; ++m) inner[m] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float q_0 = i8_to_f32(wd[j >> 2], 0), q_1 = i8_to_f32(wd[j >> 2], 1);
-      const float q_2 = i8_to_f32(wd[j >> 2], 2), q_3 = i8_to_f32(wd[j >> 2], 3);
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        const float4 xv = *reinterpret_cast<const float4*>(xk + m * nk + j);
-        inner[m] = fmaf(q_0, xv.x, inner[m]);
-        inner[m] = fmaf(q_1, xv.y, inner[m]);
-        inner[m] = fmaf(q_2, xv.z, inner[m]);
-        inner[m] = fmaf(q_3, xv.w, inner[m]);
-      }
+    for (int u = 0; u < U; ++u) {
+      const uint8_t* rec = tile_base + (size_t)(kb + u) * kRecordBytes;
+      qa[u] = ldg_stream(rec + r * 16);
+      qb[u] = ldg_stream(rec + 2048 + r * 16);
+      sh[u] = ldg_u16(rec + kScaleOffset + r * 2);
     }
 #pragma unroll
-    for (int m = 0; m < MT; ++m) acc[m] = fmaf(sc, inner[m], acc[m]);
+    for (int u = 0; u < U; ++u) gemv_block<MT>(qa[u], qb[u], sh[u], xs + (kb + u - kb0) * 32, nk, acc);
+  }
+  for (; kb < kb1; ++kb) {
+    const uint8_t* rec = tile_base + (size_t)kb * kRecordBytes;
+    gemv_block<MT>(ldg_stream(rec + r * 16), ldg_stream(rec + 2048 + r * 16), ldg_u16(rec + kScaleOffset + r * 2),
+                   xs + (kb - kb0) * 32, nk, acc);
   }
 
   if (p.splits > 1) {

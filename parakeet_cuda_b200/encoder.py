@@ -69,8 +69,14 @@ LAYER_PLAN = (
 class EncoderStack:
     """All Q8_0 linears of ``layers`` encoder layers over ``rows`` activation rows on one device."""
 
-    def __init__(self, model, runtime: Runtime, rows: int, layers: int = 24, seed: int = 0):
+    def __init__(self, model, runtime: Runtime, rows: int, layers: int = 24, seed: int = 0,
+                 producer_tf32: bool = True):
+        """``producer_tf32``: the GEMM inputs that come from outside the contraction path
+        (LayerNorm outputs, attention context, positional table) are produced TF32-rounded,
+        as a fused producer would write them, and every GEMM skips its rounding pass.
+        With False, those GEMMs round their input tile in shared memory themselves."""
         self.rt, self.rows, self.layers = runtime, rows, layers
+        self.producer_tf32 = producer_tf32
         dev = runtime.device
         self.weights: list[dict[str, PackedWeight]] = []
         for l in range(layers):
@@ -95,6 +101,9 @@ class EncoderStack:
             'pos_out': torch.empty(rows, D_MODEL, **f32),
             'gate': torch.empty(rows, D_MODEL, **f32),
         }
+        if producer_tf32:
+            for name in ('norm', 'ctx', 'pos'):
+                self.round_buffer(name)
 
     @property
     def launches_per_step(self) -> int:
@@ -103,11 +112,17 @@ class EncoderStack:
     def flops_per_step(self) -> int:
         return self.rows * self.layers * flops_per_row_per_layer()
 
+    def round_buffer(self, name: str) -> None:
+        t = self.buffers[name]
+        self.rt.lib.call('pq8_round_tf32', t.data_ptr(), t.numel(), self.rt.stream())
+
     def launch(self, layer: int, entry) -> None:
         name, _, n, k, epi, alpha, src, dst, flags = entry
         w = self.weights[layer][name]
         b = self.buffers
         resid = b['resid'] if epi == EPI_RESIDUAL else None
+        if self.producer_tf32:
+            flags |= FLAG_X_TF32
         self.rt.gemm(b[src], w, out=b[dst], resid=resid, epilogue=epi, alpha=alpha, flags=flags)
 
     def step(self, timer=None) -> None:
@@ -120,7 +135,23 @@ class EncoderStack:
                 if timer is not None:
                     timer.stop(entry[0])
 
-    def run_host(self, x_host: torch.Tensor, out_host: torch.Tensor) -> torch.Tensor:
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """Record one step (every launch of ``step``) as a CUDA graph on a side stream.
+
+        Replaying it removes the host's per-launch cost (argument checks, tensor-map
+        encoding, ctypes) from the critical path; the launches and their arguments
+        are identical. Call ``step`` once before capturing so that per-device state
+        (kernel attributes) is initialised outside the capture."""
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(self.rt.device)
+        side.wait_stream(torch.cuda.current_stream(self.rt.device))
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                self.step()
+        torch.cuda.current_stream(self.rt.device).wait_stream(side)
+        return graph
+
+    def run_host(self, x_host: torch.Tensor, out_host: torch.Tensor, graph=None) -> torch.Tensor:
         """Public end-to-end call on host buffers (pinned for asynchronous copies):
         ``x_host`` [rows, 1024] is the windows' encoder input, which starts the
         residual stream and stands in for every LayerNorm output; the final
@@ -128,6 +159,11 @@ class EncoderStack:
         current stream; the caller synchronizes."""
         self.buffers['norm'].copy_(x_host, non_blocking=True)
         self.buffers['resid'].copy_(self.buffers['norm'], non_blocking=True)
-        self.step()
+        if self.producer_tf32:
+            self.round_buffer('norm')
+        if graph is not None:
+            graph.replay()
+        else:
+            self.step()
         out_host.copy_(self.buffers['resid'], non_blocking=True)
         return out_host

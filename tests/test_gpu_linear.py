@@ -87,9 +87,14 @@ def test_gemv_reference_cases(rt, golden_dir):
         np.testing.assert_allclose(y.cpu().numpy()[0], data[f'n{n}_k{k}_gemv'], atol=2e-4, rtol=2e-4)
 
 
-@pytest.mark.parametrize('bn', ['64', '128', '256'])
-def test_gemm_reference_contract(rt, golden_dir, bn, monkeypatch):
-    monkeypatch.setenv('PQ8_GEMM_BN', bn)
+# Tile configurations of pq8_gemm (PQ8_GEMM_CONFIG): single CTA with 256/192/128/64
+# activation rows per tile, then CTA pairs (tcgen05 cta_group::2) with 256/192/128.
+CONFIGS = [str(i) for i in range(7)]
+
+
+@pytest.mark.parametrize('cfg', CONFIGS)
+def test_gemm_reference_contract(rt, golden_dir, cfg, monkeypatch):
+    monkeypatch.setenv('PQ8_GEMM_CONFIG', cfg)
     data = np.load(golden_dir / 'q8_gemm_contract.npz')
     for m, k, n, raw, x in contract_cases():
         w = rt.pack(raw, n, k)
@@ -115,21 +120,21 @@ def test_gemm_config0(rt):
     assert e_gold < 1.8e-3
 
 
-@pytest.mark.parametrize('bn', ['64', '128', '256'])
+@pytest.mark.parametrize('cfg', CONFIGS)
 @pytest.mark.parametrize('m,n,k', [(1, 3, 32), (31, 200, 64), (65, 128, 96), (200, 385, 160), (257, 64, 32),
-                                   (300, 1000, 640)])
-def test_gemm_tails(rt, bn, m, n, k, monkeypatch):
-    monkeypatch.setenv('PQ8_GEMM_BN', bn)
+                                   (300, 1000, 640), (521, 300, 128)])
+def test_gemm_tails(rt, cfg, m, n, k, monkeypatch):
+    monkeypatch.setenv('PQ8_GEMM_CONFIG', cfg)
     rng = np.random.default_rng(m * 7 + n * 3 + k)
     raw = q8_0_blocks(rng, n, k, qmin=-128)
     x = rng.normal(size=(m, k)).astype(np.float32)
     check_gemm(rt.gemm(dev(x), rt.pack(raw, n, k)), x, raw, n, k)
 
 
-@pytest.mark.parametrize('bn', ['64', '256'])
+@pytest.mark.parametrize('cfg', ['0', '3', '4', '6'])
 @pytest.mark.parametrize('epi', [EPI_NONE, EPI_RELU, EPI_SILU, EPI_RESIDUAL, EPI_GLU])
-def test_gemm_epilogues(rt, epi, bn, monkeypatch):
-    monkeypatch.setenv('PQ8_GEMM_BN', bn)
+def test_gemm_epilogues(rt, epi, cfg, monkeypatch):
+    monkeypatch.setenv('PQ8_GEMM_CONFIG', cfg)
     rng = np.random.default_rng(epi + 10)
     m, n, k = 150, 384, 256
     raw = q8_0_blocks(rng, n, k)
@@ -141,6 +146,15 @@ def test_gemm_epilogues(rt, epi, bn, monkeypatch):
     y = dev(resid) if epi == EPI_RESIDUAL else None
     y = rt.gemm(dev(x), w, out=y, bias=dev(bias), resid=y, epilogue=epi, alpha=0.5)
     check_gemm(y, x, raw, n, k, epi, bias, resid, 0.5)
+
+
+@pytest.mark.parametrize('cfg', CONFIGS)
+def test_gemm_config0_every_tile_config(rt, cfg, monkeypatch):
+    monkeypatch.setenv('PQ8_GEMM_CONFIG', cfg)
+    rng = np.random.default_rng(0)
+    raw = q8_0_blocks(rng, 4096, 1024)
+    x = rng.normal(size=(128, 1024)).astype(np.float32)
+    check_gemm(rt.gemm(dev(x), rt.pack(raw, 4096, 1024)), x, raw, 4096, 1024)
 
 
 def test_gemm_tf32_flags(rt):
