@@ -185,6 +185,21 @@ PQ8_API int pq8_joint_argmax(const void* w, const float* enc, const int* enc_row
 PQ8_API int pq8_tdt_commit(float* h, float* c, const float* h_new, const float* c_new, const int* mask, int m,
                            int layers, int hidden, void* stream);
 
+/* pq8_gemv without a workspace argument, for callers that cannot allocate
+ * device memory: a host that keeps all device memory in its own pre-reserved
+ * pool, or a latency-critical loop where cudaMalloc would synchronize the
+ * device. It has no counterpart in the reference (whose cuBLAS path uses a
+ * caller-reserved workspace). Scratch space comes from a fixed 4 MiB array
+ * built into the library, held by every GPU that loads the library until the
+ * process exits; shapes whose pq8_gemv_workspace_size() exceeds 4 MiB return
+ * PQ8_ERR_WORKSPACE. The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress) and should come before any stream capture. All calls
+ * on a device share the array: calls that overlap on the GPU race, so order
+ * them (one stream). Each call clears the array's counters itself, and calls
+ * no cudaMalloc/cudaFree. Results equal pq8_gemv's for the same inputs. */
+PQ8_API int pq8_gemv_static(const void* w, const float* x, float* y, const float* bias, const float* resid,
+                            int m, int n, int k, int epilogue, float alpha, void* stream);
+
 /* Read and clear the device-side status word that kernels set on a layout
  * mismatch or an expired bounded wait. Synchronizes `stream`. *status = 0 or
  * PQ8_ERR_LAYOUT / PQ8_ERR_TIMEOUT. */

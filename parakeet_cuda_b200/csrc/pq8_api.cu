@@ -506,3 +506,81 @@ extern "C" int pq8_device_status(int* status, void* stream) {
   *status = value;
   return PQ8_OK;
 }
+
+// ---------------------------------------------------------------------------
+// GEMV entry point that allocates nothing.
+//
+// Some callers cannot hand the library a workspace: a host that reserves all
+// device memory up front in its own pool and forbids other allocations, or a
+// latency-critical decode loop where a cudaMalloc would implicitly
+// synchronize the device. For them the split-K partials and the arrival
+// tickets live in this fixed-size array, which every GPU that loads the
+// library holds until the process exits. All calls on a device share it:
+// calls that overlap on the GPU (on different streams, or from several host
+// threads) race on it, so they must be ordered, e.g. on one stream.
+namespace pq8 {
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB per device
+__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mutex;
+void* g_static_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return to_code(e);
+  if (dev < 0 || dev >= kMaxDevices) return PQ8_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return to_code(e);
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return PQ8_OK;
+}
+
+}  // namespace
+}  // namespace pq8
+
+extern "C" int pq8_gemv_static(const void* w, const float* x, float* y, const float* bias, const float* resid, int m,
+                               int n, int k, int epilogue, float alpha, void* stream) {
+  int rc = check_linear_args(w, x, y, resid, m, n, k, epilogue);
+  if (rc || m == 0) return rc;
+  if (m > PQ8_GEMV_MAX_M) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  DeviceState* ds;
+  if ((rc = device_state(&ds))) return rc;
+  const GemvPlan plan = plan_gemv(m, n, k, ds->sms);
+  if (plan.total > kStaticScratchBytes) return PQ8_ERR_WORKSPACE;  // shape needs more than the 4 MiB built in
+  void* scratch = nullptr;
+  if ((rc = static_scratch(&scratch))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps whatever the previous call left; the tickets must start at zero.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, plan.off_bval, st);
+  if (e != cudaSuccess) return to_code(e);
+  GemvParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.x0 = x;
+  p.x_mode = kXPlain;
+  p.y = y;
+  p.bias = bias;
+  p.resid = resid;
+  p.alpha = alpha;
+  p.epi = epilogue;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.layout = epilogue == PQ8_EPI_GLU ? PQ8_LAYOUT_GLU : PQ8_LAYOUT_ROWS;
+  p.out_cols = epilogue == PQ8_EPI_GLU ? n / 2 : n;
+  p.n_tiles = (n + kTileRows - 1) / kTileRows;
+  p.k_blocks = k / 32;
+  p.mode = kGemvLinear;
+  return launch_gemv(ds, p, scratch, kStaticScratchBytes, st);
+}
+

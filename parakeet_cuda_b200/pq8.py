@@ -49,6 +49,7 @@ SIGNATURES = {
     'pq8_gemv_workspace_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
     'pq8_workspace_init': ([_P, _SZ, _P], _I),
     'pq8_gemv': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _SZ, _P], _I),
+    'pq8_gemv_static': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P], _I),
     'pq8_linear': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P, _SZ, _P], _I),
     'pq8_lstm_layer': ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P], _I),
     'pq8_joint_argmax': ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P], _I),
