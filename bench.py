@@ -43,7 +43,7 @@ UNIT = 'frames/s'
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', choices=('pq8', 'reference'), default='pq8')
     ap.add_argument('--windows-per-gpu', type=int, default=8)
@@ -78,7 +78,7 @@ class ClockSampler:
         try:
             self.f = open(self.path, 'w')
             self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={q}', '--format=csv,noheader,nounits',
-                                          '-i', ','.join(str(i) for i in range(gpus)), '-lms', '100'],
+                                          '-i', ','.join(str(i) for i in range(gpus)), '-lms', '50'],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -309,6 +309,8 @@ def run_gpu(args):
                 'bound': 'tensor', 'achieved': achieved,
                 'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved / peak,
                 'traffic': traffic.get('bytes_per_launch') if traffic else None,
+                'traffic_unit': 'DRAM bytes per launch (mean of the 9 linears; ncu capture)',
+                'traffic_bytes_per_step': traffic.get('bytes_per_step_24_layers') if traffic else None,
                 'peak_source': (f'{peak_src}: MEASURED_PEAKS.json bf16_tflops_sustained / 2 (dense TF32 is half '
                                 f'the BF16 rate); kernel timed inside a long step'),
                 'frac_of_burst': achieved / (peaks['bf16_tflops'] / 2),

@@ -217,11 +217,12 @@ int launch_gemv(DeviceState* ds, GemvParams p, void* ws, size_t ws_bytes, cudaSt
   p.partial = reinterpret_cast<float*>(base + g.off_partial);
   p.status = ds->status;
   const int grid = p.n_tiles * g.splits;
+  const size_t smem = sizeof(float) * g.mt * g.kbps * 32;
   switch (g.mt) {
-    case 1: gemv_kernel<1><<<grid, kGemvThreads, 0, st>>>(p); break;
-    case 2: gemv_kernel<2><<<grid, kGemvThreads, 0, st>>>(p); break;
-    case 4: gemv_kernel<4><<<grid, kGemvThreads, 0, st>>>(p); break;
-    default: gemv_kernel<8><<<grid, kGemvThreads, 0, st>>>(p); break;
+    case 1: gemv_kernel<1><<<grid, kGemvThreads, smem, st>>>(p); break;
+    case 2: gemv_kernel<2><<<grid, kGemvThreads, smem, st>>>(p); break;
+    case 4: gemv_kernel<4><<<grid, kGemvThreads, smem, st>>>(p); break;
+    default: gemv_kernel<8><<<grid, kGemvThreads, smem, st>>>(p); break;
   }
   return to_code(cudaGetLastError());
 }

@@ -62,7 +62,7 @@ struct GemvParams {
 };
 
 constexpr int kGemvThreads = 128;
-constexpr int kGemvXSmemFloats = 10240;  // 40 KB of staged activations per CTA
+constexpr int kGemvXSmemFloats = 10240;  // at most 40 KB of staged activations per CTA
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
@@ -129,9 +129,12 @@ __device__ __forceinline__ void gemv_block(const uint4 q0, const uint4 q1, uint1
   for (int m = 0; m < MT; ++m) acc[m] = fmaf(sc, inner[m], acc[m]);
 }
 
+// Dynamic shared memory: the staged activations of this CTA's K range
+// (MT x kb_per_split x 32 floats), sized per launch so that small rows leave
+// room for more resident CTAs, i.e. more loads in flight per SM.
 template <int MT>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) {
-  __shared__ float xs[kGemvXSmemFloats];
+__global__ void __launch_bounds__(kGemvThreads, MT <= 2 ? 8 : 4) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) float xs[];
   __shared__ float gate_s[MT][4][32];
   __shared__ float red_v[4][MT][2];
   __shared__ int red_i[4][MT][2];
