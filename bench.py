@@ -284,6 +284,8 @@ def run_gpu(args):
     if not args.no_extras:
         extras['gemv'] = gemv_measure(torch, rt, stack)
         extras['tf32_cublas_tflops'] = cublas_tf32(torch)
+        extras['tdt'] = tdt_measure(torch, rt)
+        extras['sweep'] = sweep_measure(torch, rt)
     sched.barrier()
 
     if sched.rank == 0:
@@ -397,6 +399,73 @@ def gemv_measure(torch, rt, stack):
     out['stack']['launches'] = stack.launches_per_step
     out['single']['shape'] = [big_n, big_k]
     del g, big
+    return out
+
+
+def tdt_measure(torch, rt):
+    """greedy TDT loop with random weights, ~1000 decode steps per stream,
+    batch 1 and batch 64 (lock-step; one joint launch per group of 8 streams per step)."""
+    import time
+    import numpy as np
+    from parakeet_cuda_b200.decoder import PQ8Decoder
+    from parakeet_cuda_b200.pq8 import EPI_NONE
+    from parakeet_cuda_b200.synthetic import SyntheticParakeet
+    from parakeet_cuda_b200.tdt import greedy_decode_batch
+    model = SyntheticParakeet(seed=11, encoder_layers=0)
+    rt.load_weights(model, ['joint.enc.weight', 'joint.enc.bias'])
+    w_enc, b_enc = rt.weight('joint.enc.weight'), rt.weight('joint.enc.bias').reshape(-1)
+    frames = 1150   # ~1000 joint calls per stream with these weights
+    out = {'frames_per_stream': frames, 'durations': [0, 1, 2, 3, 4]}
+    for batch in (1, 64):
+        enc = torch.randn(batch * frames, 1024, device=rt.device)      # encoder outputs ~ N(0, 1)
+        t0 = time.perf_counter()
+        projected = rt.gemm(enc, w_enc, bias=b_enc, epilogue=EPI_NONE)  # joint.enc projection (Encoder.project)
+        torch.cuda.synchronize()
+        t_proj = time.perf_counter() - t0
+        streams = [p.cpu().numpy() for p in projected.reshape(batch, frames, -1)]
+        dec = PQ8Decoder(model, rt, batch=batch)
+        greedy_decode_batch([s[:20] for s in streams], PQ8Decoder(model, rt, batch=batch), model.metadata['asr.tdt.durations'])
+        t0 = time.perf_counter()
+        res = greedy_decode_batch(streams, dec, model.metadata['asr.tdt.durations'])
+        t_dec = time.perf_counter() - t0
+        calls = sum(r['joint_calls'] for r in res)
+        steps = dec.joint_calls
+        out[f'batch{batch}'] = {'lockstep_steps': steps, 'joint_calls': calls,
+                                'tokens': sum(len(r['tokens']) for r in res), 'predict_launches': dec.predict_calls,
+                                'seconds': t_dec, 'steps_per_s': steps / t_dec, 'joint_calls_per_s': calls / t_dec,
+                                'projection_ms': t_proj * 1e3}
+    return out
+
+
+def sweep_measure(torch, rt):
+    """BASELINE config 4 roofline sweep on one GPU: M x (N, K) through pq8_linear.
+    Roofline per point = min(TF32 peak, AI x HBM), AI = 2MNK / (1.0625 NK + 4MK + 4MN)."""
+    import numpy as np
+    from parakeet_cuda_b200.synthetic import q8_0_blocks
+    peaks, _ = measured_peaks()
+    p_tf32, bw = peaks['bf16_tflops_sustained'] / 2 * 1e12, peaks['hbm_gbs'] * 1e9
+    out = []
+    for n, k in ((1024, 1024), (4096, 1024), (1024, 4096), (2560, 640), (8197, 640)):
+        w = rt.pack(q8_0_blocks(np.random.default_rng(n + k), n, k), n, k)
+        for m in (1, 16, 128, 1024, 8192, 65536):
+            x = torch.randn(m, k, device=rt.device)
+            y = torch.empty(m, n, device=rt.device)
+            rt.linear(x, w, out=y)
+            torch.cuda.synchronize()
+            reps = 10
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                rt.linear(x, w, out=y)
+            b.record()
+            torch.cuda.synchronize()
+            s_ = a.elapsed_time(b) / reps / 1e3
+            flops, nbytes = 2 * m * n * k, 1.0625 * n * k + 4 * m * k + 4 * m * n
+            roof = min(p_tf32, flops / nbytes * bw)
+            out.append({'m': m, 'n': n, 'k': k, 'us': s_ * 1e6, 'tflops': flops / s_ / 1e12,
+                        'gbs': nbytes / s_ / 1e9, 'frac_of_roofline': flops / s_ / roof,
+                        'bound': 'hbm' if flops / nbytes * bw < p_tf32 else 'tensor'})
+            del x, y
     return out
 
 

@@ -124,7 +124,7 @@ def test_tdt_decode_matches_reference_golden(rt, golden_dir):
         assert r['joint_calls'] == case['joint_calls']
 
 
-@pytest.mark.parametrize('batch', [1, 4, 8])
+@pytest.mark.parametrize('batch', [1, 4, 8, 13])
 def test_tdt_batched_decode_matches_oracle(rt, batch):
     model = SyntheticParakeet(seed=12, encoder_layers=0, blank_bias=3.0)
     rng = np.random.default_rng(40 + batch)
@@ -135,6 +135,17 @@ def test_tdt_batched_decode_matches_oracle(rt, batch):
         ref = otdt.greedy_decode(p, otdt.Decoder64(model), DURATIONS)
         assert g['tokens'] == ref['tokens']
         assert g['decode_trace'] == ref['decode_trace']
+
+
+def test_tdt_1000_steps_matches_oracle(rt):
+    """BASELINE config 3 at batch 1: ~1000 joint calls, ids identical to the float64 oracle."""
+    model = SyntheticParakeet(seed=11, encoder_layers=0)
+    projected = np.random.default_rng(2026).normal(size=(1150, 640)).astype(np.float32)
+    got = greedy_decode(projected, PQ8Decoder(model, rt, batch=1), DURATIONS)
+    ref = otdt.greedy_decode(projected, otdt.Decoder64(model), DURATIONS)
+    assert got["joint_calls"] >= 1000
+    assert got['tokens'] == ref['tokens']
+    assert got['decode_trace'] == ref['decode_trace']
 
 
 def test_status_clean(rt):
