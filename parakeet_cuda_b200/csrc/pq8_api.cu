@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "pq8.h"
@@ -91,6 +92,20 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return PQ8_ERR_DRIVER;
+  // Output tensor map for the staged epilogue: TMA needs a 16-byte-aligned base
+  // and row stride; other outputs are written with plain stores.
+  CUtensorMap tmap_y;
+  std::memset(&tmap_y, 0, sizeof(tmap_y));
+  p.tma_store = (p.out_cols % 4 == 0) && aligned(p.y, 16);
+  if (p.tma_store) {
+    const cuuint64_t ydims[2] = {static_cast<cuuint64_t>(p.out_cols), static_cast<cuuint64_t>(p.m)};
+    const cuuint64_t ystrides[1] = {static_cast<cuuint64_t>(p.out_cols) * sizeof(float)};
+    const cuuint32_t ybox[2] = {static_cast<cuuint32_t>(p.epi == PQ8_EPI_GLU ? 64 : 128), 32};
+    cr = enc(&tmap_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, p.y, ydims, ystrides, ybox, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return PQ8_ERR_DRIVER;
+  }
   auto kernel = gemm_tc_kernel<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS>;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
@@ -116,7 +131,7 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap, tmap_y, p);
   if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }
@@ -346,13 +361,13 @@ extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bi
   p.k_blocks = k / 32;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (choose_gemm(m, p.n_tiles, ds->sms)) {
-    case kG256: return launch_gemm<256, 6, 6, 1, false, 3>(ds, kG256, x, p, st);
-    case kG192: return launch_gemm<192, 7, 4, 2, false, 2>(ds, kG192, x, p, st);
-    case kG128: return launch_gemm<128, 10, 4, 2, false, 2>(ds, kG128, x, p, st);
-    case kG64: return launch_gemm<64, 12, 4, 2, false, 2>(ds, kG64, x, p, st);
-    case kP256: return launch_gemm<256, 10, 4, 1, true, 2>(ds, kP256, x, p, st);
-    case kP192: return launch_gemm<192, 12, 4, 2, true, 2>(ds, kP192, x, p, st);
-    default: return launch_gemm<128, 14, 4, 2, true, 2>(ds, kP128, x, p, st);
+    case kG256: return launch_gemm<256, 4, 6, 1, false, 3>(ds, kG256, x, p, st);
+    case kG192: return launch_gemm<192, 5, 4, 2, false, 2>(ds, kG192, x, p, st);
+    case kG128: return launch_gemm<128, 7, 4, 2, false, 2>(ds, kG128, x, p, st);
+    case kG64: return launch_gemm<64, 10, 4, 2, false, 2>(ds, kG64, x, p, st);
+    case kP256: return launch_gemm<256, 7, 4, 1, true, 2>(ds, kP256, x, p, st);
+    case kP192: return launch_gemm<192, 8, 4, 2, true, 2>(ds, kP192, x, p, st);
+    default: return launch_gemm<128, 10, 4, 2, true, 2>(ds, kP128, x, p, st);
   }
 }
 

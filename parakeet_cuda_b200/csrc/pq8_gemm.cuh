@@ -57,6 +57,7 @@ struct GemmParams {
   int layout;
   int out_cols;
   int n_tiles, k_blocks, m_tiles;
+  int tma_store;  // 1: epilogue stages chunks in shared memory and writes them with TMA stores
 };
 
 template <int BN_, int STAGES_, int ASLOTS_, int ACC_, bool PAIR_, int GROUPS_ = 2, int GROUP_WARPS_ = 4,
@@ -79,7 +80,10 @@ struct GemmCfg {
   static constexpr int kXStageBytes = kRowsPerCta * 128;  // rows x 32 fp32
   static constexpr int kXOff = 0;
   static constexpr int kWOff = STAGES * kXStageBytes;
-  static constexpr int kBarOff = kWOff + STAGES * kRecordBytes;
+  // Epilogue staging: 2 column halves x 2 buffers x [32 activation rows][128 output columns] fp32.
+  static constexpr int kOutChunkFloats = 32 * 128;
+  static constexpr int kOutOff = kWOff + STAGES * kRecordBytes;
+  static constexpr int kBarOff = kOutOff + 4 * kOutChunkFloats * 4;
   static constexpr int kNumBars = 2 * STAGES + 2 * ASLOTS + 2 * ACC + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kUsedBytes = kMiscOff + 16;
@@ -98,7 +102,7 @@ struct GemmCfg {
   static_assert(kRowsPerCta % 8 == 0, "activation rows per CTA must fill 8-row swizzle atoms");
   static_assert(ASLOTS % kGroups == 0, "each converter group owns whole tensor-memory slots");
   static_assert(GROUP_WARPS_ == 4 || GROUP_WARPS_ == 8, "a converter group covers the 4 TMEM lane quarters");
-  static_assert(kEpiCols == 16 || kEpiCols == 32, "epilogue chunk is 16 or 32 columns");
+  static_assert(kEpiCols == 32, "the staged epilogue writes 32 activation rows per chunk");
 };
 
 // Bounded wait used on the teardown path: ignores the abort flag.
@@ -114,12 +118,14 @@ __device__ __forceinline__ float silu_fast(float z) { return __fdividef(z, 1.0f 
 
 template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS = 2, int GROUP_WARPS = 4, int EPI_COLS = 32>
 __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, GROUP_WARPS, EPI_COLS>::kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
+                   const GemmParams p) {
   using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, GROUP_WARPS, EPI_COLS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xs = smem + C::kXOff;
   uint8_t* ws = smem + C::kWOff;
+  float* out_stage = reinterpret_cast<float*>(smem + C::kOutOff);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* empty = full + STAGES;
   uint64_t* conv = empty + STAGES;
@@ -159,7 +165,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     mbar_init(drain, 1);
     fence_mbar_init();
   }
-  if (warp == C::kTmaWarp && lane == 0) prefetch_tmap(&tmap_x);
+  if (warp == C::kTmaWarp && lane == 0) {
+    prefetch_tmap(&tmap_x);
+    if (p.tma_store) prefetch_tmap(&tmap_y);
+  }
   __syncthreads();
   // Both CTAs of a pair see the same header, so they leave together.
   if (*bad_flag) return;
@@ -253,12 +262,22 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   conv_done:;
   } else if (warp < C::kEpiWarp0 + C::kEpiWarps) {
     // -------------------------------------------------------------- epilogue
+    // Each half (4 warps, one per TMEM lane quarter) handles half of the BN
+    // activation rows, 32 at a time. With TMA stores, a chunk is written to a
+    // shared-memory buffer laid out as the output tile and stored by one thread;
+    // the accumulator is released as soon as it has been read, so the global
+    // writes drain while the next tile is being multiplied.
     const int q = warp & 3;                        // TMEM lane quarter
     const int half = (warp - C::kEpiWarp0) >> 2;  // which half of the BN columns
     const int r = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const bool elected = q == 0 && lane == 0;      // issues this half's TMA stores
+    const bool glu = p.epi == PQ8_EPI_GLU;
+    const int box_cols = glu ? 64 : 128;           // output columns of one tile
+    const int c_local = glu ? q * 16 + (lane & 15) : r;
     constexpr int E = C::kEpiCols;
     constexpr int kChunks = BN / E / 2;            // E-column chunks per half
+    int chunk_seq = 0;                             // chunks issued by this half (selects the buffer)
     int local = 0;
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
       const int n_tile = (tile / p.m_tiles) * C::kCtas + static_cast<int>(rank), m_tile = tile % p.m_tiles;
@@ -268,17 +287,16 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       RowMap rm;
       const bool valid = map_row(p.layout, p.n, n_tile * kTileRows + r, rm);
       const float b = (p.bias != nullptr && valid) ? p.bias[rm.src] : 0.0f;
-      const bool store_lane = valid && (p.epi != PQ8_EPI_GLU || lane < 16);
+      const bool store_lane = valid && (!glu || lane < 16);
       float* ycol = p.y + rm.col;
       const float* rcol = p.resid + rm.col;
 #pragma unroll 1
-      for (int cc = 0; cc < kChunks; ++cc) {
+      for (int cc = 0; cc < kChunks; ++cc, ++chunk_seq) {
         const int c = half * kChunks + cc;
         const int m0 = m_tile * BN + c * E;
         if (m0 >= p.m) break;
         uint32_t v[E];
-        if constexpr (E == 32) tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
-        else tmem_ld16(tmem + lane_base + acc * BN + c * E, v);
+        tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
         tmem_wait_ld();
         const int cnt = min(E, p.m - m0);  // warp-uniform
         float out[E];
@@ -288,7 +306,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
             out[j] = (store_lane && j < cnt) ? rcol[(size_t)(m0 + j) * p.out_cols] : 0.0f;
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = fmaf(p.alpha, __uint_as_float(v[j]) + b, out[j]);
-        } else if (p.epi == PQ8_EPI_GLU) {
+        } else if (glu) {
 #pragma unroll
           for (int j = 0; j < E; ++j) {
             const float z = __uint_as_float(v[j]) + b;
@@ -309,7 +327,23 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = tf32_round(out[j]);
         }
-        if (store_lane) {
+        if (p.tma_store) {
+          float* stage = out_stage + (half * 2 + (chunk_seq & 1)) * C::kOutChunkFloats;
+          // the store issued from this buffer two chunks ago must have read it
+          if (elected) bulk_wait_group_read<1>();
+          named_barrier_sync(1 + half, 128);
+          if (!glu || lane < 16) {
+#pragma unroll
+            for (int j = 0; j < E; ++j) stage[j * box_cols + c_local] = out[j];
+          }
+          fence_proxy_async_smem();
+          named_barrier_sync(1 + half, 128);
+          // rows past M and columns past the output width are clipped by the TMA unit
+          if (elected) {
+            tma_store_2d(&tmap_y, stage, n_tile * box_cols, m0);
+            bulk_commit_group();
+          }
+        } else if (store_lane) {
           float* yp = ycol + (size_t)m0 * p.out_cols;
 #pragma unroll
           for (int j = 0; j < E; ++j)
@@ -320,6 +354,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       if (PAIR && !leader) mbar_arrive_cluster(acc_empty_remote + acc * 8);
       else mbar_arrive(&acc_empty[acc]);
     }
+    if (p.tma_store && elected) bulk_wait_group_all();
   } else if (warp == C::kTmaWarp) {
     // -------------------------------------------------------------- producer
     if (lane == 0) {
