@@ -95,9 +95,26 @@ def tf32_round(a) -> np.ndarray:
     return r.view(np.float32)
 
 
+def tf32_round_even(a) -> np.ndarray:
+    """Round float32 values to TF32, nearest, ties to even.
+
+    This is how the tensor-core GEMM rounds the expanded weights: it forms
+    ``q * scale`` as an fp16 product (11 significant bits, IEEE
+    round-to-nearest-even), which is exactly TF32 precision whenever the
+    product is a normal fp16 number, and rounds the rare rows whose scale
+    falls outside that range to nearest-even in fp32 arithmetic.
+    """
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    finite = (u & 0x7F800000) != 0x7F800000
+    r = np.where(finite, (u + 0xFFF + ((u >> 13) & 1)) & 0xFFFFE000, u).astype(np.uint32)
+    return r.view(np.float32)
+
+
 def gemm_tf32(x, raw, n: int, k: int) -> np.ndarray:
-    """Float64 product of TF32-rounded operands (both X and the expanded W)."""
-    w = tf32_round(dequant_f32(raw, n, k)).astype(np.float64)
+    """Float64 product of TF32-rounded operands: the expanded W rounded to
+    nearest-even (``tf32_round_even``), X to nearest with ties away
+    (``tf32_round``, the rounding of the activation producers)."""
+    w = tf32_round_even(dequant_f32(raw, n, k)).astype(np.float64)
     return tf32_round(np.asarray(x, np.float32)).astype(np.float64) @ w.T
 
 

@@ -77,9 +77,9 @@ int encode_fn(EncodeTiledFn* fn) {
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // ---------------------------------------------------------------- GEMM
-template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS>
+template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS, int WSTAGES>
 int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaStream_t st) {
-  using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS>;
+  using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES>;
   EncodeTiledFn enc;
   int rc = encode_fn(&enc);
   if (rc) return rc;
@@ -106,7 +106,7 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return PQ8_ERR_DRIVER;
   }
-  auto kernel = gemm_tc_kernel<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS>;
+  auto kernel = gemm_tc_kernel<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES>;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
     if (!ds->attr_set[cfg_id]) {
@@ -141,18 +141,22 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
 enum GemmConfig { kG256 = 0, kG192, kG128, kG64, kP256, kP192, kP128, kNumGemmConfigs };
 struct GemmShape {
   int bn, pair, acc;
+  // Time model, in units of one 32-wide K block of the BN = 192 tile:
+  // a launch takes waves * KB * t + (waves - 1) * e + f, where e is the
+  // epilogue a single accumulator serialises with the next tile and f the
+  // per-launch fixed cost (pipeline fill, last epilogue). Fitted to B200
+  // measurements of the encoder shapes at M = 3000.
+  double t, e, f;
 };
-constexpr GemmShape kGemmShapes[kNumGemmConfigs] = {{256, 0, 1}, {192, 0, 2}, {128, 0, 2}, {64, 0, 2},
-                                                    {256, 1, 1}, {192, 1, 2}, {128, 1, 2}};
+constexpr GemmShape kGemmShapes[kNumGemmConfigs] = {
+    {256, 0, 1, 1.31, 3.6, 20.6}, {192, 0, 2, 1.00, 0.0, 26.4}, {128, 0, 2, 0.86, 0.0, 26.4},
+    {64, 0, 2, 0.80, 0.0, 26.4},  {256, 1, 1, 1.04, 7.3, 29.1}, {192, 1, 2, 1.02, 0.0, 26.4},
+    {128, 1, 2, 0.88, 0.0, 26.4}};
 
-// Fewest estimated cycles: waves x per-tile cost, where a tile costs its MMA
-// work (bn) plus a fixed weight-conversion share. Measured on B200 at
-// M = 3000, CTA pairs run slightly slower per SM than single CTAs (their
-// cross-CTA handoffs add latency while shared-memory traffic is not the
-// limit), hence their small penalty.
+// The configuration with the least modelled time is chosen.
 // PQ8_GEMM_CONFIG=<index> or PQ8_GEMM_BN=64|128|192|256 (single CTA) in the
 // environment force a configuration; the tests use this to cover all of them.
-int choose_gemm(int m, int n_tiles, int sms) {
+int choose_gemm(int m, int n_tiles, int kb, int sms) {
   if (const char* force = std::getenv("PQ8_GEMM_CONFIG")) {
     const int v = std::atoi(force);
     if (v >= 0 && v < kNumGemmConfigs) return v;
@@ -173,8 +177,7 @@ int choose_gemm(int m, int n_tiles, int sms) {
     const long units = static_cast<long>(g.pair ? (n_tiles + 1) / 2 : n_tiles) * ((m + g.bn - 1) / g.bn);
     const long slots = g.pair ? sms / 2 : sms;
     const long waves = (units + slots - 1) / slots;
-    const double per_tile = (g.bn + 48) * (g.pair ? 1.05 : 1.0);
-    const double cost = waves * per_tile;
+    const double cost = waves * kb * g.t + (waves - 1) * g.e + g.f;
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = c;
@@ -360,14 +363,14 @@ extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bi
   p.n_tiles = (n + kTileRows - 1) / kTileRows;
   p.k_blocks = k / 32;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (choose_gemm(m, p.n_tiles, ds->sms)) {
-    case kG256: return launch_gemm<256, 4, 6, 1, false, 3>(ds, kG256, x, p, st);
-    case kG192: return launch_gemm<192, 5, 4, 2, false, 2>(ds, kG192, x, p, st);
-    case kG128: return launch_gemm<128, 7, 4, 2, false, 2>(ds, kG128, x, p, st);
-    case kG64: return launch_gemm<64, 10, 4, 2, false, 2>(ds, kG64, x, p, st);
-    case kP256: return launch_gemm<256, 7, 4, 1, true, 2>(ds, kP256, x, p, st);
-    case kP192: return launch_gemm<192, 8, 4, 2, true, 2>(ds, kP192, x, p, st);
-    default: return launch_gemm<128, 10, 4, 2, true, 2>(ds, kP128, x, p, st);
+  switch (choose_gemm(m, p.n_tiles, p.k_blocks, ds->sms)) {
+    case kG256: return launch_gemm<256, 4, 4, 1, false, 2, 7>(ds, kG256, x, p, st);
+    case kG192: return launch_gemm<192, 5, 4, 2, false, 2, 8>(ds, kG192, x, p, st);
+    case kG128: return launch_gemm<128, 7, 4, 2, false, 2, 8>(ds, kG128, x, p, st);
+    case kG64: return launch_gemm<64, 10, 4, 2, false, 2, 8>(ds, kG64, x, p, st);
+    case kP256: return launch_gemm<256, 7, 4, 1, true, 2, 8>(ds, kP256, x, p, st);
+    case kP192: return launch_gemm<192, 8, 4, 2, true, 2, 8>(ds, kP192, x, p, st);
+    default: return launch_gemm<128, 10, 4, 2, true, 2, 8>(ds, kP128, x, p, st);
   }
 }
 

@@ -68,6 +68,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of phase `parity` (acquire, CTA scope): lets a thread
+// start the check for its next phase before it needs the answer.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar`. Gives up (returns false) when the CTA's
 // abort flag is raised or after kWaitLimitNs, raising the flag and recording
 // PQ8_ERR_TIMEOUT in the device status word.
@@ -121,6 +135,20 @@ __device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.b
 // Barrier over `count` threads (a multiple of 32) using hardware barrier `id` (1..15).
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Two-warp rendezvous on named barrier `id` (64 threads) that also ORs one
+// flag across both warps. Both warps must call it the same number of times.
+__device__ __forceinline__ bool rendezvous_or(int id, bool flag) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred q, p;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, 64, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(flag)), "r"(id)
+      : "memory");
+  return out != 0;
 }
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
@@ -203,6 +231,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA
 // with 128-byte swizzling: 8-row x 128-byte swizzle atoms stacked at a
 // 1024-byte stride (SBO), version 1 (sm_100), layout SWIZZLE_128B (2).
+// Commit variants taking the barrier's shared-window address (no conversion
+// per call; used by the MMA warp, whose instruction count is on the critical path).
+__device__ __forceinline__ void mma_commit_addr(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mma_commit_pair_addr(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
          (2ull << 61);
@@ -222,6 +261,10 @@ __device__ __forceinline__ uint32_t tf32_round_bits(uint32_t u) {
   return ((u & 0x7F800000u) == 0x7F800000u) ? u : ((u + 0x1000u) & 0xFFFFE000u);
 }
 __device__ __forceinline__ float tf32_round(float f) { return __uint_as_float(tf32_round_bits(__float_as_uint(f))); }
+// fp32 bits -> TF32 bits, round to nearest, ties to even (finite inputs).
+__device__ __forceinline__ uint32_t tf32_rne_bits(uint32_t u) {
+  return (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+}
 
 // Signed int8 lane `i` (0..3) of a 32-bit word as an exact float: the biased
 // byte (q + 128) is placed in the mantissa of 2^23 and the bias removed.

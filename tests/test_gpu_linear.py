@@ -1,7 +1,8 @@
 """GPU parity of the Q8_0 contraction kernels against the CPU oracle.
 
 Tolerances:
-* GEMM (tensor cores, TF32 operands rounded to nearest)
+* GEMM (tensor cores, TF32 operands rounded to nearest: weights ties-to-even,
+  activations ties-away)
   ``max|y - golden| <= 2e-3 * rms(golden)`` against the float64 golden, and
   ``<= 1e-4 * rms`` against ``oracle.q8.gemm_tf32`` (the same TF32-rounded
   operands summed in float64): what remains is FP32 accumulation order, while
@@ -234,6 +235,49 @@ def test_large_shape_rows_sampled(rt):
     gold = q8.gemm(x[rows], raw, n, k)
     assert q8.max_err_over_rms(y[rows], gold) <= NORTH_STAR
     assert q8.max_err_over_rms(y[rows], q8.gemm_tf32(x[rows], raw, n, k)) <= TF32_EXACT
+
+
+@pytest.mark.parametrize('cfg', CONFIGS)
+def test_gemm_scales_outside_fp16_exact_range(rt, cfg, monkeypatch):
+    """Rows whose fp16 scale is subnormal (< 2^-14) or above 511 take the
+    fp32 expansion path instead of the fp16 product; both must match the
+    TF32 model (weights rounded to nearest-even)."""
+    monkeypatch.setenv('PQ8_GEMM_CONFIG', cfg)
+    rng = np.random.default_rng(41)
+    m, n, k = 96, 256, 256
+    raw = q8_0_blocks(rng, n, k, qmin=-128)
+    scales = raw[:, :2].copy().view('<f2')
+    nb = raw.shape[0]
+    pick = rng.integers(0, 4, nb)
+    scales[pick == 0, 0] = rng.uniform(1e-7, 6e-5, (pick == 0).sum()).astype(np.float16)  # fp16 subnormals
+    scales[pick == 1, 0] = rng.uniform(512.0, 3000.0, (pick == 1).sum()).astype(np.float16)
+    scales[pick == 2, 0] = 0
+    raw[:, :2] = scales.view(np.uint8)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    y = rt.gemm(dev(x), rt.pack(raw, n, k)).cpu().numpy().astype(np.float64)
+    tf = q8.gemm_tf32(x, raw, n, k)
+    assert np.isfinite(y).all()
+    assert float(np.max(np.abs(y - tf))) / q8.rms(tf) <= TF32_EXACT
+
+
+@pytest.mark.parametrize('cfg', ['0', '1', '4'])
+def test_gemm_inplace_rounding_repeatable(rt, cfg, monkeypatch):
+    """Several output tiles per CTA with the activations rounded to TF32 inside
+    the kernel: every launch must equal the launch on pre-rounded activations
+    bit for bit (the same operands in the same order). This catches a weight
+    record or activation stage being refilled while still being read."""
+    monkeypatch.setenv('PQ8_GEMM_CONFIG', cfg)
+    rng = np.random.default_rng(8)
+    m, n, k = 8192, 4096, 1024
+    w = rt.pack(q8_0_blocks(rng, n, k), n, k)
+    x = torch.randn(m, k, device='cuda', generator=torch.Generator(device='cuda').manual_seed(3))
+    xr = x.clone()
+    rt.lib.call('pq8_round_tf32', xr.data_ptr(), xr.numel(), rt.stream())
+    want = rt.gemm(xr, w, flags=pq8.FLAG_X_TF32)
+    for _ in range(12):
+        got = rt.gemm(x, w)
+        assert torch.equal(got, want)
+    assert rt.device_status() == 0
 
 
 def test_status_clean_at_end(rt):

@@ -121,6 +121,13 @@ def test_tf32_rounding_model():
     assert r[3] == np.float32(-(1.0 + 2 * 2**-10))
     assert np.isinf(r[4]) and np.isinf(r[5])
     assert np.all((r[:4].view(np.uint32) & 0x1FFF) == 0)
+    e = q8.tf32_round_even(np.array([1.0 + 2**-11, 1.0 + 3 * 2**-11, -(1.0 + 3 * 2**-11), 1.0 + 2**-11 + 2**-20,
+                                     np.inf], np.float32))
+    assert e[0] == 1.0                               # tie rounds to the even neighbour (down)
+    assert e[1] == np.float32(1.0 + 2 * 2**-10)      # tie rounds to the even neighbour (up)
+    assert e[2] == np.float32(-(1.0 + 2 * 2**-10))
+    assert e[3] == np.float32(1.0 + 2**-10)          # above the tie rounds up
+    assert np.isinf(e[4])
     # TF32-RN on both operands meets the north-star tolerance on config 0 shapes
     rng = np.random.default_rng(0)
     raw = q8_0_blocks(rng, 512, 1024)
