@@ -136,6 +136,14 @@ __device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.b
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// running; griddep_wait blocks until that kernel has completed and its memory
+// is visible (a no-op without the launch attribute). griddep_launch lets the
+// next kernel start launching as soon as every CTA of this one has called it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Two-warp rendezvous on named barrier `id` (64 threads) that also ORs one
 // flag across both warps. Both warps must call it the same number of times.
 __device__ __forceinline__ bool rendezvous_or(int id, bool flag) {

@@ -214,6 +214,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   int* bad_flag = reinterpret_cast<int*>(smem + C::kMiscOff + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The next kernel may launch now: its CTAs take SMs as this grid's CTAs
+  // exit, set up and fetch and convert their (constant) weights, and wait for
+  // this grid before touching activations or outputs.
+  griddep_launch();
   const uint32_t rank = PAIR ? cluster_rank() : 0;  // 0 = leader (issues the MMAs)
   const bool leader = rank == 0;
   const int unit0 = blockIdx.x / C::kCtas;          // first work unit of this CTA (pair)
@@ -404,6 +408,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     constexpr int kChunks = BN / E / 2;            // E-column chunks per half
     int chunk_seq = 0;                             // chunks issued by this half (selects the buffer)
     int local = 0;
+    griddep_wait();  // the residual and the output may be in use by the previous kernel
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
       const int n_tile = (tile / p.m_tiles) * C::kCtas + static_cast<int>(rank), m_tile = tile % p.m_tiles;
       const int acc = local % ACC;
@@ -483,6 +488,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   } else if (warp == C::kTmaWarp) {
     // ----------------------------------------------------- activation producer
     if (lane == 0) {
+      griddep_wait();  // the activations may come from the previous kernel
       uint32_t issued = 0;
       Ring<STAGES> xr;
       for (int tile = unit0; tile < num_tiles; tile += unit_stride) {
