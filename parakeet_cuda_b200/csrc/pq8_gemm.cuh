@@ -565,7 +565,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         }
       }
     }
-  } else {
+  } else if (warp == C::kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     // Whole warp: meets the scheduler once per RK K blocks; lane 0 issues.
     // The operands advance incrementally (descriptor start address, slot
