@@ -185,6 +185,29 @@ PQ8_API int pq8_joint_argmax(const void* w, const float* enc, const int* enc_row
 PQ8_API int pq8_tdt_commit(float* h, float* c, const float* h_new, const float* c_new, const int* mask, int m,
                            int layers, int hidden, void* stream);
 
+/* One step of the greedy TDT loop for m <= 1024 streams, on the device. It
+ * has no counterpart in the reference, whose loop runs on the host
+ * (decoder.py:78-97) and reads the joint's ids back every step; here a decode
+ * step is a fixed launch sequence (pq8_lstm_layer x2 + pq8_gemv, then
+ * pq8_joint_argmax, pq8_tdt_control, pq8_tdt_commit) that a CUDA graph can
+ * replay, with the host polling *remaining now and then.
+ * ids: int[m][2] from pq8_joint_argmax (token, duration index); durations:
+ * int[n_durations] (model metadata asr.tdt.durations); state: int[m][8] =
+ * {frames, t, symbols, previous token, emitted, joint calls, done, 0}, set by
+ * the caller to {frames_i, 0, 0, 8192, 0, 0, frames_i == 0, 0} before the
+ * first step. Applies the reference's rules (blank 8192; blank with duration 0
+ * advances one frame; at most 10 symbols per frame) to the streams not done,
+ * then writes the next step's inputs: tokens[i] (predictor input = last
+ * emitted token), enc_rows[i] = i * enc_stride + min(t, frames - 1) (row of
+ * the next joint call), commit_mask[i] (1 when this step emitted), and
+ * *remaining (streams not done). Per joint call it appends {t, token, skip}
+ * to trace[i][trace_capacity][3], per emitted token {token, t, skip} to
+ * emitted[i][emitted_capacity][3]; a full buffer records PQ8_ERR_WORKSPACE in
+ * the device status word instead of writing past it. */
+PQ8_API int pq8_tdt_control(const int* ids, const int* durations, int n_durations, int* state, int m,
+                            int enc_stride, int* tokens, int* enc_rows, int* commit_mask, int* emitted,
+                            int emitted_capacity, int* trace, int trace_capacity, int* remaining, void* stream);
+
 /* pq8_gemv without a workspace argument, for callers that cannot allocate
  * device memory: a host that keeps all device memory in its own pre-reserved
  * pool, or a latency-critical loop where cudaMalloc would synchronize the

@@ -12,6 +12,7 @@
 #include "pq8_device.cuh"
 #include "pq8_gemm.cuh"
 #include "pq8_gemv.cuh"
+#include "pq8_tdt.cuh"
 
 namespace pq8 {
 
@@ -512,6 +513,25 @@ extern "C" int pq8_tdt_commit(float* h, float* c, const float* h_new, const floa
   const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * ds->sms);
   tdt_commit_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(h, c, h_new, c_new, mask, m, layers,
                                                                          hidden);
+  return to_code(cudaGetLastError());
+}
+
+extern "C" int pq8_tdt_control(const int* ids, const int* durations, int n_durations, int* state, int m,
+                               int enc_stride, int* tokens, int* enc_rows, int* commit_mask, int* emitted,
+                               int emitted_capacity, int* trace, int trace_capacity, int* remaining, void* stream) {
+  if (m < 1 || m > 1024 || n_durations < 1 || enc_stride < 0 || emitted_capacity < 0 || trace_capacity < 0)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (ids == nullptr || durations == nullptr || state == nullptr || tokens == nullptr || enc_rows == nullptr ||
+      commit_mask == nullptr || remaining == nullptr || (emitted_capacity > 0 && emitted == nullptr) ||
+      (trace_capacity > 0 && trace == nullptr))
+    return PQ8_ERR_INVALID_ARGUMENT;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  const int threads = (m + 31) / 32 * 32;
+  tdt_control_kernel<<<1, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, durations, n_durations, state, m, enc_stride, tokens, enc_rows, commit_mask, emitted, emitted_capacity,
+      trace, trace_capacity, remaining, ds->status);
   return to_code(cudaGetLastError());
 }
 

@@ -1,0 +1,91 @@
+// Greedy TDT control on the device: one thread per stream applies the result
+// of one joint call (token, duration index) exactly as the reference's host
+// loop does (parakeet_cuda/decoder.py:78-97):
+//   * a blank with duration 0 advances one frame;
+//   * a non-blank token is emitted, becomes the predictor's next input, and
+//     its candidate LSTM state is committed;
+//   * at most kMaxSymbols joint calls per frame: the 10th call without a frame
+//     advance moves on by one frame.
+// It then prepares the next step (predictor input, encoder row of the next
+// joint call, commit mask) so that a decode step is a fixed sequence of
+// launches (predict, joint, control, commit) that can be captured in a CUDA
+// graph and replayed without the host reading anything per step.
+#pragma once
+
+#include "pq8_device.cuh"
+
+namespace pq8 {
+
+constexpr int kTdtBlank = 8192;
+constexpr int kTdtMaxSymbols = 10;
+// Per-stream state words (int[m][kTdtStateWords]).
+enum TdtState { kTdtFrames = 0, kTdtT, kTdtSymbols, kTdtPrevious, kTdtEmitted, kTdtCalls, kTdtDone, kTdtStateWords = 8 };
+
+// One block; m <= blockDim.x.
+__global__ void tdt_control_kernel(const int* __restrict__ ids, const int* __restrict__ durations, int n_durations,
+                                   int* __restrict__ state, int m, int enc_stride, int* __restrict__ tokens,
+                                   int* __restrict__ enc_rows, int* __restrict__ commit_mask,
+                                   int* __restrict__ emitted, int emitted_capacity, int* __restrict__ trace,
+                                   int trace_capacity, int* __restrict__ remaining, int* status) {
+  const int i = threadIdx.x;
+  bool live = false;
+  if (i < m) {
+    int* s = state + i * kTdtStateWords;
+    const int frames = s[kTdtFrames];
+    int t = s[kTdtT], symbols = s[kTdtSymbols], previous = s[kTdtPrevious];
+    int n_emitted = s[kTdtEmitted], n_calls = s[kTdtCalls], done = s[kTdtDone];
+    int commit = 0;
+    if (!done) {
+      const int token = ids[2 * i];
+      const int d = ids[2 * i + 1];
+      int skip = (d >= 0 && d < n_durations) ? durations[d] : 0;
+      if (d < 0 || d >= n_durations) atomicCAS(status, 0, PQ8_ERR_INVALID_ARGUMENT);
+      if (token == kTdtBlank && skip == 0) skip = 1;
+      if (n_calls < trace_capacity) {
+        int* tr = trace + (static_cast<size_t>(i) * trace_capacity + n_calls) * 3;
+        tr[0] = t;
+        tr[1] = token;
+        tr[2] = skip;
+      } else {
+        atomicCAS(status, 0, PQ8_ERR_WORKSPACE);
+      }
+      ++n_calls;
+      if (token != kTdtBlank) {
+        commit = 1;
+        if (n_emitted < emitted_capacity) {
+          int* em = emitted + (static_cast<size_t>(i) * emitted_capacity + n_emitted) * 3;
+          em[0] = token;
+          em[1] = t;
+          em[2] = skip;
+        } else {
+          atomicCAS(status, 0, PQ8_ERR_WORKSPACE);
+        }
+        ++n_emitted;
+        previous = token;
+      }
+      ++symbols;
+      t += skip;
+      if (skip) {
+        symbols = 0;
+      } else if (symbols == kTdtMaxSymbols) {
+        ++t;
+        symbols = 0;
+      }
+      done = t >= frames;
+      s[kTdtT] = t;
+      s[kTdtSymbols] = symbols;
+      s[kTdtPrevious] = previous;
+      s[kTdtEmitted] = n_emitted;
+      s[kTdtCalls] = n_calls;
+      s[kTdtDone] = done;
+    }
+    commit_mask[i] = commit;
+    tokens[i] = previous;
+    enc_rows[i] = i * enc_stride + (frames > 0 ? min(t, frames - 1) : 0);
+    live = !done;
+  }
+  const int n_live = __syncthreads_count(live);
+  if (threadIdx.x == 0) *remaining = n_live;
+}
+
+}  // namespace pq8

@@ -103,7 +103,8 @@ class PQ8Decoder:
         """Token/duration ids of all rows into ``self.ids`` (device); ``enc`` rows selected by ``enc_rows``."""
         rows = None
         if enc_rows is not None:
-            self.enc_rows.copy_(enc_rows, non_blocking=True)
+            if enc_rows.data_ptr() != self.enc_rows.data_ptr():  # a device loop writes self.enc_rows itself
+                self.enc_rows.copy_(enc_rows, non_blocking=True)
             rows = self.enc_rows.data_ptr()
         ws = self.rt.workspace
         st = self.rt.stream()
@@ -119,10 +120,16 @@ class PQ8Decoder:
 
     def commit_rows(self, mask: torch.Tensor):
         """Rows with ``mask != 0`` adopt their candidate state."""
-        self.commit_mask.copy_(mask, non_blocking=True)
+        if mask.data_ptr() != self.commit_mask.data_ptr():  # a device loop writes self.commit_mask itself
+            self.commit_mask.copy_(mask, non_blocking=True)
         self.rt.lib.call('pq8_tdt_commit', self.h.data_ptr(), self.c.data_ptr(), self.hn.data_ptr(),
                          self.cn.data_ptr(), self.commit_mask.data_ptr(), self.batch, LAYERS, HIDDEN,
                          self.rt.stream())
+
+    def reset_state(self):
+        """Zero the LSTM state of every row (a fresh decode)."""
+        for t in (self.h, self.c, self.hn, self.cn, self.pred):
+            t.zero_()
 
     def read_ids(self) -> np.ndarray:
         self.ids_host.copy_(self.ids, non_blocking=True)

@@ -11,6 +11,12 @@ after an emitted token; an emitted token commits the candidate LSTM state.
 per step for all streams, one predict for all streams whenever any stream
 needs it (a stream whose inputs did not change gets bit-identical candidates
 again, so this is equivalent to predicting it alone), and a masked commit.
+``greedy_decode_device`` runs the same loop without the host: the control
+rules run in a kernel (``pq8_tdt_control``), so a step is a fixed launch
+sequence (predict, joint, control, commit) replayed from a CUDA graph of
+several steps, and the host only polls how many streams remain between
+replays. It predicts every step: a stream that emitted nothing recomputes
+bit-identical candidates, so the results equal ``greedy_decode_batch``'s.
 """
 from __future__ import annotations
 
@@ -118,3 +124,86 @@ def greedy_decode_batch(projected, decoder, durations, max_steps: int | None = N
             decoder.commit_rows(mask_h)
         steps += 1
     return [s.result() for s in streams]
+
+
+def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 16,
+                         max_steps: int | None = None) -> list:
+    """B streams (``projected[b]`` = frames of stream b, [T_b, 640]) on a batched PQ8Decoder,
+    with the greedy control on the device; same results as ``greedy_decode_batch``."""
+    b = decoder.batch
+    if len(projected) != b:
+        raise ValueError(f'decoder has {b} rows, got {len(projected)} streams')
+    rt, dev = decoder.rt, decoder.rt.device
+    frames = [len(p) for p in projected]
+    t_max = max(max(frames), 1)
+    table = np.zeros((b * t_max, projected[0].shape[1]), np.float32)
+    for i, p in enumerate(projected):
+        table[i * t_max:i * t_max + len(p)] = p
+    enc = torch.from_numpy(table).to(dev)
+    cap = t_max * MAX_SYMBOLS  # a frame takes at most MAX_SYMBOLS joint calls
+    i32 = dict(dtype=torch.int32, device=dev)
+    state = torch.zeros(b, 8, dtype=torch.int32)
+    state[:, 0] = torch.tensor(frames, dtype=torch.int32)
+    state[:, 3] = BLANK
+    state[:, 6] = (state[:, 0] == 0).to(torch.int32)
+    state = state.to(dev)
+    dur = torch.tensor(list(durations), **i32)
+    emitted = torch.zeros(b, cap, 3, **i32)
+    trace = torch.zeros(b, cap, 3, **i32)
+    remaining = torch.zeros(1, **i32)
+    decoder.reset_state()
+    decoder.tokens.fill_(BLANK)
+    decoder.enc_rows.copy_(torch.arange(b, dtype=torch.int32) * t_max)
+    lib = rt.lib
+
+    def step():
+        decoder.predict_device()
+        decoder.joint_device(enc, decoder.enc_rows)
+        lib.call('pq8_tdt_control', decoder.ids.data_ptr(), dur.data_ptr(), dur.numel(), state.data_ptr(), b,
+                 t_max, decoder.tokens.data_ptr(), decoder.enc_rows.data_ptr(), decoder.commit_mask.data_ptr(),
+                 emitted.data_ptr(), cap, trace.data_ptr(), cap, remaining.data_ptr(), rt.stream())
+        decoder.commit_rows(decoder.commit_mask)
+
+    # Kernel attributes and workspaces are set up outside the capture: this
+    # predict/joint pair computes exactly what the first step will compute.
+    decoder.predict_device()
+    decoder.joint_device(enc, decoder.enc_rows)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(steps_per_graph):
+                step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    steps = 0
+    limit = max_steps if max_steps is not None else None
+    while limit is None or steps < limit:
+        if limit is not None and limit - steps < steps_per_graph:
+            for _ in range(limit - steps):
+                step()
+            steps = limit
+        else:
+            graph.replay()
+            steps += steps_per_graph
+        if int(remaining.item()) == 0 and steps > 0:
+            break
+    torch.cuda.synchronize(dev)
+    del graph
+    decoder.steps = steps
+    status = rt.device_status()
+    if status:
+        raise RuntimeError(f'device status {status} after the device TDT loop')
+    st, em, tr = state.cpu().numpy(), emitted.cpu().numpy(), trace.cpu().numpy()
+    out = []
+    for i in range(b):
+        ne, nc = int(st[i, 4]), int(st[i, 5])
+        out.append({
+            'tokens': [int(v) for v in em[i, :ne, 0]],
+            'token_times': [[int(e[1]) * FRAME_SECONDS, (int(e[1]) + max(1, int(e[2]))) * FRAME_SECONDS]
+                            for e in em[i, :ne]],
+            'decode_trace': [[int(v) for v in r] for r in tr[i, :nc]],
+            'joint_calls': nc,
+        })
+    return out

@@ -11,7 +11,7 @@ from parakeet_cuda_b200 import pq8
 from parakeet_cuda_b200.decoder import PQ8Decoder
 from parakeet_cuda_b200.runtime import Runtime, pack_concat_host
 from parakeet_cuda_b200.synthetic import SyntheticParakeet, q8_0_blocks
-from parakeet_cuda_b200.tdt import greedy_decode, greedy_decode_batch
+from parakeet_cuda_b200.tdt import greedy_decode, greedy_decode_batch, greedy_decode_device
 
 pytestmark = pytest.mark.gpu
 
@@ -146,6 +146,51 @@ def test_tdt_1000_steps_matches_oracle(rt):
     assert got["joint_calls"] >= 1000
     assert got['tokens'] == ref['tokens']
     assert got['decode_trace'] == ref['decode_trace']
+
+
+def test_tdt_device_loop_matches_reference_golden(rt, golden_dir):
+    """The device-resident loop (control kernel + graph replay) on the
+    reference's own decodes: blanks, zero durations and the 10-symbol cap."""
+    meta = json.loads((golden_dir / 'golden_meta.json').read_text())
+    data = np.load(golden_dir / 'tdt_decode.npz')
+    for case in meta['tdt_random']:
+        seed = case['seed']
+        model = SyntheticParakeet(seed=seed, encoder_layers=0, blank_bias=case['blank_bias'],
+                                  duration0_bias=case['duration0_bias'])
+        [r] = greedy_decode_device([data[f'seed{seed}_projected']], PQ8Decoder(model, rt, batch=1), DURATIONS,
+                                   steps_per_graph=4)
+        np.testing.assert_array_equal(np.asarray(r['tokens'], np.int32), data[f'seed{seed}_tokens'])
+        np.testing.assert_array_equal(np.asarray(r['decode_trace'], np.int32).reshape(-1, 3),
+                                      data[f'seed{seed}_trace'])
+        assert r['joint_calls'] == case['joint_calls']
+
+
+@pytest.mark.parametrize('batch', [1, 4, 13, 64])
+def test_tdt_device_loop_matches_host_loop(rt, batch):
+    """Streams of different lengths (and one empty) through the device loop and
+    the host loop: identical tokens, times and per-call traces."""
+    model = SyntheticParakeet(seed=12, encoder_layers=0, blank_bias=1.0)
+    rng = np.random.default_rng(70 + batch)
+    lengths = [int(rng.integers(5, 60)) for _ in range(batch)]
+    if batch > 1:
+        lengths[1] = 0
+    projected = [rng.normal(size=(n, 640)).astype(np.float32) for n in lengths]
+    want = greedy_decode_batch([p if len(p) else np.zeros((0, 640), np.float32) for p in projected],
+                               PQ8Decoder(model, rt, batch=batch), DURATIONS)
+    got = greedy_decode_device(projected, PQ8Decoder(model, rt, batch=batch), DURATIONS, steps_per_graph=8)
+    for g, w in zip(got, want):
+        assert g == w
+
+
+def test_tdt_device_loop_step_limit(rt):
+    """max_steps stops the loop after exactly that many lock-step steps."""
+    model = SyntheticParakeet(seed=11, encoder_layers=0)
+    projected = [np.random.default_rng(5).normal(size=(200, 640)).astype(np.float32)]
+    d = PQ8Decoder(model, rt, batch=1)
+    [r] = greedy_decode_device(projected, d, DURATIONS, steps_per_graph=16, max_steps=37)
+    assert d.steps == 37 and r['joint_calls'] == 37
+    ref = otdt.greedy_decode(projected[0], otdt.Decoder64(model), DURATIONS)
+    assert r['decode_trace'] == ref['decode_trace'][:37]
 
 
 def test_status_clean(rt):
