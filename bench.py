@@ -421,7 +421,7 @@ def tdt_measure(torch, rt):
     from parakeet_cuda_b200.decoder import PQ8Decoder
     from parakeet_cuda_b200.pq8 import EPI_NONE
     from parakeet_cuda_b200.synthetic import SyntheticParakeet
-    from parakeet_cuda_b200.tdt import greedy_decode_batch
+    from parakeet_cuda_b200.tdt import greedy_decode_batch, greedy_decode_device
     model = SyntheticParakeet(seed=11, encoder_layers=0)
     rt.load_weights(model, ['joint.enc.weight', 'joint.enc.bias'])
     w_enc, b_enc = rt.weight('joint.enc.weight'), rt.weight('joint.enc.bias').reshape(-1)
@@ -444,7 +444,20 @@ def tdt_measure(torch, rt):
         out[f'batch{batch}'] = {'lockstep_steps': steps, 'joint_calls': calls,
                                 'tokens': sum(len(r['tokens']) for r in res), 'predict_launches': dec.predict_calls,
                                 'seconds': t_dec, 'steps_per_s': steps / t_dec, 'joint_calls_per_s': calls / t_dec,
-                                'projection_ms': t_proj * 1e3}
+                                'projection_ms': t_proj * 1e3, 'loop': 'host (reads ids every step)'}
+        # the same decode with the control on the device (graph of 16 steps, host polls between replays)
+        ddev = PQ8Decoder(model, rt, batch=batch)
+        greedy_decode_device([s[:20] for s in streams], ddev, model.metadata['asr.tdt.durations'])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res_dev = greedy_decode_device(streams, ddev, model.metadata['asr.tdt.durations'])
+        t_dev = time.perf_counter() - t0
+        out[f'batch{batch}_device_loop'] = {
+            'lockstep_steps': ddev.steps, 'joint_calls': sum(r['joint_calls'] for r in res_dev),
+            'seconds': t_dev, 'steps_per_s': ddev.steps / t_dev,
+            'joint_calls_per_s': sum(r['joint_calls'] for r in res_dev) / t_dev,
+            'same_result_as_host_loop': res_dev == res,
+            'loop': 'device (pq8_tdt_control; CUDA graph of 16 steps, host polls the remaining count)'}
     return out
 
 

@@ -239,12 +239,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       mbar_init(&wempty[s], GROUP_WARPS);
     }
     for (int a = 0; a < ASLOTS; ++a) {
-      mbar_init(&conv[a], C::kGroupThreads * C::kCtas);
+      mbar_init(&conv[a], GROUP_WARPS * C::kCtas);  // one arrival per converter warp
       mbar_init(&afree[a], 1);
     }
     for (int a = 0; a < ACC; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], C::kEpiWarps * 32 * C::kCtas);
+      mbar_init(&acc_empty[a], C::kEpiWarps * C::kCtas);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -385,8 +385,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       w_ready = mbar_test_wait(smem_addr(&wfull[wr.idx]), wr.phase);
       tmem_wait_st();
       tc_fence_before();
-      if (PAIR && !leader) mbar_arrive_cluster(conv_remote + slot * 8);
-      else mbar_arrive(&conv[slot]);
+      // every lane's tensor-memory stores are complete and fenced: one arrival per warp
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR && !leader) mbar_arrive_cluster(conv_remote + slot * 8);
+        else mbar_arrive(&conv[slot]);
+      }
     }
   conv_done:;
   } else if (warp >= C::kEpiWarp0) {
@@ -481,8 +485,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         }
       }
       tc_fence_before();
-      if (PAIR && !leader) mbar_arrive_cluster(acc_empty_remote + acc * 8);
-      else mbar_arrive(&acc_empty[acc]);
+      __syncwarp();  // every lane's accumulator loads are complete: one arrival per warp
+      if (lane == 0) {
+        if (PAIR && !leader) mbar_arrive_cluster(acc_empty_remote + acc * 8);
+        else mbar_arrive(&acc_empty[acc]);
+      }
     }
     if (p.tma_store && elected) bulk_wait_group_all();
   } else if (warp == C::kTmaWarp) {
