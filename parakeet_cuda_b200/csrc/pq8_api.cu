@@ -195,6 +195,7 @@ int choose_gemm(int m, int n_tiles, int kb, int sms) {
 // ---------------------------------------------------------------- GEMV
 struct GemvPlan {
   int mt, splits, kbps;
+  bool stream;  // weights brought in by bulk copies (HBM regime: few rows, long K range per CTA)
   size_t off_tickets, off_done, off_bval, off_bidx, off_partial, total;
 };
 
@@ -205,11 +206,25 @@ GemvPlan plan_gemv(int m, int n, int k, int sms) {
   g.mt = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
   const int n_tiles = (n + kTileRows - 1) / kTileRows;
   const int kb = k / 32;
-  int splits = std::max(1, std::min(kb, (2 * sms + n_tiles - 1) / n_tiles));
-  int kbps = (kb + splits - 1) / splits;
   const int max_kbps = kGemvXSmemFloats / (32 * g.mt);
-  if (kbps > max_kbps) kbps = max_kbps;
-  splits = (kb + kbps - 1) / kbps;
+  int splits = 0, kbps = 0;
+  if (g.mt == 1) {
+    // One wave of two streaming CTAs per SM, if that leaves every CTA a long
+    // run of K blocks to stream (measured: worth it for one row; with two the
+    // per-CTA arithmetic, not the bytes in flight, sets the pace).
+    int s = std::max(1, (2 * sms) / n_tiles);
+    int b = std::min((kb + s - 1) / s, max_kbps);
+    if (b >= 8) {
+      g.stream = true;
+      kbps = b;
+      splits = (kb + b - 1) / b;
+    }
+  }
+  if (!g.stream) {
+    splits = std::max(1, std::min(kb, (2 * sms + n_tiles - 1) / n_tiles));
+    kbps = std::min((kb + splits - 1) / splits, max_kbps);
+    splits = (kb + kbps - 1) / kbps;
+  }
   g.splits = splits;
   g.kbps = kbps;
   size_t off = 0;
@@ -241,12 +256,29 @@ int launch_gemv(DeviceState* ds, GemvParams p, void* ws, size_t ws_bytes, cudaSt
   p.partial = reinterpret_cast<float*>(base + g.off_partial);
   p.status = ds->status;
   const int grid = p.n_tiles * g.splits;
-  const size_t smem = sizeof(float) * g.mt * g.kbps * 32;
+  size_t smem = sizeof(float) * g.mt * g.kbps * 32;
+  if (g.stream) {
+    smem = ((smem + 127) & ~size_t(127)) + kStreamRingBytes;
+    auto kernel = g.mt == 1 ? gemv_kernel<1, true> : gemv_kernel<2, true>;
+    const int attr_id = g.mt == 1 ? 14 : 15;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      if (!ds->attr_set[attr_id]) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(sizeof(float) * 2 * kGemvXSmemFloats + 128 +
+                                                              kStreamRingBytes));
+        if (e != cudaSuccess) return to_code(e);
+        ds->attr_set[attr_id] = true;
+      }
+    }
+    kernel<<<grid, kStreamThreads, smem, st>>>(p);
+    return to_code(cudaGetLastError());
+  }
   switch (g.mt) {
-    case 1: gemv_kernel<1><<<grid, kGemvThreads, smem, st>>>(p); break;
-    case 2: gemv_kernel<2><<<grid, kGemvThreads, smem, st>>>(p); break;
-    case 4: gemv_kernel<4><<<grid, kGemvThreads, smem, st>>>(p); break;
-    default: gemv_kernel<8><<<grid, kGemvThreads, smem, st>>>(p); break;
+    case 1: gemv_kernel<1, false><<<grid, kGemvThreads, smem, st>>>(p); break;
+    case 2: gemv_kernel<2, false><<<grid, kGemvThreads, smem, st>>>(p); break;
+    case 4: gemv_kernel<4, false><<<grid, kGemvThreads, smem, st>>>(p); break;
+    default: gemv_kernel<8, false><<<grid, kGemvThreads, smem, st>>>(p); break;
   }
   return to_code(cudaGetLastError());
 }

@@ -103,6 +103,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait used on the teardown path: ignores the abort flag.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_addr(bar);
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(a, parity)) {
+    if (global_timer_ns() - t0 > kWaitLimitNs) return;
+  }
+}
+
+// Position in a ring of SIZE buffers and the parity of the pass over it,
+// advanced without divisions (the roles' loops run on issue-starved warps,
+// where a division by a non-power-of-two constant is a long dependent chain).
+template <int SIZE>
+struct Ring {
+  uint32_t idx = 0, phase = 0;
+  __device__ __forceinline__ void advance(uint32_t n) {  // n <= SIZE
+    idx += n;
+    if (idx >= SIZE) {
+      idx -= SIZE;
+      phase ^= 1u;
+    }
+  }
+};
+
 // ---------------------------------------------------------------------------
 // Bulk / tensor copies (global -> shared, completion counted on an mbarrier)
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -126,31 +126,8 @@ struct GemmCfg {
   static_assert(kConvWarp0 % 4 == 0 && kEpiWarp0 % 4 == 0, "converter and epilogue warps start on lane quarter 0");
 };
 
-// Bounded wait used on the teardown path: ignores the abort flag.
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = smem_addr(bar);
-  const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(a, parity)) {
-    if (global_timer_ns() - t0 > kWaitLimitNs) return;
-  }
-}
-
 __device__ __forceinline__ float silu_fast(float z) { return __fdividef(z, 1.0f + __expf(-z)); }
 
-// Position in a ring of SIZE buffers and the parity of the pass over it,
-// advanced without divisions (the roles' loops run on issue-starved warps,
-// where a division by a non-power-of-two constant is a long dependent chain).
-template <int SIZE>
-struct Ring {
-  uint32_t idx = 0, phase = 0;
-  __device__ __forceinline__ void advance(uint32_t n) {  // n <= SIZE
-    idx += n;
-    if (idx >= SIZE) {
-      idx -= SIZE;
-      phase ^= 1u;
-    }
-  }
-};
 
 // True when every product q * s (|q| <= 128) of this fp16 scale is zero or a
 // normal fp16 number: s = 0, or 2^-14 <= |s| <= 511 (exponent field 1..23).

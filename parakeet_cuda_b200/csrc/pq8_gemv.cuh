@@ -63,6 +63,15 @@ struct GemvParams {
 
 constexpr int kGemvThreads = 128;
 constexpr int kGemvXSmemFloats = 10240;  // at most 40 KB of staged activations per CTA
+// Streamed weights (HBM regime): a producer warp copies the CTA's records in
+// chunks of kStreamChunk records into a ring of kStreamRing chunks.
+constexpr int kStreamChunk = 4;
+constexpr int kStreamRing = 4;
+constexpr int kStreamRingBytes = kStreamRing * kStreamChunk * kRecordBytes;
+// Streaming CTAs run two groups of 128 compute threads (alternate records of
+// each chunk, combined before the epilogue) and one producer warp.
+constexpr int kStreamCompute = 2 * kGemvThreads;
+constexpr int kStreamThreads = kStreamCompute + 32;
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   uint4 v;
@@ -103,42 +112,89 @@ __device__ __forceinline__ void argmax_merge(float& v, int& i, float ov, int oi)
 }
 
 // acc[m] += scale * sum_j q_j * x[m][j] over one 32-wide K block of this thread's row.
+// Packed f32x2 arithmetic (sm_100): two lanes of FP32 per instruction.
+__device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float f32x2_sum(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+
+// One 32-wide K block of one row against MT activation rows: the codes become
+// floats by placing the biased byte under 2^23 (PRMT) and subtracting
+// 2^23 + 128, two at a time with packed f32x2 adds; the products accumulate
+// in packed f32x2 FMAs (even and odd K positions in the two halves), so the
+// GEMV spends about 2 instructions per weight and row instead of 3. The block
+// sum is scaled once.
 template <int MT>
 __device__ __forceinline__ void gemv_block(const uint4 q0, const uint4 q1, uint16_t scale_bits, const float* xk,
                                            int nk, float (&acc)[MT]) {
   const float sc = __half2float(__ushort_as_half(scale_bits));
   const uint32_t wd[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
                           q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
-  float inner[MT];
+  const uint64_t minus_bias = f32x2_pack(-8388736.0f, -8388736.0f);
+  uint64_t inner[MT];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) inner[m] = 0.0f;
+  for (int m = 0; m < MT; ++m) inner[m] = 0;  // (+0, +0)
 #pragma unroll
   for (int j = 0; j < 32; j += 4) {
-    const float q_0 = i8_to_f32(wd[j >> 2], 0), q_1 = i8_to_f32(wd[j >> 2], 1);
-    const float q_2 = i8_to_f32(wd[j >> 2], 2), q_3 = i8_to_f32(wd[j >> 2], 3);
+    const uint32_t w = wd[j >> 2];
+    const uint64_t q01 = f32x2_add(f32x2_pack(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540)),
+                                              __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541))),
+                                   minus_bias);
+    const uint64_t q23 = f32x2_add(f32x2_pack(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7542)),
+                                              __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7543))),
+                                   minus_bias);
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
       const float4 xv = *reinterpret_cast<const float4*>(xk + m * nk + j);
-      inner[m] = fmaf(q_0, xv.x, inner[m]);
-      inner[m] = fmaf(q_1, xv.y, inner[m]);
-      inner[m] = fmaf(q_2, xv.z, inner[m]);
-      inner[m] = fmaf(q_3, xv.w, inner[m]);
+      inner[m] = f32x2_fma(q01, f32x2_pack(xv.x, xv.y), inner[m]);
+      inner[m] = f32x2_fma(q23, f32x2_pack(xv.z, xv.w), inner[m]);
     }
   }
 #pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = fmaf(sc, inner[m], acc[m]);
+  for (int m = 0; m < MT; ++m) acc[m] = fmaf(sc, f32x2_sum(inner[m]), acc[m]);
 }
 
-// Dynamic shared memory: the staged activations of this CTA's K range
-// (MT x kb_per_split x 32 floats), sized per launch so that small rows leave
-// room for more resident CTAs, i.e. more loads in flight per SM.
-template <int MT>
-__global__ void __launch_bounds__(kGemvThreads, MT <= 2 ? 8 : 4) gemv_kernel(const GemvParams p) {
-  extern __shared__ __align__(16) float xs[];
+// Barrier among the 128 compute threads (named barrier 1 when the producer
+// warp of the streaming variant has left).
+template <bool STREAM>
+__device__ __forceinline__ void compute_sync() {
+  if constexpr (STREAM) named_barrier_sync(1, kGemvThreads);
+  else __syncthreads();
+}
+
+// STREAM: the weight records are brought in by bulk copies from a producer
+// warp (tens of KB in flight per CTA without holding them in registers, which
+// is what HBM streaming at M = 1 needs), and two groups of 128 threads
+// consume alternate records of each chunk; otherwise each thread loads its
+// row's bytes itself, U K blocks ahead (small launches where latency matters
+// more than bytes in flight).
+template <int MT, bool STREAM>
+__global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM ? 2 : (MT <= 2 ? 8 : 4))
+    gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) float xs[];
   __shared__ float gate_s[MT][4][32];
   __shared__ float red_v[4][MT][2];
   __shared__ int red_i[4][MT][2];
   __shared__ int ticket_s;
+  __shared__ uint64_t full[kStreamRing], empty[kStreamRing];
+  __shared__ int abort_s;
+  __shared__ float comb[STREAM ? MT : 1][kGemvThreads];  // second group's sums
 
   const int t = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
   const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
@@ -153,17 +209,83 @@ __global__ void __launch_bounds__(kGemvThreads, MT <= 2 ? 8 : 4) gemv_kernel(con
   }
 
   // Stage the activations of this CTA's K range: xs[m * nk + kk].
-  for (int i = r; i < MT * nk; i += kGemvThreads) {
-    const int m = i / nk, kk = i - m * nk;
-    xs[i] = (m < p.m) ? load_x(p, m, kb0 * 32 + kk) : 0.0f;
+  constexpr int kStagers = STREAM ? kStreamCompute : kGemvThreads;
+  if (r < kStagers)
+    for (int i = r; i < MT * nk; i += kStagers) {
+      const int m = i / nk, kk = i - m * nk;
+      xs[i] = (m < p.m) ? load_x(p, m, kb0 * 32 + kk) : 0.0f;
+    }
+  const uint8_t* tile_base = p.w + PQ8_HEADER_BYTES + (size_t)t * p.k_blocks * kRecordBytes;
+  const int nrec = kb1 - kb0;
+  const int chunks = (nrec + kStreamChunk - 1) / kStreamChunk;
+  uint8_t* ring = reinterpret_cast<uint8_t*>(xs) + ((MT * nk * 4 + 127) & ~127);
+  if constexpr (STREAM) {
+    if (r == kStreamCompute) {
+      for (int i = 0; i < kStreamRing; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], kStreamCompute / 32);  // one arrival per compute warp
+      }
+      abort_s = 0;
+      fence_mbar_init();
+    }
   }
   __syncthreads();
+
+  if constexpr (STREAM) {
+    if (r >= kStreamCompute) {
+      // ------------------------------------------------ producer warp
+      if (lane == 0) {
+        Ring<kStreamRing> pr;
+        int issued = 0;
+        for (int j = 0; j < chunks; ++j, pr.advance(1)) {
+          if (!mbar_wait(&empty[pr.idx], pr.phase ^ 1u, &abort_s, p.status)) break;
+          const int n_in = min(kStreamChunk, nrec - j * kStreamChunk);
+          const uint32_t bytes = static_cast<uint32_t>(n_in * kRecordBytes);
+          mbar_expect_tx(&full[pr.idx], bytes);
+          bulk_g2s(ring + pr.idx * (kStreamChunk * kRecordBytes),
+                   tile_base + (size_t)(kb0 + j * kStreamChunk) * kRecordBytes, bytes, &full[pr.idx]);
+          ++issued;
+        }
+        // Never leave the CTA with copies still landing in its shared memory.
+        for (int j = issued > kStreamRing ? issued - kStreamRing : 0; j < issued; ++j)
+          mbar_drain(&full[j % kStreamRing], (j / kStreamRing) & 1);
+      }
+      return;  // the compute warps synchronise among themselves from here on
+    }
+  }
 
   float acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
 
-  const uint8_t* tile_base = p.w + PQ8_HEADER_BYTES + (size_t)t * p.k_blocks * kRecordBytes;
+  if constexpr (STREAM) {
+    const int row = r & (kGemvThreads - 1), grp = r / kGemvThreads;  // group 1 takes the odd records
+    Ring<kStreamRing> cr;
+    for (int j = 0; j < chunks; ++j, cr.advance(1)) {
+      if (!mbar_wait(&full[cr.idx], cr.phase, &abort_s, p.status)) break;
+      const uint8_t* cs = ring + cr.idx * (kStreamChunk * kRecordBytes);
+      const int n_in = min(kStreamChunk, nrec - j * kStreamChunk);
+      for (int u = grp; u < n_in; u += 2) {
+        const uint8_t* rec = cs + u * kRecordBytes;
+        gemv_block<MT>(*reinterpret_cast<const uint4*>(rec + row * 16),
+                       *reinterpret_cast<const uint4*>(rec + 2048 + row * 16),
+                       *reinterpret_cast<const uint16_t*>(rec + kScaleOffset + row * 2),
+                       xs + (j * kStreamChunk + u) * 32, nk, acc);
+      }
+      // the chunk's values have been consumed by this warp's arithmetic
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[cr.idx]);
+    }
+    // Second group hands its sums to the first, which runs the epilogue.
+    if (grp == 1) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) comb[m][row] = acc[m];
+    }
+    named_barrier_sync(2, kStreamCompute);
+    if (grp == 1) return;
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] += comb[m][row];
+  } else {
   // Loads for U consecutive K blocks are issued before any of them is used, so
   // each thread keeps U x 34 bytes of weights in flight.
   constexpr int U = MT <= 2 ? 4 : 2;
@@ -186,15 +308,16 @@ __global__ void __launch_bounds__(kGemvThreads, MT <= 2 ? 8 : 4) gemv_kernel(con
     gemv_block<MT>(ldg_stream(rec + r * 16), ldg_stream(rec + 2048 + r * 16), ldg_u16(rec + kScaleOffset + r * 2),
                    xs + (kb - kb0) * 32, nk, acc);
   }
+  }
 
   if (p.splits > 1) {
     float* mine = p.partial + (((size_t)t * p.splits + split) * kGemvThreads + r) * MT;
 #pragma unroll
     for (int m = 0; m < MT; ++m) __stcg(mine + m, acc[m]);
     __threadfence();
-    __syncthreads();
+    compute_sync<STREAM>();
     if (r == 0) ticket_s = atomicAdd(&p.tickets[t], 1);
-    __syncthreads();
+    compute_sync<STREAM>();
     if (ticket_s != p.splits - 1) return;
     __threadfence();
 #pragma unroll
@@ -234,7 +357,7 @@ __global__ void __launch_bounds__(kGemvThreads, MT <= 2 ? 8 : 4) gemv_kernel(con
     // Tile row r holds gate (r / 32) of hidden unit t*32 + r%32.
 #pragma unroll
     for (int m = 0; m < MT; ++m) gate_s[m][warp][lane] = acc[m] + b;
-    __syncthreads();
+    compute_sync<STREAM>();
     if (warp == 0) {
       const int u = t * 32 + lane;
       if (u < p.hidden) {
@@ -282,7 +405,7 @@ __global__ void __launch_bounds__(kGemvThreads, MT <= 2 ? 8 : 4) gemv_kernel(con
         red_i[warp][m][part] = i;
       }
     }
-  __syncthreads();
+  compute_sync<STREAM>();
   if (r < MT * 2) {
     const int m = r >> 1, part = r & 1;
     float v = red_v[0][m][part];
@@ -292,9 +415,9 @@ __global__ void __launch_bounds__(kGemvThreads, MT <= 2 ? 8 : 4) gemv_kernel(con
     __stcg(p.best_idx + ((size_t)t * MT + m) * 2 + part, i);
   }
   __threadfence();
-  __syncthreads();
+  compute_sync<STREAM>();
   if (r == 0) ticket_s = atomicAdd(p.done_count, 1);
-  __syncthreads();
+  compute_sync<STREAM>();
   if (ticket_s != p.n_tiles - 1) return;
   __threadfence();
   if (r < MT * 2) {

@@ -280,6 +280,25 @@ def test_gemm_inplace_rounding_repeatable(rt, cfg, monkeypatch):
     assert rt.device_status() == 0
 
 
+@pytest.mark.parametrize('m', [1, 2])
+@pytest.mark.parametrize('n,k', [(8192, 2080), (16384, 4096)])
+def test_gemv_streamed_weights_match_oracle(rt, m, n, k):
+    """Shapes where each CTA streams a long run of K blocks (the HBM regime):
+    the weights come in by bulk copies into a shared-memory ring. (8192, 2080)
+    ends on a partial chunk and splits K unevenly."""
+    rng = np.random.default_rng(n + k + m)
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    resid = rng.normal(size=(m, n)).astype(np.float32)
+    y, xd, bd = dev(resid), dev(x), dev(bias)  # keep the device copies alive across the launch
+    rt.linear(xd, w, out=y, bias=bd, resid=y, epilogue=EPI_RESIDUAL, alpha=0.5)
+    gold = resid + 0.5 * (q8.gemm(x, raw, n, k) + bias)
+    np.testing.assert_allclose(y.cpu().numpy(), gold, atol=2e-4, rtol=2e-4)
+    assert rt.device_status() == 0
+
+
 def test_status_clean_at_end(rt):
     torch.cuda.synchronize()
     assert rt.device_status() == 0
