@@ -50,6 +50,8 @@ def parse():
     ap.add_argument('--layers', type=int, default=24)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
+    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep',
+                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep)')
     return ap.parse_args()
 
 
@@ -284,10 +286,15 @@ def run_gpu(args):
 
     extras = {}
     if not args.no_extras:
-        extras['gemv'] = gemv_measure(torch, rt, stack)
-        extras['tf32_cublas_tflops'] = cublas_tf32(torch)
-        extras['tdt'] = tdt_measure(torch, rt)
-        extras['sweep'] = sweep_measure(torch, rt)
+        wanted = set(args.extras.split(','))
+        if 'gemv' in wanted:
+            extras['gemv'] = gemv_measure(torch, rt, stack)
+        if 'cublas' in wanted:
+            extras['tf32_cublas_tflops'] = cublas_tf32(torch)
+        if 'tdt' in wanted:
+            extras['tdt'] = tdt_measure(torch, rt)
+        if 'sweep' in wanted:
+            extras['sweep'] = sweep_measure(torch, rt)
     sched.barrier()
 
     if sched.rank == 0:
