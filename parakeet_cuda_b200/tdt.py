@@ -169,13 +169,18 @@ def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 1
     decoder.predict_device()
     decoder.joint_device(enc, decoder.enc_rows)
     torch.cuda.synchronize(dev)
+    # capture_begin/end rather than the torch.cuda.graph context, which also
+    # runs a garbage collection and empties the allocator cache on entry.
     graph = torch.cuda.CUDAGraph()
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
-        with torch.cuda.graph(graph, stream=side):
+        graph.capture_begin()
+        try:
             for _ in range(steps_per_graph):
                 step()
+        finally:
+            graph.capture_end()
     torch.cuda.current_stream(dev).wait_stream(side)
     steps = 0
     limit = max_steps if max_steps is not None else None
