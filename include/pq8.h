@@ -78,7 +78,8 @@ extern "C" {
 #define PQ8_HEADER_BYTES 256
 #define PQ8_TILE_ROWS 128
 #define PQ8_RECORD_BYTES 4352 /* 128 rows x 32 int8 + 128 fp16 scales */
-#define PQ8_GEMV_MAX_M 8      /* pq8_gemv handles m <= 8; pq8_linear sends larger m to pq8_gemm */
+#define PQ8_GEMV_MAX_M 64        /* the GEMV entry points (pq8_gemv, pq8_lstm_layer, pq8_joint_argmax) take m <= 64 */
+#define PQ8_LINEAR_GEMV_MAX_M 8  /* pq8_linear sends m <= 8 to pq8_gemv, larger m to pq8_gemm */
 
 /* Name of an error code (static string; never NULL). */
 PQ8_API const char* pq8_error_string(int code);
@@ -133,11 +134,15 @@ PQ8_API int pq8_gemm(const void* w, const float* x, float* y, const float* bias,
              int m, int n, int k, int epilogue, float alpha, int flags, void* stream);
 
 /* Workspace bytes needed by pq8_gemv / pq8_lstm_layer / pq8_joint_argmax for
- * this shape on the current device. */
+ * this shape on the current device. Every workspace starts with a fixed 64 KiB
+ * counter area; shapes whose split-K tiles need more counters than it holds
+ * (over 16,320 tile x row-group pairs with K split) return
+ * PQ8_ERR_UNSUPPORTED_SHAPE. */
 PQ8_API int pq8_gemv_workspace_size(int m, int n, int k, size_t* bytes);
 
 /* Zero a workspace before its first use (its counters reset themselves
- * after every call, so this is needed once per buffer). */
+ * after every call, so this is needed once per buffer; one buffer serves calls
+ * of any shape it is large enough for). */
 PQ8_API int pq8_workspace_init(void* workspace, size_t bytes, void* stream);
 
 /* HBM-streaming GEMV for the decoder regime, 1 <= m <= PQ8_GEMV_MAX_M:
@@ -149,7 +154,7 @@ PQ8_API int pq8_gemv(const void* w, const float* x, float* y, const float* bias,
              int m, int n, int k, int epilogue, float alpha, void* workspace, size_t workspace_bytes,
              void* stream);
 
-/* Dispatch by m: pq8_gemv for m <= PQ8_GEMV_MAX_M (needs the workspace),
+/* Dispatch by m: pq8_gemv for m <= PQ8_LINEAR_GEMV_MAX_M (needs the workspace),
  * otherwise pq8_gemm. The drop-in for Blas.linear (gpu.py:87-90). */
 PQ8_API int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid,
                int m, int n, int k, int epilogue, float alpha, int flags, void* workspace,

@@ -142,6 +142,25 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   return to_code(cudaGetLastError());
 }
 
+// Launch with programmatic dependent launch allowed: the kernel may start
+// while the previous kernel in the stream finishes (it calls griddep_wait
+// before reading that kernel's results).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // GEMM configurations: activation rows per tile (the MMA N), single CTA or a
 // pair of CTAs sharing one MMA, accumulator buffers.
 enum GemmConfig { kG256 = 0, kG192, kG128, kG64, kP256, kP192, kP128, kNumGemmConfigs };
@@ -193,10 +212,29 @@ int choose_gemm(int m, int n_tiles, int kb, int sms) {
 }
 
 // ---------------------------------------------------------------- GEMV
+// Workspace layout. The counters (split-K tickets, joint completion counts,
+// joint arg-max keys) live in a fixed area at the start that no plan uses for
+// anything else: they reset themselves after every launch, so a workspace
+// zeroed once stays valid across calls of any shape. (If the counters followed
+// each plan's own data regions, a plan with more tiles would find its tickets
+// on bytes an earlier plan had left its partial sums in.) Tickets fill the
+// area from the start; then come the arg-max keys (row groups x 8 rows x 2
+// parts) and, in the last 256 bytes, one completion counter per row group.
+constexpr size_t kGemvCounterBytes = size_t(64) << 10;
+constexpr size_t kGemvDoneOffset = kGemvCounterBytes - 256;
+constexpr size_t kGemvKeyOffset = kGemvDoneOffset - 1024;
+constexpr int kGemvMaxTickets = static_cast<int>(kGemvKeyOffset / sizeof(int));
+static_assert((PQ8_GEMV_MAX_M + 7) / 8 * sizeof(int) <= kGemvCounterBytes - kGemvDoneOffset,
+              "one completion counter per row group");
+static_assert((PQ8_GEMV_MAX_M + 7) / 8 * 8 * 2 * sizeof(unsigned long long) <= kGemvDoneOffset - kGemvKeyOffset,
+              "arg-max keys of every row group");
+
 struct GemvPlan {
-  int mt, splits, kbps;
-  bool stream;  // weights brought in by bulk copies (HBM regime: few rows, long K range per CTA)
-  size_t off_tickets, off_done, off_bval, off_bidx, off_partial, total;
+  bool ok;                       // false: more split tiles than the counter area holds
+  int mt, groups, splits, kbps;  // rows per CTA, row groups (grid y), K splits, K blocks per split
+  bool stream;   // weights brought in by bulk copies (HBM regime: few rows, long K range per CTA)
+  bool cluster;  // the K splits of a tile reduce through a thread-block cluster's shared memory
+  size_t off_tickets, off_done, off_keys, off_partial, total;
 };
 
 size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -204,7 +242,9 @@ size_t round256(size_t v) { return (v + 255) & ~size_t(255); }
 GemvPlan plan_gemv(int m, int n, int k, int sms) {
   GemvPlan g{};
   g.mt = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+  g.groups = (m + g.mt - 1) / g.mt;
   const int n_tiles = (n + kTileRows - 1) / kTileRows;
+  const int units = n_tiles * g.groups;  // CTAs per K split
   const int kb = k / 32;
   const int max_kbps = kGemvXSmemFloats / (32 * g.mt);
   int splits = 0, kbps = 0;
@@ -221,29 +261,31 @@ GemvPlan plan_gemv(int m, int n, int k, int sms) {
     }
   }
   if (!g.stream) {
-    splits = std::max(1, std::min(kb, (2 * sms + n_tiles - 1) / n_tiles));
-    kbps = std::min((kb + splits - 1) / splits, max_kbps);
+    // Fill the CTA slots of one wave (kGemvCtasPerSm per SM) without a second
+    // wave. Up to kGemvMaxClusterSplits splits reduce inside a cluster; a K
+    // range longer than the activation staging area may need more splits,
+    // which reduce through the workspace.
+    const int want = std::max(1, std::min({kb, (kGemvCtasPerSm * sms) / units, kGemvMaxClusterSplits}));
+    kbps = std::min((kb + want - 1) / want, max_kbps);
     splits = (kb + kbps - 1) / kbps;
+    g.cluster = splits > 1 && splits <= kGemvMaxClusterSplits;
   }
   g.splits = splits;
   g.kbps = kbps;
-  size_t off = 0;
-  g.off_tickets = off;
-  off += round256(sizeof(int) * n_tiles);
-  g.off_done = off;
-  off += 256;
-  g.off_bval = off;
-  off += round256(sizeof(float) * n_tiles * g.mt * 2);
-  g.off_bidx = off;
-  off += round256(sizeof(int) * n_tiles * g.mt * 2);
+  g.ok = splits == 1 || g.cluster || units <= kGemvMaxTickets;
+  g.off_tickets = 0;
+  g.off_done = kGemvDoneOffset;
+  g.off_keys = kGemvKeyOffset;
+  size_t off = kGemvCounterBytes;
   g.off_partial = off;
-  off += (splits > 1) ? round256(sizeof(float) * (size_t)n_tiles * splits * kTileRows * g.mt) : 0;
+  off += (splits > 1 && !g.cluster) ? round256(sizeof(float) * (size_t)units * splits * kTileRows * g.mt) : 0;
   g.total = off;
   return g;
 }
 
 int launch_gemv(DeviceState* ds, GemvParams p, void* ws, size_t ws_bytes, cudaStream_t st) {
   const GemvPlan g = plan_gemv(p.m, p.n, p.k, ds->sms);
+  if (!g.ok) return PQ8_ERR_UNSUPPORTED_SHAPE;
   if (ws == nullptr || ws_bytes < g.total) return PQ8_ERR_WORKSPACE;
   if (!aligned(ws, 256)) return PQ8_ERR_MISALIGNED;
   auto* base = static_cast<unsigned char*>(ws);
@@ -251,11 +293,10 @@ int launch_gemv(DeviceState* ds, GemvParams p, void* ws, size_t ws_bytes, cudaSt
   p.kb_per_split = g.kbps;
   p.tickets = reinterpret_cast<int*>(base + g.off_tickets);
   p.done_count = reinterpret_cast<int*>(base + g.off_done);
-  p.best_val = reinterpret_cast<float*>(base + g.off_bval);
-  p.best_idx = reinterpret_cast<int*>(base + g.off_bidx);
+  p.best_key = reinterpret_cast<unsigned long long*>(base + g.off_keys);
   p.partial = reinterpret_cast<float*>(base + g.off_partial);
   p.status = ds->status;
-  const int grid = p.n_tiles * g.splits;
+  const dim3 grid(p.n_tiles * g.splits, g.groups);
   size_t smem = sizeof(float) * g.mt * g.kbps * 32;
   if (g.stream) {
     smem = ((smem + 127) & ~size_t(127)) + kStreamRingBytes;
@@ -271,15 +312,45 @@ int launch_gemv(DeviceState* ds, GemvParams p, void* ws, size_t ws_bytes, cudaSt
         ds->attr_set[attr_id] = true;
       }
     }
-    kernel<<<grid, kStreamThreads, smem, st>>>(p);
+    cudaError_t e = launch_pdl(kernel, grid, dim3(kStreamThreads), smem, st, p);
+    if (e != cudaSuccess) return to_code(e);
     return to_code(cudaGetLastError());
   }
-  switch (g.mt) {
-    case 1: gemv_kernel<1, false><<<grid, kGemvThreads, smem, st>>>(p); break;
-    case 2: gemv_kernel<2, false><<<grid, kGemvThreads, smem, st>>>(p); break;
-    case 4: gemv_kernel<4, false><<<grid, kGemvThreads, smem, st>>>(p); break;
-    default: gemv_kernel<8, false><<<grid, kGemvThreads, smem, st>>>(p); break;
+  auto kernel = g.mt == 1 ? gemv_kernel<1, false>
+              : g.mt == 2 ? gemv_kernel<2, false>
+              : g.mt == 4 ? gemv_kernel<4, false>
+                          : gemv_kernel<8, false>;
+  const int attr_id = 8 + (g.mt == 1 ? 0 : g.mt == 2 ? 1 : g.mt == 4 ? 2 : 3);
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!ds->attr_set[attr_id]) {
+      // staged activations plus the cluster reduction's partial sums
+      const int max_smem = static_cast<int>(sizeof(float) * kGemvXSmemFloats + 128 +
+                                            sizeof(float) * kGemvMaxClusterSplits * kGemvThreads * g.mt);
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return to_code(e);
+      ds->attr_set[attr_id] = true;
+    }
   }
+  p.cluster_reduce = g.cluster;
+  if (g.cluster) smem = ((smem + 127) & ~size_t(127)) + sizeof(float) * g.splits * kGemvThreads * g.mt;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = g.cluster ? g.splits : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g.cluster ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }
 
@@ -418,7 +489,9 @@ extern "C" int pq8_gemv_workspace_size(int m, int n, int k, size_t* bytes) {
   DeviceState* ds;
   int rc = device_state(&ds);
   if (rc) return rc;
-  *bytes = plan_gemv(m, n, k, ds->sms).total;
+  const GemvPlan g = plan_gemv(m, n, k, ds->sms);
+  if (!g.ok) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  *bytes = g.total;
   return PQ8_OK;
 }
 
@@ -439,6 +512,7 @@ extern "C" int pq8_gemv(const void* w, const float* x, float* y, const float* bi
   p.w = static_cast<const uint8_t*>(w);
   p.x0 = x;
   p.x_mode = kXPlain;
+  p.x_vec4 = aligned(x, 16);
   p.y = y;
   p.bias = bias;
   p.resid = resid;
@@ -458,7 +532,7 @@ extern "C" int pq8_gemv(const void* w, const float* x, float* y, const float* bi
 extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid, int m,
                           int n, int k, int epilogue, float alpha, int flags, void* workspace, size_t workspace_bytes,
                           void* stream) {
-  if (m >= 1 && m <= PQ8_GEMV_MAX_M)
+  if (m >= 1 && m <= PQ8_LINEAR_GEMV_MAX_M)
     return pq8_gemv(w, x, y, bias, resid, m, n, k, epilogue, alpha, workspace, workspace_bytes, stream);
   return pq8_gemm(w, x, y, bias, resid, m, n, k, epilogue, alpha, flags, stream);
 }
@@ -483,6 +557,7 @@ extern "C" int pq8_lstm_layer(const void* w, const float* x, const uint16_t* emb
   p.embed = embed_f16;
   p.tokens = tokens;
   p.x_mode = embed_f16 ? kXEmbedConcat : kXConcat;
+  p.x_vec4 = (embed_f16 ? aligned(embed_f16, 8) : aligned(x, 16)) && aligned(h, 16);
   p.k0 = in_k;
   p.bias = bias;
   p.m = m;
@@ -517,6 +592,7 @@ extern "C" int pq8_joint_argmax(const void* w, const float* enc, const int* enc_
   p.x0_rows = enc_rows;
   p.x1 = pred;
   p.x_mode = kXReluSum;
+  p.x_vec4 = aligned(enc, 16) && aligned(pred, 16);
   p.y = logits;
   p.bias = bias;
   p.m = m;
@@ -543,8 +619,9 @@ extern "C" int pq8_tdt_commit(float* h, float* c, const float* h_new, const floa
   if (rc) return rc;
   const long long total = (long long)layers * m * hidden;
   const int grid = (int)std::min<long long>((total + 255) / 256, 4LL * ds->sms);
-  tdt_commit_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(h, c, h_new, c_new, mask, m, layers,
-                                                                         hidden);
+  cudaError_t e = launch_pdl(tdt_commit_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), h, c,
+                             h_new, c_new, mask, m, layers, hidden);
+  if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }
 
@@ -561,9 +638,10 @@ extern "C" int pq8_tdt_control(const int* ids, const int* durations, int n_durat
   int rc = device_state(&ds);
   if (rc) return rc;
   const int threads = (m + 31) / 32 * 32;
-  tdt_control_kernel<<<1, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      ids, durations, n_durations, state, m, enc_stride, tokens, enc_rows, commit_mask, emitted, emitted_capacity,
-      trace, trace_capacity, remaining, ds->status);
+  cudaError_t e = launch_pdl(tdt_control_kernel, dim3(1), dim3(threads), 0, static_cast<cudaStream_t>(stream), ids,
+                             durations, n_durations, state, m, enc_stride, tokens, enc_rows, commit_mask, emitted,
+                             emitted_capacity, trace, trace_capacity, remaining, ds->status);
+  if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }
 
@@ -637,13 +715,14 @@ extern "C" int pq8_gemv_static(const void* w, const float* x, float* y, const fl
   void* scratch = nullptr;
   if ((rc = static_scratch(&scratch))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The array keeps whatever the previous call left; the tickets must start at zero.
-  cudaError_t e = cudaMemsetAsync(scratch, 0, plan.off_bval, st);
+  // The array keeps whatever the previous call left; the counters must start at zero.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, kGemvCounterBytes, st);
   if (e != cudaSuccess) return to_code(e);
   GemvParams p{};
   p.w = static_cast<const uint8_t*>(w);
   p.x0 = x;
   p.x_mode = kXPlain;
+  p.x_vec4 = aligned(x, 16);
   p.y = y;
   p.bias = bias;
   p.resid = resid;

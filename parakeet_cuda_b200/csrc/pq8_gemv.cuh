@@ -1,4 +1,4 @@
-// Decoder-regime contraction (m <= 8 activation rows): an HBM-streaming,
+// Decoder-regime contraction (m <= 64 activation rows): an HBM-streaming,
 // split-K GEMV over the packed Q8_0 records, with the TDT tails fused.
 //
 // One CTA of 128 threads handles one 128-row weight tile over a range of K
@@ -8,17 +8,31 @@
 // (a warp reads 512 contiguous bytes per instruction). The activations of
 // the CTA's K range are staged once in shared memory and read as broadcasts.
 //
-// When a tile's K range is split over several CTAs, each writes its partial
-// sums to the workspace and the last CTA to arrive (atomic ticket) adds the
-// partials in split order and runs the epilogue, so results do not depend on
-// CTA timing. Tickets reset themselves, so a zeroed workspace stays valid
-// across calls.
+// When a tile's K range is split over S <= 16 CTAs, the splits form one
+// thread-block cluster that reduces and scatters: CTA j finishes the tile
+// rows r with (r % 16) % S == j (so a GLU pair r, r + 16 and the four LSTM
+// gates r % 32 + 32 g of one hidden unit stay together). Every CTA stores each
+// row's partial sums into the shared memory of that row's owner, one cluster
+// barrier publishes them, and each owner adds its rows' partials in split
+// order and runs the epilogue for them. The partial sums thus spread over all
+// SMs of the cluster instead of converging on one. With more splits, each CTA
+// writes its partials to the workspace and the last CTA to arrive (atomic
+// ticket) adds them in split order; tickets reset themselves, so a zeroed
+// workspace stays valid across calls. Either way the result does not depend
+// on CTA timing.
 //
 // Modes: plain linear (bias / ReLU / SiLU / GLU / residual epilogues), one
 // LSTM layer (GATES4 layout: the four gates of 32 hidden units per tile are
 // combined in shared memory and the cell update runs in the epilogue), and
-// the TDT joint (ReLU(enc + pred) staged as the activation; per-tile argmax
-// partials reduced by the last tile to finish).
+// the TDT joint (ReLU(enc + pred) staged as the activation; each CTA folds its
+// rows' arg-max into one 64-bit key per (row, part) with an atomic maximum,
+// which the last CTA to finish decodes).
+//
+// A CTA handles MT <= 8 activation rows; larger m runs ceil(m / 8) row groups
+// as the grid's y dimension of one launch (rows [8y, 8y + 8)), each with its
+// own slice of every workspace region, so that the groups' tiles run
+// concurrently instead of one launch after another. The weights are re-read
+// per group, from L2 for decoder-sized matrices.
 #pragma once
 
 #include <float.h>
@@ -39,6 +53,7 @@ struct GemvParams {
   const int* tokens;
   const int* x0_rows;  // optional row indices into x0 (joint: frame of each stream)
   int x_mode;
+  int x_vec4;  // activation pointers allow 16-byte loads (embedding: 8-byte)
   int k0;  // width of the first segment in concat modes
   float* y;
   const float* bias;
@@ -46,11 +61,11 @@ struct GemvParams {
   float alpha;
   int epi;
   int m, n, k, layout, out_cols, n_tiles, k_blocks, splits, kb_per_split;
-  float* partial;  // [n_tiles][splits][128][MT]
-  int* tickets;    // [n_tiles]
-  int* done_count; // joint: tiles finished
-  float* best_val; // joint: [n_tiles][m][2]
-  int* best_idx;
+  int cluster_reduce;  // the splits of a tile form one thread-block cluster (rank = split)
+  float* partial;  // [row groups][n_tiles][splits][128][MT]
+  int* tickets;    // [row groups][n_tiles]
+  int* done_count; // joint: [row groups] CTAs finished
+  unsigned long long* best_key;  // joint: [row groups][MT][2] arg-max keys (argmax_key)
   const float* c_prev;
   float* h_out;
   float* c_out;
@@ -63,6 +78,8 @@ struct GemvParams {
 
 constexpr int kGemvThreads = 128;
 constexpr int kGemvXSmemFloats = 10240;  // at most 40 KB of staged activations per CTA
+constexpr int kGemvMaxClusterSplits = 16;  // cluster size (non-portable above 8)
+constexpr int kGemvCtasPerSm = 4;          // resident CTAs per SM (launch bounds; 128 registers)
 // Streamed weights (HBM regime): a producer warp copies the CTA's records in
 // chunks of kStreamChunk records into a ring of kStreamRing chunks.
 constexpr int kStreamChunk = 4;
@@ -101,6 +118,43 @@ __device__ __forceinline__ float load_x(const GemvParams& p, int m, int kg) {
     default:
       return p.x0[(size_t)m * p.k + kg];
   }
+}
+
+__device__ __forceinline__ float4 ldg_f4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Four consecutive activation elements (row m, columns kg..kg+3; kg % 4 == 0,
+// so a group never straddles a concat boundary, k0 % 32 == 0). x0_row is the
+// resolved row of x0 (joint: the stream's frame; embedding: the token).
+__device__ __forceinline__ float4 load_x4(const GemvParams& p, int m, int x0_row, int kg) {
+  switch (p.x_mode) {
+    case kXConcat:
+      return kg < p.k0 ? ldg_f4(p.x0 + (size_t)m * p.k0 + kg) : ldg_f4(p.x1 + (size_t)m * (p.k - p.k0) + (kg - p.k0));
+    case kXReluSum: {
+      const float4 a = ldg_f4(p.x0 + (size_t)x0_row * p.k + kg), b = ldg_f4(p.x1 + (size_t)m * p.k + kg);
+      return make_float4(fmaxf(a.x + b.x, 0.0f), fmaxf(a.y + b.y, 0.0f), fmaxf(a.z + b.z, 0.0f),
+                         fmaxf(a.w + b.w, 0.0f));
+    }
+    case kXEmbedConcat: {
+      if (kg >= p.k0) return ldg_f4(p.x1 + (size_t)m * (p.k - p.k0) + (kg - p.k0));
+      const uint2 h = *reinterpret_cast<const uint2*>(p.embed + (size_t)x0_row * p.k0 + kg);
+      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+      return make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+    default:
+      return ldg_f4(p.x0 + (size_t)m * p.k + kg);
+  }
+}
+
+// (value, index) as one 64-bit key whose unsigned order is the arg-max order
+// of argmax_merge: larger value first, then the lower index. -0 counts as +0
+// (they compare equal); a NaN never wins (key 0, as in a strict greater-than
+// scan). The value's bits are mapped to an order-preserving unsigned integer.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  if (v != v) return 0ull;
+  uint32_t b = __float_as_uint(v + 0.0f);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(b) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(i));
 }
 
 // (value, index) arg-max with ties to the lowest index.
@@ -185,8 +239,9 @@ __device__ __forceinline__ void compute_sync() {
 // row's bytes itself, U K blocks ahead (small launches where latency matters
 // more than bytes in flight).
 template <int MT, bool STREAM>
-__global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM ? 2 : (MT <= 2 ? 8 : 4))
+__global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM ? 2 : kGemvCtasPerSm)
     gemv_kernel(const GemvParams p) {
+  static_assert(MT * 2 * 8 <= kGemvThreads, "the joint tail gives 8 threads to each (row, part) pair");
   extern __shared__ __align__(128) float xs[];
   __shared__ float gate_s[MT][4][32];
   __shared__ float red_v[4][MT][2];
@@ -198,27 +253,59 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
 
   const int t = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
   const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
-  const int kb0 = split * p.kb_per_split;
+  // Row group: activation rows [row0, row0 + mg) of the launch's p.m rows.
+  const int row0 = blockIdx.y * MT;
+  const int mg = min(MT, p.m - row0);
+  const size_t grp_sel = blockIdx.y;
+  float* const partial = p.partial + grp_sel * ((size_t)p.n_tiles * p.splits * kGemvThreads * MT);
+  int* const tickets = p.tickets + grp_sel * p.n_tiles;
+  int* const done_count = p.done_count + grp_sel;
+  // Rows this CTA finishes: all, or in a cluster of S splits those with (r % 16) % S == split.
+  const int own_s = (!STREAM && p.cluster_reduce) ? p.splits : 1;
+  const int own_j = own_s > 1 ? split : 0;
+  const bool own = ((r & 15) % own_s) == own_j;
+  unsigned long long* const best_key = p.best_key + grp_sel * (MT * 2);
+  // (the last splits of a power-of-two cluster may have an empty K range)
+  const int kb0 = min(p.k_blocks, split * p.kb_per_split);
   const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
   const int nk = (kb1 - kb0) * 32;
 
-  if (r == 0 && blockIdx.x == 0) {
+  // Programmatic dependent launch: the next kernel in the stream may start its
+  // own weight prefetch now; it waits for this grid before touching anything
+  // this grid writes.
+  griddep_launch();
+  // Cluster split-K stores into the leader's shared memory only once every
+  // CTA of the cluster is known to have started (first barrier phase).
+  if (!STREAM && p.cluster_reduce) cluster_arrive_relaxed();
+  if (r == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
     const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
     if (!(h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout && h->n_tiles == p.n_tiles))
       atomicCAS(p.status, 0, PQ8_ERR_LAYOUT);
   }
-
-  // Stage the activations of this CTA's K range: xs[m * nk + kk].
-  constexpr int kStagers = STREAM ? kStreamCompute : kGemvThreads;
-  if (r < kStagers)
-    for (int i = r; i < MT * nk; i += kStagers) {
-      const int m = i / nk, kk = i - m * nk;
-      xs[i] = (m < p.m) ? load_x(p, m, kb0 * 32 + kk) : 0.0f;
-    }
   const uint8_t* tile_base = p.w + PQ8_HEADER_BYTES + (size_t)t * p.k_blocks * kRecordBytes;
   const int nrec = kb1 - kb0;
   const int chunks = (nrec + kStreamChunk - 1) / kStreamChunk;
   uint8_t* ring = reinterpret_cast<uint8_t*>(xs) + ((MT * nk * 4 + 127) & ~127);
+
+  // Weights do not depend on the previous kernel: their first loads (the first
+  // ring of chunks, or the first U blocks of this thread's row) are issued
+  // before waiting for it, so they overlap its tail.
+  constexpr int U = MT <= 2 ? 4 : 2;                 // K blocks per batch of loads
+  constexpr bool kDoubleBuffer = !STREAM && MT <= 4;  // next batch in flight during the arithmetic
+  uint4 qa[U], qb[U];
+  uint16_t sh[U];
+  auto load_batch = [&](int kb, uint4(&a)[U], uint4(&b)[U], uint16_t(&sc)[U]) {
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (kb + u < kb1) {
+        const uint8_t* rec = tile_base + (size_t)(kb + u) * kRecordBytes;
+        a[u] = ldg_stream(rec + r * 16);
+        b[u] = ldg_stream(rec + 2048 + r * 16);
+        sc[u] = ldg_u16(rec + kScaleOffset + r * 2);
+      }
+  };
+  Ring<kStreamRing> pr;  // producer position (STREAM)
+  int issued = 0;
   if constexpr (STREAM) {
     if (r == kStreamCompute) {
       for (int i = 0; i < kStreamRing; ++i) {
@@ -227,6 +314,60 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
       }
       abort_s = 0;
       fence_mbar_init();
+      // the first ring of chunks needs no free slot
+      for (; issued < min(chunks, kStreamRing); ++issued, pr.advance(1)) {
+        const int n_in = min(kStreamChunk, nrec - issued * kStreamChunk);
+        const uint32_t bytes = static_cast<uint32_t>(n_in * kRecordBytes);
+        mbar_expect_tx(&full[pr.idx], bytes);
+        bulk_g2s(ring + pr.idx * (kStreamChunk * kRecordBytes),
+                 tile_base + (size_t)(kb0 + issued * kStreamChunk) * kRecordBytes, bytes, &full[pr.idx]);
+      }
+    }
+  } else {
+    load_batch(kb0, qa, qb, sh);
+  }
+  griddep_wait();
+
+  // Stage the activations of this CTA's K range: xs[m * nk + kk]. The
+  // indirect rows (joint frame, embedding token) are resolved once; each
+  // thread then keeps kStageUnroll independent 16-byte loads in flight.
+  __shared__ int x0row_s[MT];
+  if (r < MT) {
+    const int row = row0 + r;
+    int v = row;
+    if (r < mg) {
+      if (p.x_mode == kXReluSum && p.x0_rows != nullptr) v = p.x0_rows[row];
+      else if (p.x_mode == kXEmbedConcat) v = p.tokens[row];
+    }
+    x0row_s[r] = v;
+  }
+  __syncthreads();
+  constexpr int kStagers = STREAM ? kStreamCompute : kGemvThreads;
+  if (r < kStagers) {
+    if (p.x_vec4) {
+      constexpr int kStageUnroll = 4;
+      const int nk4 = nk >> 2, n4 = MT * nk4;
+      float4* xs4 = reinterpret_cast<float4*>(xs);
+      for (int i0 = r; i0 < n4; i0 += kStageUnroll * kStagers) {
+        float4 v[kStageUnroll];
+#pragma unroll
+        for (int u = 0; u < kStageUnroll; ++u) {
+          const int i = i0 + u * kStagers;
+          v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          if (i < n4) {
+            const int m = i / nk4, kk = (i - m * nk4) * 4;
+            if (m < mg) v[u] = load_x4(p, row0 + m, x0row_s[m], kb0 * 32 + kk);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kStageUnroll; ++u)
+          if (i0 + u * kStagers < n4) xs4[i0 + u * kStagers] = v[u];
+      }
+    } else {
+      for (int i = r; i < MT * nk; i += kStagers) {
+        const int m = i / nk, kk = i - m * nk;
+        xs[i] = (m < mg) ? load_x(p, row0 + m, kb0 * 32 + kk) : 0.0f;
+      }
     }
   }
   __syncthreads();
@@ -235,16 +376,13 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
     if (r >= kStreamCompute) {
       // ------------------------------------------------ producer warp
       if (lane == 0) {
-        Ring<kStreamRing> pr;
-        int issued = 0;
-        for (int j = 0; j < chunks; ++j, pr.advance(1)) {
+        for (; issued < chunks; ++issued, pr.advance(1)) {
           if (!mbar_wait(&empty[pr.idx], pr.phase ^ 1u, &abort_s, p.status)) break;
-          const int n_in = min(kStreamChunk, nrec - j * kStreamChunk);
+          const int n_in = min(kStreamChunk, nrec - issued * kStreamChunk);
           const uint32_t bytes = static_cast<uint32_t>(n_in * kRecordBytes);
           mbar_expect_tx(&full[pr.idx], bytes);
           bulk_g2s(ring + pr.idx * (kStreamChunk * kRecordBytes),
-                   tile_base + (size_t)(kb0 + j * kStreamChunk) * kRecordBytes, bytes, &full[pr.idx]);
-          ++issued;
+                   tile_base + (size_t)(kb0 + issued * kStreamChunk) * kRecordBytes, bytes, &full[pr.idx]);
         }
         // Never leave the CTA with copies still landing in its shared memory.
         for (int j = issued > kStreamRing ? issued - kStreamRing : 0; j < issued; ++j)
@@ -286,48 +424,76 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[m] += comb[m][row];
   } else {
-  // Loads for U consecutive K blocks are issued before any of them is used, so
-  // each thread keeps U x 34 bytes of weights in flight.
-  constexpr int U = MT <= 2 ? 4 : 2;
-  int kb = kb0;
-  for (; kb + U <= kb1; kb += U) {
-    uint4 qa[U], qb[U];
-    uint16_t sh[U];
+    // Batches of U K blocks (U x 34 bytes of weights per thread in flight);
+    // with double buffering the next batch is requested before this one's
+    // arithmetic. The blocks are summed in K order either way.
+    for (int kb = kb0; kb < kb1; kb += U) {
+      if constexpr (kDoubleBuffer) {
+        uint4 na[U], nb[U];
+        uint16_t nsh[U];
+        if (kb + U < kb1) load_batch(kb + U, na, nb, nsh);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const uint8_t* rec = tile_base + (size_t)(kb + u) * kRecordBytes;
-      qa[u] = ldg_stream(rec + r * 16);
-      qb[u] = ldg_stream(rec + 2048 + r * 16);
-      sh[u] = ldg_u16(rec + kScaleOffset + r * 2);
+        for (int u = 0; u < U; ++u)
+          if (kb + u < kb1) gemv_block<MT>(qa[u], qb[u], sh[u], xs + (kb + u - kb0) * 32, nk, acc);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          qa[u] = na[u];
+          qb[u] = nb[u];
+          sh[u] = nsh[u];
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (kb + u < kb1) gemv_block<MT>(qa[u], qb[u], sh[u], xs + (kb + u - kb0) * 32, nk, acc);
+        if (kb + U < kb1) load_batch(kb + U, qa, qb, sh);
+      }
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) gemv_block<MT>(qa[u], qb[u], sh[u], xs + (kb + u - kb0) * 32, nk, acc);
-  }
-  for (; kb < kb1; ++kb) {
-    const uint8_t* rec = tile_base + (size_t)kb * kRecordBytes;
-    gemv_block<MT>(ldg_stream(rec + r * 16), ldg_stream(rec + 2048 + r * 16), ldg_u16(rec + kScaleOffset + r * 2),
-                   xs + (kb - kb0) * 32, nk, acc);
-  }
   }
 
-  if (p.splits > 1) {
-    float* mine = p.partial + (((size_t)t * p.splits + split) * kGemvThreads + r) * MT;
+  if (!STREAM && p.cluster_reduce) {
+    // part_s[split][r][MT] in the owner's shared memory, after the largest
+    // staged-activation area of the launch.
+    float* part_s = xs + ((MT * p.kb_per_split * 32 + 31) & ~31);
+    const uint32_t dst =
+        map_to_rank(part_s + ((size_t)split * kGemvThreads + r) * MT, static_cast<uint32_t>((r & 15) % own_s));
+    cluster_wait();  // all CTAs of the cluster are running
+    if constexpr (MT == 1) {
+      st_cluster_f32(dst, acc[0]);
+    } else if constexpr (MT == 2) {
+      st_cluster_f32x2(dst, acc[0], acc[1]);
+    } else {
+#pragma unroll
+      for (int m = 0; m < MT; m += 4) st_cluster_f32x4(dst + 16 * (m / 4), acc[m], acc[m + 1], acc[m + 2], acc[m + 3]);
+    }
+    cluster_sync();  // second phase: release the stores / acquire everyone's
+    if (own) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+      for (int s = 0; s < own_s; ++s) {
+        const float* part = part_s + ((size_t)s * kGemvThreads + r) * MT;
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[m] += part[m];
+      }
+    }
+  } else if (p.splits > 1) {
+    float* mine = partial + (((size_t)t * p.splits + split) * kGemvThreads + r) * MT;
 #pragma unroll
     for (int m = 0; m < MT; ++m) __stcg(mine + m, acc[m]);
     __threadfence();
     compute_sync<STREAM>();
-    if (r == 0) ticket_s = atomicAdd(&p.tickets[t], 1);
+    if (r == 0) ticket_s = atomicAdd(&tickets[t], 1);
     compute_sync<STREAM>();
     if (ticket_s != p.splits - 1) return;
     __threadfence();
 #pragma unroll
     for (int m = 0; m < MT; ++m) acc[m] = 0.0f;
+#pragma unroll 4
     for (int s = 0; s < p.splits; ++s) {
-      const float* part = p.partial + (((size_t)t * p.splits + s) * kGemvThreads + r) * MT;
+      const float* part = partial + (((size_t)t * p.splits + s) * kGemvThreads + r) * MT;
 #pragma unroll
       for (int m = 0; m < MT; ++m) acc[m] += __ldcg(part + m);
     }
-    if (r == 0) p.tickets[t] = 0;
+    if (r == 0) tickets[t] = 0;
   }
 
   RowMap rm;
@@ -335,20 +501,29 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
   const float b = (p.bias != nullptr && valid) ? p.bias[rm.src] : 0.0f;
 
   if (p.mode == kGemvLinear) {
+    // The residual rows are all read before any output is written (y may
+    // alias resid), so they cost one memory round trip, not one per row.
+    float res[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      res[m] = (p.epi == PQ8_EPI_RESIDUAL && valid && own && m < mg)
+                   ? p.resid[(size_t)(row0 + m) * p.out_cols + rm.col]
+                   : 0.0f;
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
-      if (m >= p.m) break;
+      if (m >= mg) break;
+      const size_t row = row0 + m;
       const float z = acc[m] + b;
       float out;
       if (p.epi == PQ8_EPI_GLU) {
         const float gate = __shfl_down_sync(0xffffffffu, z, 16);
         out = z * sigmoidf_(gate);
       } else if (p.epi == PQ8_EPI_RESIDUAL) {
-        out = valid ? p.resid[(size_t)m * p.out_cols + rm.col] + p.alpha * z : 0.0f;
+        out = valid ? res[m] + p.alpha * z : 0.0f;
       } else {
         out = apply_act(z, p.epi);
       }
-      if (valid && (p.epi != PQ8_EPI_GLU || lane < 16)) p.y[(size_t)m * p.out_cols + rm.col] = out;
+      if (valid && own && (p.epi != PQ8_EPI_GLU || lane < 16)) p.y[row * p.out_cols + rm.col] = out;
     }
     return;
   }
@@ -358,18 +533,29 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
 #pragma unroll
     for (int m = 0; m < MT; ++m) gate_s[m][warp][lane] = acc[m] + b;
     compute_sync<STREAM>();
-    if (warp == 0) {
-      const int u = t * 32 + lane;
-      if (u < p.hidden) {
-        for (int m = 0; m < p.m && m < MT; ++m) {
-          const float gi = gate_s[m][0][lane], gf = gate_s[m][1][lane];
-          const float gg = gate_s[m][2][lane], go = gate_s[m][3][lane];
-          const float si = 1.0f / (1.0f + expf(-gi)), sf = 1.0f / (1.0f + expf(-gf));
-          const float so = 1.0f / (1.0f + expf(-go));
-          const float c = sf * p.c_prev[(size_t)m * p.hidden + u] + si * tanhf(gg);
-          p.c_out[(size_t)m * p.hidden + u] = c;
-          p.h_out[(size_t)m * p.hidden + u] = so * tanhf(c);
-        }
+    // Cell update: warp w takes rows w, w + 4, ... of the group, lane = hidden
+    // unit; all c_prev values are loaded before any state is written.
+    constexpr int kRowsPerWarp = (MT + 3) / 4;
+    const int u = t * 32 + lane;
+    const bool unit = u < p.hidden && ((lane & 15) % own_s) == own_j;  // this CTA finishes unit u
+    float cp[kRowsPerWarp];
+#pragma unroll
+    for (int j = 0; j < kRowsPerWarp; ++j) {
+      const int m = warp + 4 * j;
+      cp[j] = (m < mg && unit) ? p.c_prev[(size_t)(row0 + m) * p.hidden + u] : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < kRowsPerWarp; ++j) {
+      const int m = warp + 4 * j;
+      if (m < mg && unit) {
+        const size_t row = row0 + m;
+        const float gi = gate_s[m][0][lane], gf = gate_s[m][1][lane];
+        const float gg = gate_s[m][2][lane], go = gate_s[m][3][lane];
+        const float si = 1.0f / (1.0f + expf(-gi)), sf = 1.0f / (1.0f + expf(-gf));
+        const float so = 1.0f / (1.0f + expf(-go));
+        const float c = sf * cp[j] + si * tanhf(gg);
+        p.c_out[row * p.hidden + u] = c;
+        p.h_out[row * p.hidden + u] = so * tanhf(c);
       }
     }
     return;
@@ -381,8 +567,8 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     const float z = acc[m] + b;
-    if (valid && m < p.m) p.y[(size_t)m * p.n + rm.src] = z;
-    const bool tok = valid && rm.src < p.vocab, dur = valid && rm.src >= p.vocab;
+    if (valid && own && m < mg) p.y[(size_t)(row0 + m) * p.n + rm.src] = z;
+    const bool tok = valid && own && rm.src < p.vocab, dur = valid && own && rm.src >= p.vocab;
     bv[m][0] = tok ? z : -INFINITY;
     bi[m][0] = tok ? rm.src : INT_MAX;
     bv[m][1] = dur ? z : -INFINITY;
@@ -411,27 +597,27 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
     float v = red_v[0][m][part];
     int i = red_i[0][m][part];
     for (int w = 1; w < 4; ++w) argmax_merge(v, i, red_v[w][m][part], red_i[w][m][part]);
-    __stcg(p.best_val + ((size_t)t * MT + m) * 2 + part, v);
-    __stcg(p.best_idx + ((size_t)t * MT + m) * 2 + part, i);
+    if (m < mg && i != INT_MAX) atomicMax(best_key + m * 2 + part, argmax_key(v, i));
   }
   __threadfence();
   compute_sync<STREAM>();
-  if (r == 0) ticket_s = atomicAdd(p.done_count, 1);
+  if (r == 0) ticket_s = atomicAdd(done_count, 1);
   compute_sync<STREAM>();
-  if (ticket_s != p.n_tiles - 1) return;
+  const int n_slots = p.n_tiles * own_s;
+  if (ticket_s != n_slots - 1) return;
   __threadfence();
+  // Last CTA of the row group: decode the keys (the atomics resolved in L2)
+  // and reset them for the next call.
   if (r < MT * 2) {
     const int m = r >> 1, part = r & 1;
-    if (m < p.m) {
-      float v = -INFINITY;
-      int i = INT_MAX;
-      for (int tt = 0; tt < p.n_tiles; ++tt)
-        argmax_merge(v, i, __ldcg(p.best_val + ((size_t)tt * MT + m) * 2 + part),
-                     __ldcg(p.best_idx + ((size_t)tt * MT + m) * 2 + part));
-      p.ids[m * 2 + part] = (i == INT_MAX) ? 0 : i - (part ? p.vocab : 0);
+    if (m < mg) {
+      const unsigned long long key = __ldcg(best_key + m * 2 + part);
+      const int i = key ? static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key)) : -1;
+      p.ids[(row0 + m) * 2 + part] = i < 0 ? 0 : i - (part ? p.vocab : 0);
+      best_key[m * 2 + part] = 0ull;
     }
   }
-  if (r == 0) *p.done_count = 0;
+  if (r == 0) *done_count = 0;
 }
 
 // TDT commit: rows whose mask is set take the candidate LSTM state
@@ -439,6 +625,8 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
 __global__ void tdt_commit_kernel(float* __restrict__ h, float* __restrict__ c, const float* __restrict__ hn,
                                   const float* __restrict__ cn, const int* __restrict__ mask, int m, int layers,
                                   int hidden) {
+  griddep_launch();
+  griddep_wait();  // the mask and the candidates come from the kernels before
   const long long total = (long long)layers * m * hidden;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {

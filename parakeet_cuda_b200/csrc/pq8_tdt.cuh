@@ -27,6 +27,8 @@ __global__ void tdt_control_kernel(const int* __restrict__ ids, const int* __res
                                    int* __restrict__ enc_rows, int* __restrict__ commit_mask,
                                    int* __restrict__ emitted, int emitted_capacity, int* __restrict__ trace,
                                    int trace_capacity, int* __restrict__ remaining, int* status) {
+  griddep_launch();
+  griddep_wait();  // the joint's ids and the previous step's state
   const int i = threadIdx.x;
   bool live = false;
   if (i < m) {

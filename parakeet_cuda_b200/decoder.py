@@ -27,15 +27,15 @@ VOCAB = 8193
 
 
 class PQ8Decoder:
-    """Prediction/joint network for ``batch`` streams; launches cover up to 8 streams
-    (``PQ8_GEMV_MAX_M``) each, so larger batches run one launch per group of 8 rows."""
+    """Prediction/joint network for ``batch`` streams. Every launch covers all
+    streams (up to ``PQ8_GEMV_MAX_M``; beyond 8 rows the kernels run their row
+    groups side by side in one grid)."""
 
-    MAX_BATCH = 64
+    MAX_BATCH = GEMV_MAX_M
 
     def __init__(self, model, runtime: Runtime, batch: int = 1):
         if not 1 <= batch <= self.MAX_BATCH:
             raise ValueError(f'batch must be in [1, {self.MAX_BATCH}]')
-        self.groups = [(g0, min(GEMV_MAX_M, batch - g0)) for g0 in range(0, batch, GEMV_MAX_M)]
         self.model, self.rt, self.batch = model, runtime, batch
         dev = runtime.device
         self.lstm = []
@@ -70,11 +70,10 @@ class PQ8Decoder:
         self.commit_mask = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.ids = torch.zeros(batch, 2, dtype=torch.int32, device=dev)
         self.ids_host = torch.zeros(batch, 2, dtype=torch.int32).pin_memory()
-        gm = min(batch, GEMV_MAX_M)
         for l in range(LAYERS):
-            runtime.ensure_workspace(gm, 4 * HIDDEN, self.lstm[l][2] + HIDDEN)
-        runtime.ensure_workspace(gm, self.n_out, HIDDEN)
-        runtime.ensure_workspace(gm, HIDDEN, HIDDEN)
+            runtime.ensure_workspace(batch, 4 * HIDDEN, self.lstm[l][2] + HIDDEN)
+        runtime.ensure_workspace(batch, self.n_out, HIDDEN)
+        runtime.ensure_workspace(batch, HIDDEN, HIDDEN)
         self.predict_calls = self.joint_calls = 0
 
     # -- batched device-side steps ------------------------------------------
@@ -84,19 +83,17 @@ class PQ8Decoder:
             self.tokens.copy_(tokens, non_blocking=True)
         rt, lib, ws = self.rt, self.rt.lib, self.rt.workspace
         st = rt.stream()
-        f4 = 4
-        for g0, m in self.groups:
-            row = g0 * HIDDEN * f4          # byte offset of the group's first row in a [batch, 640] buffer
-            for l, (w, bias, k_in) in enumerate(self.lstm):
-                x = None if l == 0 else self.hn[l - 1].data_ptr() + row
-                embed = self.embed.data_ptr() if l == 0 else None
-                toks = self.tokens.data_ptr() + g0 * 4 if l == 0 else None
-                lib.call('pq8_lstm_layer', w.pointer, x, embed, toks, self.h[l].data_ptr() + row,
-                         self.c[l].data_ptr() + row, bias.data_ptr(), self.hn[l].data_ptr() + row,
-                         self.cn[l].data_ptr() + row, m, HIDDEN, k_in, ws.data_ptr(), ws.numel(), st)
-            lib.call('pq8_gemv', self.w_pred.pointer, self.hn[LAYERS - 1].data_ptr() + row,
-                     self.pred.data_ptr() + row, self.b_pred.data_ptr(), None, m, self.w_pred.n, self.w_pred.k,
-                     EPI_NONE, 1.0, ws.data_ptr(), ws.numel(), st)
+        m = self.batch
+        for l, (w, bias, k_in) in enumerate(self.lstm):
+            x = None if l == 0 else self.hn[l - 1].data_ptr()
+            embed = self.embed.data_ptr() if l == 0 else None
+            toks = self.tokens.data_ptr() if l == 0 else None
+            lib.call('pq8_lstm_layer', w.pointer, x, embed, toks, self.h[l].data_ptr(), self.c[l].data_ptr(),
+                     bias.data_ptr(), self.hn[l].data_ptr(), self.cn[l].data_ptr(), m, HIDDEN, k_in, ws.data_ptr(),
+                     ws.numel(), st)
+        lib.call('pq8_gemv', self.w_pred.pointer, self.hn[LAYERS - 1].data_ptr(), self.pred.data_ptr(),
+                 self.b_pred.data_ptr(), None, m, self.w_pred.n, self.w_pred.k, EPI_NONE, 1.0, ws.data_ptr(),
+                 ws.numel(), st)
         self.predict_calls += 1
 
     def joint_device(self, enc: torch.Tensor, enc_rows: torch.Tensor | None = None):
@@ -107,15 +104,9 @@ class PQ8Decoder:
                 self.enc_rows.copy_(enc_rows, non_blocking=True)
             rows = self.enc_rows.data_ptr()
         ws = self.rt.workspace
-        st = self.rt.stream()
-        for g0, m in self.groups:
-            # without a row map, group g reads enc rows g0.. (enc is [batch, 640])
-            e_ptr = enc.data_ptr() if rows is not None else enc.data_ptr() + g0 * HIDDEN * 4
-            self.rt.lib.call('pq8_joint_argmax', self.w_joint.pointer, e_ptr,
-                             rows + g0 * 4 if rows is not None else None, self.pred.data_ptr() + g0 * HIDDEN * 4,
-                             self.b_joint.data_ptr(), self.logits.data_ptr() + g0 * self.n_out * 4,
-                             self.ids.data_ptr() + g0 * 8, m, self.n_out, self.w_joint.k, VOCAB, ws.data_ptr(),
-                             ws.numel(), st)
+        self.rt.lib.call('pq8_joint_argmax', self.w_joint.pointer, enc.data_ptr(), rows, self.pred.data_ptr(),
+                         self.b_joint.data_ptr(), self.logits.data_ptr(), self.ids.data_ptr(), self.batch,
+                         self.n_out, self.w_joint.k, VOCAB, ws.data_ptr(), ws.numel(), self.rt.stream())
         self.joint_calls += 1
 
     def commit_rows(self, mask: torch.Tensor):

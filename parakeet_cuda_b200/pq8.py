@@ -33,7 +33,8 @@ LAYOUT_ROWS, LAYOUT_GLU, LAYOUT_GATES4 = 0, 1, 2
 EPI_NONE, EPI_RELU, EPI_SILU, EPI_GLU, EPI_RESIDUAL = 0, 1, 2, 3, 4
 FLAG_X_TF32, FLAG_OUT_TF32 = 1, 2
 HEADER_BYTES, TILE_ROWS, RECORD_BYTES = 256, 128, 4352
-GEMV_MAX_M = 8
+GEMV_MAX_M = 64          # rows the GEMV entry points take (row groups of 8 run in one launch)
+LINEAR_GEMV_MAX_M = 8    # pq8_linear's GEMV/GEMM dispatch threshold
 
 _P, _I, _F, _SZ, _LL = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_longlong
 

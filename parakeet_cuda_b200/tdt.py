@@ -21,6 +21,7 @@ bit-identical candidates, so the results equal ``greedy_decode_batch``'s.
 from __future__ import annotations
 
 from dataclasses import dataclass, field
+import time
 
 import numpy as np
 import torch
@@ -128,18 +129,22 @@ def greedy_decode_batch(projected, decoder, durations, max_steps: int | None = N
 
 def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 16,
                          max_steps: int | None = None) -> list:
-    """B streams (``projected[b]`` = frames of stream b, [T_b, 640]) on a batched PQ8Decoder,
-    with the greedy control on the device; same results as ``greedy_decode_batch``."""
+    """B streams (``projected[b]`` = frames of stream b, [T_b, 640], a host array or a
+    device tensor) on a batched PQ8Decoder, with the greedy control on the device;
+    same results as ``greedy_decode_batch``. ``decoder.loop_seconds`` records the
+    wall time of the replay loop alone (first replay to the last poll)."""
     b = decoder.batch
     if len(projected) != b:
         raise ValueError(f'decoder has {b} rows, got {len(projected)} streams')
     rt, dev = decoder.rt, decoder.rt.device
-    frames = [len(p) for p in projected]
+    frames = [int(p.shape[0]) for p in projected]
     t_max = max(max(frames), 1)
-    table = np.zeros((b * t_max, projected[0].shape[1]), np.float32)
+    # frame table [b * t_max, 640] on the device: stream i's frames at rows i * t_max ...
+    enc = torch.zeros(b * t_max, int(projected[0].shape[1]), dtype=torch.float32, device=dev)
     for i, p in enumerate(projected):
-        table[i * t_max:i * t_max + len(p)] = p
-    enc = torch.from_numpy(table).to(dev)
+        if frames[i]:
+            src = p if isinstance(p, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(p, np.float32))
+            enc[i * t_max:i * t_max + frames[i]].copy_(src)
     cap = t_max * MAX_SYMBOLS  # a frame takes at most MAX_SYMBOLS joint calls
     i32 = dict(dtype=torch.int32, device=dev)
     state = torch.zeros(b, 8, dtype=torch.int32)
@@ -182,6 +187,8 @@ def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 1
         finally:
             graph.capture_end()
     torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    t_loop = time.perf_counter()
     steps = 0
     limit = max_steps if max_steps is not None else None
     while limit is None or steps < limit:
@@ -195,20 +202,25 @@ def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 1
         if int(remaining.item()) == 0 and steps > 0:
             break
     torch.cuda.synchronize(dev)
+    decoder.loop_seconds = time.perf_counter() - t_loop
     del graph
     decoder.steps = steps
     status = rt.device_status()
     if status:
         raise RuntimeError(f'device status {status} after the device TDT loop')
-    st, em, tr = state.cpu().numpy(), emitted.cpu().numpy(), trace.cpu().numpy()
+    st = state.cpu().numpy()
+    # only the filled prefix of the per-stream records crosses to the host
+    em = emitted[:, :max(1, int(st[:, 4].max()))].cpu().numpy()
+    tr = trace[:, :max(1, int(st[:, 5].max()))].cpu().numpy()
     out = []
     for i in range(b):
         ne, nc = int(st[i, 4]), int(st[i, 5])
+        t = em[i, :ne, 1].astype(np.float64)
+        span = np.maximum(1, em[i, :ne, 2]).astype(np.float64)
         out.append({
-            'tokens': [int(v) for v in em[i, :ne, 0]],
-            'token_times': [[int(e[1]) * FRAME_SECONDS, (int(e[1]) + max(1, int(e[2]))) * FRAME_SECONDS]
-                            for e in em[i, :ne]],
-            'decode_trace': [[int(v) for v in r] for r in tr[i, :nc]],
+            'tokens': em[i, :ne, 0].tolist(),
+            'token_times': np.stack([t * FRAME_SECONDS, (t + span) * FRAME_SECONDS], axis=1).tolist(),
+            'decode_trace': tr[i, :nc].tolist(),
             'joint_calls': nc,
         })
     return out

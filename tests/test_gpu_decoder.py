@@ -27,7 +27,7 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-@pytest.mark.parametrize('m', [1, 3, 8])
+@pytest.mark.parametrize('m', [1, 3, 8, 19, 64])
 def test_lstm_layer_matches_oracle(rt, m):
     rng = np.random.default_rng(20 + m)
     hid, k_in = 640, 640
@@ -63,7 +63,7 @@ def test_lstm_layer_embedding_input(rt):
         np.testing.assert_allclose(d.pred[1].cpu().numpy(), o.pred, atol=1e-4, rtol=1e-4)
 
 
-@pytest.mark.parametrize('m', [1, 5])
+@pytest.mark.parametrize('m', [1, 5, 12, 64])
 def test_joint_argmax_matches_oracle(rt, m):
     rng = np.random.default_rng(30 + m)
     n, k = 8198, 640
@@ -124,7 +124,7 @@ def test_tdt_decode_matches_reference_golden(rt, golden_dir):
         assert r['joint_calls'] == case['joint_calls']
 
 
-@pytest.mark.parametrize('batch', [1, 4, 8, 13])
+@pytest.mark.parametrize('batch', [1, 4, 8, 13, 40])
 def test_tdt_batched_decode_matches_oracle(rt, batch):
     model = SyntheticParakeet(seed=12, encoder_layers=0, blank_bias=3.0)
     rng = np.random.default_rng(40 + batch)

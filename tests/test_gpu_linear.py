@@ -299,6 +299,53 @@ def test_gemv_streamed_weights_match_oracle(rt, m, n, k):
     assert rt.device_status() == 0
 
 
+@pytest.mark.parametrize('m', [9, 23, 64])
+@pytest.mark.parametrize('epi', [EPI_NONE, EPI_GLU, EPI_RESIDUAL])
+def test_gemv_row_groups_match_oracle(rt, m, epi):
+    """m > 8: one launch runs ceil(m / 8) row groups side by side (grid y),
+    each with its own split-K partials and tickets; called twice to check that
+    every group's tickets reset themselves."""
+    rng = np.random.default_rng(100 + m + epi)
+    n, k = 1280, 640
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
+    out_n = n // 2 if epi == EPI_GLU else n
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    resid = rng.normal(size=(m, out_n)).astype(np.float32)
+    gold = q8.epilogue(q8.gemm(x, raw, n, k), epi, bias, resid, 0.5)
+    rt.ensure_workspace(m, n, k)
+    xd, bd = dev(x), dev(bias)
+    for _ in range(2):
+        y = dev(resid)
+        rt.lib.call('pq8_gemv', w.pointer, xd.data_ptr(), y.data_ptr(), bd.data_ptr(),
+                    y.data_ptr() if epi == EPI_RESIDUAL else None, m, n, k, epi, 0.5, rt.workspace.data_ptr(),
+                    rt.workspace.numel(), rt.stream())
+        np.testing.assert_allclose(y.cpu().numpy(), gold, atol=2e-4 * max(1.0, q8.rms(gold)), rtol=2e-4)
+    assert rt.device_status() == 0
+
+
+def test_workspace_shared_across_shapes(rt):
+    """One workspace for a sequence of shapes: a plan with many split tiles
+    after a plan that left split-K partial sums in the same buffer. The
+    counters live in an area no plan stores data in, so each call starts from
+    zeroed tickets."""
+    rng = np.random.default_rng(77)
+    # the last shape needs more than 16 K splits, which reduce through workspace partials
+    for m, n, k in ((8, 640, 4096), (9, 20000, 2048), (3, 640, 4096), (17, 9000, 1536), (8, 256, 24576)):
+        raw = q8_0_blocks(rng, n, k)
+        w = rt.pack(raw, n, k)
+        x = rng.normal(size=(m, k)).astype(np.float32)
+        rt.ensure_workspace(m, n, k)
+        xd = dev(x)
+        y = torch.empty(m, n, device='cuda')
+        rt.lib.call('pq8_gemv', w.pointer, xd.data_ptr(), y.data_ptr(), None, None, m, n, k, EPI_NONE, 1.0,
+                    rt.workspace.data_ptr(), rt.workspace.numel(), rt.stream())
+        gold = q8.gemm(x, raw, n, k)
+        np.testing.assert_allclose(y.cpu().numpy(), gold, atol=2e-4 * max(1.0, q8.rms(gold)), rtol=2e-4)
+    assert rt.device_status() == 0
+
+
 def test_status_clean_at_end(rt):
     torch.cuda.synchronize()
     assert rt.device_status() == 0

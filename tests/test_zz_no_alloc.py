@@ -47,9 +47,11 @@ def test_static_scratch_rejects_oversized_shape():
     rt = Runtime(0)
     w = torch.zeros(4096, dtype=torch.uint8, device='cuda')
     x = torch.zeros(8, 32, device='cuda')
-    n = 4_300_000  # its counters alone need more than the built-in 4 MiB
-    assert rt.lib.gemv_workspace_size(8, n, 32) > 4 << 20
+    # K longer than 16 splits of the activation staging area: the splits
+    # reduce through workspace partials, 25 MB of them for 313 tiles
+    n, k = 40_000, 25_600
+    assert rt.lib.gemv_workspace_size(8, n, k) > 4 << 20
     with pytest.raises(pq8.PQ8Error) as e:
-        rt.lib.call('pq8_gemv_static', w.data_ptr(), x.data_ptr(), x.data_ptr(), None, None, 8, n, 32, pq8.EPI_NONE,
+        rt.lib.call('pq8_gemv_static', w.data_ptr(), x.data_ptr(), x.data_ptr(), None, None, 8, n, k, pq8.EPI_NONE,
                     1.0, rt.stream())
     assert e.value.code == pq8.ERR_WORKSPACE
