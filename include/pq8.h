@@ -176,7 +176,8 @@ PQ8_API int pq8_lstm_layer(const void* w, const float* x, const uint16_t* embed_
  * then ids[i] = {argmax logits[i][0:vocab), argmax logits[i][vocab:n)} with ties
  * to the lowest index. enc: float[R][k]; row i of the activation uses enc row
  * enc_rows[i] (device int[m]) or, when enc_rows is NULL, row i. pred:
- * float[m][k]; logits: float[m][n]; ids: int[m][2].
+ * float[m][k]; logits: float[m][n], or NULL when only the ids are wanted;
+ * ids: int[m][2].
  * Replaces joint_relu + Blas.linear + bias_act + argmax_tdt (decoder.py:66-72,
  * runtime.cu:164-179). */
 PQ8_API int pq8_joint_argmax(const void* w, const float* enc, const int* enc_rows, const float* pred,

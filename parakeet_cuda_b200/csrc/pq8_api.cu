@@ -580,7 +580,7 @@ extern "C" int pq8_joint_argmax(const void* w, const float* enc, const int* enc_
                                 void* workspace, size_t workspace_bytes, void* stream) {
   if (m < 1 || m > PQ8_GEMV_MAX_M || n < 2 || k <= 0 || k % 32 || vocab < 1 || vocab >= n)
     return PQ8_ERR_UNSUPPORTED_SHAPE;
-  if (w == nullptr || enc == nullptr || pred == nullptr || logits == nullptr || ids == nullptr)
+  if (w == nullptr || enc == nullptr || pred == nullptr || ids == nullptr)
     return PQ8_ERR_INVALID_ARGUMENT;
   if (!aligned(w, 16)) return PQ8_ERR_MISALIGNED;
   DeviceState* ds;

@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     const float z = acc[m] + b;
-    if (valid && own && m < mg) p.y[(size_t)(row0 + m) * p.n + rm.src] = z;
+    if (p.y != nullptr && valid && own && m < mg) p.y[(size_t)(row0 + m) * p.n + rm.src] = z;
     const bool tok = valid && own && rm.src < p.vocab, dur = valid && own && rm.src >= p.vocab;
     bv[m][0] = tok ? z : -INFINITY;
     bi[m][0] = tok ? rm.src : INT_MAX;

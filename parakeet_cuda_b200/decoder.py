@@ -33,7 +33,7 @@ class PQ8Decoder:
 
     MAX_BATCH = GEMV_MAX_M
 
-    def __init__(self, model, runtime: Runtime, batch: int = 1):
+    def __init__(self, model, runtime: Runtime, batch: int = 1, keep_logits: bool = False):
         if not 1 <= batch <= self.MAX_BATCH:
             raise ValueError(f'batch must be in [1, {self.MAX_BATCH}]')
         self.model, self.rt, self.batch = model, runtime, batch
@@ -64,7 +64,8 @@ class PQ8Decoder:
         self.cn = torch.zeros(LAYERS, batch, HIDDEN, **f32)
         self.pred = torch.zeros(batch, HIDDEN, **f32)
         self.enc = torch.zeros(batch, HIDDEN, **f32)
-        self.logits = torch.zeros(batch, self.n_out, **f32)
+        # joint logits are written only on request (the greedy loop needs the ids alone)
+        self.logits = torch.zeros(batch, self.n_out, **f32) if keep_logits else None
         self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.enc_rows = torch.zeros(batch, dtype=torch.int32, device=dev)
         self.commit_mask = torch.zeros(batch, dtype=torch.int32, device=dev)
@@ -105,7 +106,8 @@ class PQ8Decoder:
             rows = self.enc_rows.data_ptr()
         ws = self.rt.workspace
         self.rt.lib.call('pq8_joint_argmax', self.w_joint.pointer, enc.data_ptr(), rows, self.pred.data_ptr(),
-                         self.b_joint.data_ptr(), self.logits.data_ptr(), self.ids.data_ptr(), self.batch,
+                         self.b_joint.data_ptr(), None if self.logits is None else self.logits.data_ptr(),
+                         self.ids.data_ptr(), self.batch,
                          self.n_out, self.w_joint.k, VOCAB, ws.data_ptr(), ws.numel(), self.rt.stream())
         self.joint_calls += 1
 

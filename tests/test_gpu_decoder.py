@@ -88,6 +88,11 @@ def test_joint_argmax_matches_oracle(rt, m):
         got = ids.cpu().numpy()
         for i in range(m):
             assert tuple(got[i]) == otdt.argmax_tdt(gold[i]), (i, otdt.top2_margin(gold[i]))
+    # without a logits buffer: the same ids
+    ids2 = torch.full((m, 2), -1, dtype=torch.int32, device='cuda')
+    rt.lib.call('pq8_joint_argmax', w.pointer, ed.data_ptr(), rd.data_ptr(), pd.data_ptr(), bd.data_ptr(), None,
+                ids2.data_ptr(), m, n, k, 8193, ws.data_ptr(), ws.numel(), rt.stream())
+    np.testing.assert_array_equal(ids2.cpu().numpy(), got)
 
 
 def test_joint_argmax_ties_lowest_index(rt):
