@@ -50,8 +50,8 @@ def parse():
     ap.add_argument('--layers', type=int, default=24)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
-    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep',
-                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep)')
+    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep,load',
+                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep, load)')
     return ap.parse_args()
 
 
@@ -212,8 +212,15 @@ def run_gpu(args):
     torch.cuda.set_device(dev)
     rows = args.windows_per_gpu * WINDOW_FRAMES
     model = SyntheticParakeet(seed=0, encoder_layers=args.layers, decoder=False)
+    for name in model.tensors:  # generate the random GGUF bytes before the upload is timed
+        model.raw(name)
     rt = Runtime(dev)
     stack = EncoderStack(model, rt, rows, layers=args.layers, seed=1 + sched.rank)
+    load = {'device_upload': {'layers': args.layers, 'seconds': stack.load_seconds,
+                              'gguf_bytes': rt.uploader().bytes_uploaded,
+                              'gbs': rt.uploader().bytes_uploaded / stack.load_seconds / 1e9}}
+    if sched.rank == 0 and not args.no_extras and 'load' in args.extras.split(','):
+        load.update(load_measure(torch, rt, model))
     del model
     torch.cuda.synchronize()
 
@@ -295,6 +302,8 @@ def run_gpu(args):
             extras['tdt'] = tdt_measure(torch, rt)
         if 'sweep' in wanted:
             extras['sweep'] = sweep_measure(torch, rt)
+        if 'load' in wanted:
+            extras['weight_load'] = load
     sched.barrier()
 
     if sched.rank == 0:
@@ -471,6 +480,54 @@ def tdt_measure(torch, rt):
             'loop': 'device (pq8_tdt_control; CUDA graph of 16 steps, host polls the remaining count); '
                     'steps_per_s over the replay loop, call_* over the whole call (frame table, graph capture, '
                     'results to host lists)'}
+    return out
+
+
+def load_measure(torch, rt, model):
+    """Weight upload, SURVEY-(f)3: GGUF bytes -> resident packed weights.
+    device_upload (measured by the caller on the full stack): pinned staging,
+    async H2D, repack kernel. Here: the same for 2 layers packed on the host
+    (pq8_pack_q8_0, then the packed bytes copied), the pinned H2D copy rate
+    that bounds the device path, and the repack kernel alone."""
+    import numpy as np
+    from parakeet_cuda_b200.encoder import EncoderStack
+    out = {}
+    layers = min(2, len([n for n in model.tensors if n.endswith('feed_forward1.linear1.weight')]))
+    host = EncoderStack(model, rt, 375, layers=layers, upload='host')
+    nbytes = sum(int(np.asarray(model.raw(n)).size) for n in model.tensors
+                 if n.startswith('encoder.') and any(n.startswith(f'encoder.layers.{l}.') for l in range(layers))
+                 and model.tensors[n].kind == 8)
+    out['host_pack_upload'] = {'layers': layers, 'seconds': host.load_seconds, 'gguf_bytes': nbytes,
+                               'gbs': nbytes / host.load_seconds / 1e9}
+    del host
+    pinned = torch.empty(256 << 20, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(256 << 20, dtype=torch.uint8, device=rt.device)
+    dst.copy_(pinned, non_blocking=True)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(4):
+        dst.copy_(pinned, non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    out['pinned_h2d_gbs'] = 4 * pinned.numel() / (a.elapsed_time(b) / 1e3) / 1e9
+    # the repack kernel alone: FFN up weight (4096 x 1024), device to device
+    n, k = 4096, 1024
+    raw = torch.from_numpy(np.asarray(model.raw('encoder.layers.0.feed_forward1.linear1.weight')).copy()).to(rt.device)
+    packed = torch.empty(rt.lib.packed_size(n, k, 0), dtype=torch.uint8, device=rt.device)
+    for _ in range(3):
+        rt.lib.call('pq8_pack_q8_0_device', raw.data_ptr(), n, k, 0, packed.data_ptr(), rt.stream())
+    torch.cuda.synchronize()
+    reps = 50
+    a.record()
+    for _ in range(reps):
+        rt.lib.call('pq8_pack_q8_0_device', raw.data_ptr(), n, k, 0, packed.data_ptr(), rt.stream())
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / reps
+    moved = raw.numel() + packed.numel()
+    out['repack_kernel'] = {'shape': [n, k], 'us': us, 'bytes_moved': moved, 'gbs': moved / us / 1e3,
+                            'note': 'reads the 34-byte blocks, writes the 4352-byte records; L2-resident at this size'}
     return out
 
 

@@ -111,6 +111,19 @@ PQ8_API int pq8_pack_q8_0_part(const void* gguf_blocks, int n, int k_src, int k_
 
 /* ---- device kernels ------------------------------------------------------ */
 
+/* pq8_pack_q8_0 / pq8_pack_q8_0_part on the device: gguf_blocks are the
+ * GGUF bytes already copied to the device (2-byte aligned), packed a device
+ * buffer of pq8_packed_size() bytes (16-byte aligned). Same bytes as the host
+ * packer once every K part has been written: the k_offset == 0 call writes
+ * the header, each call writes all 128 rows (zeros for padding rows) of its
+ * K blocks. A later part whose header does not match records PQ8_ERR_LAYOUT
+ * in the device status word (pq8_device_status). Replaces the per-layer
+ * upload + dequant_q8 of GPU.load_weights (gpu.py:169-184): the raw bytes are
+ * copied once and repacked in HBM. */
+PQ8_API int pq8_pack_q8_0_device(const void* gguf_blocks, int n, int k, int layout, void* packed, void* stream);
+PQ8_API int pq8_pack_q8_0_part_device(const void* gguf_blocks, int n, int k_src, int k_total, int k_offset,
+                                      int layout, void* packed, void* stream);
+
 /* Q8_0 -> FP32 expansion, bit-identical to dequant_q8 (runtime.cu:26-33).
  * gguf_blocks: device, n_elements/32 records of 34 bytes; out: device float[n_elements]. */
 PQ8_API int pq8_dequant_q8_0(const void* gguf_blocks, float* out, long long n_elements, void* stream);

@@ -365,6 +365,63 @@ __global__ void dequant_kernel(const uint8_t* __restrict__ src, float* __restric
   for (int i = 0; i < 32; ++i) o[i] = s * static_cast<float>(static_cast<int8_t>(rec[2 + i]));
 }
 
+// GGUF Q8_0 bytes already on the device -> packed records (the layout of
+// pq8_pack_q8_0_part, pq8_pack.cpp). One thread per packed row of a tile
+// (128 per CTA), kRepackChunk K blocks per CTA: each block's 34 bytes are read
+// as 2-byte words (a block is 2-byte aligned) and written as two 16-byte value
+// stores and one scale store, so a warp writes 512 contiguous bytes per store.
+// Padding rows get zeros. The first part (k_offset 0) writes the header; a
+// later part checks it and records PQ8_ERR_LAYOUT in the status word if it
+// does not match.
+constexpr int kRepackChunk = 8;
+__global__ void repack_q8_0_kernel(const uint16_t* __restrict__ raw, int n, int kb_src, int kb_total, int kb_off,
+                                   int layout, uint8_t* __restrict__ packed, int* status) {
+  const int t = blockIdx.y, r = threadIdx.x;
+  RowMap rm;
+  const bool valid = map_row(layout, n, t * kTileRows + r, rm);
+  if (blockIdx.x == 0 && t == 0) {
+    auto* h = reinterpret_cast<PackedHeader*>(packed);
+    const int n_tiles = gridDim.y, out_cols = layout == PQ8_LAYOUT_GLU ? n / 2 : layout == PQ8_LAYOUT_GATES4 ? n / 4 : n;
+    if (kb_off == 0) {
+      uint32_t word = 0;
+      switch (r) {
+        case 0: word = kMagic; break;
+        case 1: word = 1; break;
+        case 2: word = static_cast<uint32_t>(n); break;
+        case 3: word = static_cast<uint32_t>(kb_total * 32); break;
+        case 4: word = static_cast<uint32_t>(layout); break;
+        case 5: word = static_cast<uint32_t>(n_tiles); break;
+        case 6: word = static_cast<uint32_t>(kb_total); break;
+        case 7: word = static_cast<uint32_t>(out_cols); break;
+        default: break;
+      }
+      if (r < PQ8_HEADER_BYTES / 4) reinterpret_cast<uint32_t*>(packed)[r] = word;
+    } else if (r == 0 && !(h->magic == kMagic && h->n == n && h->k == kb_total * 32 && h->layout == layout)) {
+      atomicCAS(status, 0, PQ8_ERR_LAYOUT);
+    }
+  }
+  const uint16_t* row = raw + static_cast<size_t>(valid ? rm.src : 0) * kb_src * 17;
+  uint8_t* data = packed + PQ8_HEADER_BYTES;
+  const int kb_end = min(kb_src, (blockIdx.x + 1) * kRepackChunk);
+  for (int kb = blockIdx.x * kRepackChunk; kb < kb_end; ++kb) {
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+    uint16_t sc = 0;
+    if (valid) {
+      const uint16_t* b = row + static_cast<size_t>(kb) * 17;
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = b[1 + i];
+      sc = b[0];
+      lo = make_uint4(w[0] | w[1] << 16, w[2] | w[3] << 16, w[4] | w[5] << 16, w[6] | w[7] << 16);
+      hi = make_uint4(w[8] | w[9] << 16, w[10] | w[11] << 16, w[12] | w[13] << 16, w[14] | w[15] << 16);
+    }
+    uint8_t* rec = data + (static_cast<size_t>(t) * kb_total + kb_off + kb) * kRecordBytes;
+    *reinterpret_cast<uint4*>(rec + r * 16) = lo;
+    *reinterpret_cast<uint4*>(rec + 2048 + r * 16) = hi;
+    *reinterpret_cast<uint16_t*>(rec + kScaleOffset + r * 2) = sc;
+  }
+}
+
 __global__ void round_tf32_kernel(uint32_t* __restrict__ x, long long n) {
   const long long n4 = n >> 2;
   uint4* x4 = reinterpret_cast<uint4*>(x);
@@ -431,6 +488,30 @@ extern "C" int pq8_dequant_q8_0(const void* gguf_blocks, float* out, long long n
   dequant_kernel<<<static_cast<unsigned>(grid), threads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(gguf_blocks), out, blocks);
   return to_code(cudaGetLastError());
+}
+
+extern "C" int pq8_pack_q8_0_part_device(const void* gguf_blocks, int n, int k_src, int k_total, int k_offset,
+                                         int layout, void* packed, void* stream) {
+  if (gguf_blocks == nullptr || packed == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  size_t total = 0;
+  int rc = pq8_packed_size(n, k_total, layout, &total);
+  if (rc) return rc;
+  if (k_src <= 0 || k_src % 32 || k_offset < 0 || k_offset % 32 || k_offset + k_src > k_total)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(gguf_blocks, 2) || !aligned(packed, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  if ((rc = device_state(&ds))) return rc;
+  const int n_tiles = (n + kTileRows - 1) / kTileRows, kb_src = k_src / 32;
+  if (n_tiles > 65535) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  const dim3 grid((kb_src + kRepackChunk - 1) / kRepackChunk, n_tiles);
+  repack_q8_0_kernel<<<grid, kTileRows, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(gguf_blocks), n, kb_src, k_total / 32, k_offset / 32, layout,
+      static_cast<uint8_t*>(packed), ds->status);
+  return to_code(cudaGetLastError());
+}
+
+extern "C" int pq8_pack_q8_0_device(const void* gguf_blocks, int n, int k, int layout, void* packed, void* stream) {
+  return pq8_pack_q8_0_part_device(gguf_blocks, n, k, k, 0, layout, packed, stream);
 }
 
 extern "C" int pq8_round_tf32(float* x, long long n, void* stream) {

@@ -19,7 +19,7 @@ import numpy as np
 import torch
 
 from .pq8 import EPI_NONE, GEMV_MAX_M, LAYOUT_GATES4
-from .runtime import PackedWeight, Runtime, pack_concat_host
+from .runtime import PackedWeight, Runtime
 
 HIDDEN = 640
 LAYERS = 2
@@ -43,9 +43,9 @@ class PQ8Decoder:
             ih, hh = f'decoder.prediction.dec_rnn.lstm.ih_l{l}', f'decoder.prediction.dec_rnn.lstm.hh_l{l}'
             n, k_in = model.tensors[ih + '.weight'].shape
             k_h = model.tensors[hh + '.weight'].shape[1]
-            packed = pack_concat_host([(model.raw(ih + '.weight'), k_in), (model.raw(hh + '.weight'), k_h)], n,
-                                      LAYOUT_GATES4, runtime.lib)
-            w = runtime.upload_packed(packed, n, k_in + k_h, LAYOUT_GATES4)
+            # [W_ih | W_hh] side by side along K, repacked on the device
+            w = runtime.uploader().pack([(model.raw(ih + '.weight'), k_in), (model.raw(hh + '.weight'), k_h)], n,
+                                        LAYOUT_GATES4)
             bias = (np.asarray(model.array(ih + '.bias'), np.float32).reshape(-1)
                     + np.asarray(model.array(hh + '.bias'), np.float32).reshape(-1))
             self.lstm.append((w, torch.from_numpy(bias).to(dev), k_in))

@@ -34,6 +34,8 @@ segments) so that rows from several windows share one launch.
 """
 from __future__ import annotations
 
+import time
+
 import numpy as np
 import torch
 
@@ -70,24 +72,36 @@ class EncoderStack:
     """All Q8_0 linears of ``layers`` encoder layers over ``rows`` activation rows on one device."""
 
     def __init__(self, model, runtime: Runtime, rows: int, layers: int = 24, seed: int = 0,
-                 producer_tf32: bool = True):
+                 producer_tf32: bool = True, upload: str = 'device'):
         """``producer_tf32``: the GEMM inputs that come from outside the contraction path
         (LayerNorm outputs, attention context, positional table) are produced TF32-rounded,
         as a fused producer would write them, and every GEMM skips its rounding pass.
-        With False, those GEMMs round their input tile in shared memory themselves."""
+        With False, those GEMMs round their input tile in shared memory themselves.
+        ``upload``: 'device' copies the GGUF bytes and repacks them on the GPU
+        (``WeightUploader``); 'host' packs on the host and copies the packed bytes
+        (the same result, kept to measure the difference)."""
         self.rt, self.rows, self.layers = runtime, rows, layers
         self.producer_tf32 = producer_tf32
         dev = runtime.device
         self.weights: list[dict[str, PackedWeight]] = []
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        up = runtime.uploader()
         for l in range(layers):
             base = f'encoder.layers.{l}.'
             packed = {}
             for name, keys, n, k, epi, _, _, _, _ in LAYER_PLAN:
-                raw = np.concatenate([np.asarray(model.raw(base + key + '.weight'), np.uint8).reshape(-1)
-                                      for key in keys])
+                raws = [model.raw(base + key + '.weight') for key in keys]
                 layout = LAYOUT_GLU if epi == EPI_GLU else 0
-                packed[name] = runtime.upload_packed(pack_host(raw, n, k, layout, runtime.lib), n, k, layout)
+                if upload == 'device':
+                    packed[name] = up.pack_rows(raws, n, k, layout)
+                else:
+                    raw = np.concatenate([np.asarray(r, np.uint8).reshape(-1) for r in raws])
+                    packed[name] = runtime.upload_packed(pack_host(raw, n, k, layout, runtime.lib), n, k, layout)
             self.weights.append(packed)
+        up.finish()
+        torch.cuda.synchronize(dev)
+        self.load_seconds = time.perf_counter() - t0
         self.weight_bytes = sum(w.data.numel() for layer in self.weights for w in layer.values())
         g = torch.Generator(device='cpu').manual_seed(seed)
         f32 = dict(dtype=torch.float32, device=dev)

@@ -44,6 +44,8 @@ SIGNATURES = {
     'pq8_packed_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
     'pq8_pack_q8_0': ([_P, _I, _I, _I, _P], _I),
     'pq8_pack_q8_0_part': ([_P, _I, _I, _I, _I, _I, _P], _I),
+    'pq8_pack_q8_0_device': ([_P, _I, _I, _I, _P, _P], _I),
+    'pq8_pack_q8_0_part_device': ([_P, _I, _I, _I, _I, _I, _P, _P], _I),
     'pq8_dequant_q8_0': ([_P, _P, _LL, _P], _I),
     'pq8_round_tf32': ([_P, _LL, _P], _I),
     'pq8_gemm': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P], _I),
