@@ -50,8 +50,8 @@ def parse():
     ap.add_argument('--layers', type=int, default=24)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
-    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep,load',
-                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep, load)')
+    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep,load,block',
+                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep, load, block)')
     return ap.parse_args()
 
 
@@ -304,6 +304,8 @@ def run_gpu(args):
             extras['sweep'] = sweep_measure(torch, rt)
         if 'load' in wanted:
             extras['weight_load'] = load
+        if 'block' in wanted:
+            extras['full_block'] = block_measure(torch, rt, args, ms)
     sched.barrier()
 
     if sched.rank == 0:
@@ -481,6 +483,41 @@ def tdt_measure(torch, rt):
                     'steps_per_s over the replay loop, call_* over the whole call (frame table, graph capture, '
                     'results to host lists)'}
     return out
+
+
+def block_measure(torch, rt, args, linear_ms):
+    """Whole FastConformer blocks (SURVEY-(f)2): every layer of config 2's shapes with
+    LayerNorms, rel-pos attention and the conv module on the device around the same Q8_0
+    linears, 8 windows x 375 frames per GPU; one CUDA-graph replay per step. Random
+    block-scale weights (SyntheticParakeet(block=True))."""
+    from parakeet_cuda_b200.block import EncoderBlocks
+    from parakeet_cuda_b200.synthetic import SyntheticParakeet
+    model = SyntheticParakeet(seed=5, encoder_layers=args.layers, decoder=False, block=True)
+    blocks = EncoderBlocks(model, rt, args.windows_per_gpu, WINDOW_FRAMES, layers=args.layers)
+    del model
+    blocks.buf['x'].normal_()
+    blocks.step()
+    torch.cuda.synchronize()
+    graph = blocks.capture()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    del graph
+    frames = args.windows_per_gpu * WINDOW_FRAMES
+    return {'layers': args.layers, 'windows': args.windows_per_gpu, 'frames_per_window': WINDOW_FRAMES,
+            'ms_per_step': ms, 'frames_per_s': frames / ms * 1e3,
+            'tflops_algorithmic': blocks.flops_per_step() / ms / 1e9,
+            'linear_stack_ms_per_step': linear_ms,
+            'attention_products': 'cuBLAS TF32 batched GEMMs; shift + softmax, LayerNorm, depthwise conv: pq8 kernels',
+            'note': 'linear_pos once per layer on the 2T-1 positional rows, shared by all windows'}
 
 
 def load_measure(torch, rt, model):

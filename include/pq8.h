@@ -58,6 +58,7 @@ extern "C" {
 #define PQ8_ERR_LAYOUT 1006            /* device-side: packed header does not match n/k/layout */
 #define PQ8_ERR_TIMEOUT 1007           /* device-side: a bounded wait inside a kernel expired */
 #define PQ8_ERR_DRIVER 1008            /* CUDA driver entry point missing or tensor-map encode failed */
+#define PQ8_ERR_LIBRARY 1009           /* a cuBLAS call of pq8_rel_attention failed */
 
 /* ---- packed weight layouts ---- */
 #define PQ8_LAYOUT_ROWS 0   /* packed row p = source row p */
@@ -74,6 +75,7 @@ extern "C" {
 /* ---- flags ---- */
 #define PQ8_FLAG_X_TF32 1   /* x already holds TF32-rounded values: skip the in-kernel rounding pass */
 #define PQ8_FLAG_OUT_TF32 2 /* round y to TF32 (nearest) so that it can feed another GEMM with PQ8_FLAG_X_TF32 */
+#define PQ8_ATTN_FP32 4     /* pq8_rel_attention: FP32 products instead of TF32 tensor-core products */
 
 #define PQ8_HEADER_BYTES 256
 #define PQ8_TILE_ROWS 128
@@ -246,6 +248,43 @@ PQ8_API int pq8_gemv_static(const void* w, const float* x, float* y, const float
  * mismatch or an expired bounded wait. Synchronizes `stream`. *status = 0 or
  * PQ8_ERR_LAYOUT / PQ8_ERR_TIMEOUT. */
 PQ8_API int pq8_device_status(int* status, void* stream);
+
+/* ---- the FastConformer block around the linears ----------------------------
+ * The rest of one encoder block (parakeet_cuda/reference.py:33-66) on the
+ * device: with these and pq8_gemm, a whole block runs without the host. */
+
+/* LayerNorm of rows of `width` floats (multiple of 128, at most 1024), eps
+ * 1e-5: y = (x - mean) / sqrt(var + eps) * w + b. PQ8_FLAG_OUT_TF32 rounds y
+ * to TF32 for a following pq8_gemm with PQ8_FLAG_X_TF32. All pointers 16-byte
+ * aligned. Replaces layer_norm (runtime.cu:38-48). */
+PQ8_API int pq8_layer_norm(const float* x, const float* w, const float* b, float* y, int rows, int width,
+                           int flags, void* stream);
+
+/* Conv-module middle (reference.py:60-63): depthwise convolution with 9 taps
+ * along the frames of each of `windows` windows of `t` frames (zero rows
+ * beyond a window's ends), BatchNorm with running statistics (eps 1e-5),
+ * SiLU. x, y: float[windows * t][channels] (distinct, 16-byte aligned);
+ * w9_f16: the GGUF fp16 depthwise weight [channels][9]; bn_*: float[channels].
+ * Replaces depthwise1 (runtime.cu:63-71). */
+PQ8_API int pq8_conv_depthwise_bn_silu(const float* x, const uint16_t* w9_f16, const float* bn_weight,
+                                       const float* bn_bias, const float* bn_mean, const float* bn_var, float* y,
+                                       int windows, int t, int channels, int flags, void* stream);
+
+/* Relative-position self-attention of 8 heads x 128 over `windows` windows of
+ * `t` frames (reference.py:46-57). qkv: float[windows * t][3072] (Q | K | V,
+ * the packed linear_q/k/v output); pos: float[2t - 1][1024], linear_pos of
+ * the positional rows pe[limit - t : limit + t - 1], shared by all windows;
+ * pos_bias_u / _v: float[1024] (head-major); ctx: float[windows * t][1024],
+ * heads merged. Scores ((q + u) k + (q + v) p_{t-1+j-i}) / sqrt(128), softmax
+ * over keys, context = probabilities x V. The three batched products go to
+ * cuBLAS (TF32 tensor cores, or FP32 with PQ8_ATTN_FP32); the biases, the
+ * shift and the softmax are pq8 kernels. PQ8_FLAG_OUT_TF32 rounds ctx for
+ * linear_out. Replaces query_bias, rel_scores, softmax and the attention
+ * GEMMs of encoder.py:95-112 (runtime.cu:115-137). */
+PQ8_API int pq8_attention_workspace_size(int windows, int t, size_t* bytes);
+PQ8_API int pq8_rel_attention(const float* qkv, const float* pos, const float* pos_bias_u, const float* pos_bias_v,
+                              float* ctx, int windows, int t, int flags, void* workspace, size_t workspace_bytes,
+                              void* stream);
 
 #ifdef __cplusplus
 }

@@ -49,7 +49,7 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
     if not force and not stale():
         return LIB
     cmd = [nvcc_path(), *ARCH_FLAGS, *COMMON_FLAGS, '-I', str(INCLUDE), '-I', str(CSRC), '-shared',
-           *extra, '-o', str(LIB) + '.tmp', *map(str, sources())]
+           *extra, '-o', str(LIB) + '.tmp', *map(str, sources()), '-lcublas']
     if verbose:
         print(' '.join(cmd), file=sys.stderr)
     r = subprocess.run(cmd, capture_output=True, text=True)

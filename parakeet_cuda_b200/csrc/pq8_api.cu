@@ -1,5 +1,6 @@
 // C ABI of libpq8: argument checking, per-device state, tile-shape choice and
 // kernel launches. See include/pq8.h for the contract of each entry point.
+#include <cublas_v2.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -12,6 +13,7 @@
 #include "pq8_device.cuh"
 #include "pq8_gemm.cuh"
 #include "pq8_gemv.cuh"
+#include "pq8_block.cuh"
 #include "pq8_tdt.cuh"
 
 namespace pq8 {
@@ -27,6 +29,8 @@ struct DeviceState {
   int sms = 0;
   int* status = nullptr;
   bool attr_set[16] = {};
+  cublasHandle_t blas = nullptr;  // attention GEMMs; created on first use, guarded by blas_mutex
+  std::mutex blas_mutex;
 };
 
 std::mutex g_mutex;
@@ -467,6 +471,7 @@ extern "C" const char* pq8_error_string(int code) {
     case PQ8_ERR_LAYOUT: return "PQ8_ERR_LAYOUT: packed weight header does not match n/k/layout";
     case PQ8_ERR_TIMEOUT: return "PQ8_ERR_TIMEOUT: a bounded wait inside a kernel expired";
     case PQ8_ERR_DRIVER: return "PQ8_ERR_DRIVER: CUDA driver entry point unavailable or tensor map rejected";
+    case PQ8_ERR_LIBRARY: return "PQ8_ERR_LIBRARY: a cuBLAS call of the attention failed";
     default:
       if (code > 0 && code < 1000) return cudaGetErrorString(static_cast<cudaError_t>(code));
       return "unknown pq8 error";
@@ -820,3 +825,169 @@ extern "C" int pq8_gemv_static(const void* w, const float* x, float* y, const fl
   return launch_gemv(ds, p, scratch, kStaticScratchBytes, st);
 }
 
+
+// ---------------------------------------------------------------- the block around the linears
+extern "C" int pq8_layer_norm(const float* x, const float* w, const float* b, float* y, int rows, int width,
+                              int flags, void* stream) {
+  if (rows < 0 || width <= 0 || width % 128 || width > 1024) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (rows == 0) return PQ8_OK;
+  if (x == nullptr || w == nullptr || b == nullptr || y == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (flags & ~PQ8_FLAG_OUT_TF32) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(w, 16) || !aligned(b, 16) || !aligned(y, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  const int round_out = (flags & PQ8_FLAG_OUT_TF32) ? 1 : 0;
+  constexpr int kRowsPerCta = 8;  // one warp per row
+  const dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void (*const kernels[8])(const float*, const float*, const float*, float*, int, int) = {
+      layer_norm_kernel<1>, layer_norm_kernel<2>, layer_norm_kernel<3>, layer_norm_kernel<4>,
+      layer_norm_kernel<5>, layer_norm_kernel<6>, layer_norm_kernel<7>, layer_norm_kernel<8>};
+  cudaError_t e = launch_pdl(kernels[width / 128 - 1], grid, dim3(32 * kRowsPerCta), 0, st, x, w, b, y, rows,
+                             round_out);
+  if (e != cudaSuccess) return to_code(e);
+  return to_code(cudaGetLastError());
+}
+
+extern "C" int pq8_conv_depthwise_bn_silu(const float* x, const uint16_t* w9_f16, const float* bn_weight,
+                                          const float* bn_bias, const float* bn_mean, const float* bn_var, float* y,
+                                          int windows, int t, int channels, int flags, void* stream) {
+  if (windows < 0 || t < 0 || channels <= 0 || channels % 2 || channels > 4096 || windows > 65535)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (windows == 0 || t == 0) return PQ8_OK;
+  if (x == nullptr || w9_f16 == nullptr || bn_weight == nullptr || bn_bias == nullptr || bn_mean == nullptr ||
+      bn_var == nullptr || y == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  if (x == y) return PQ8_ERR_INVALID_ARGUMENT;  // neighbouring rows are read after a row is written
+  if (flags & ~PQ8_FLAG_OUT_TF32) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(w9_f16, 2)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  const dim3 grid((t + kConvStrip - 1) / kConvStrip, windows, (channels / 2 + kConvThreads - 1) / kConvThreads);
+  cudaError_t e = launch_pdl(conv_depthwise_bn_silu_kernel, grid, dim3(kConvThreads), 0,
+                             static_cast<cudaStream_t>(stream), x, w9_f16, bn_weight, bn_bias, bn_mean, bn_var, y, t,
+                             channels, (flags & PQ8_FLAG_OUT_TF32) ? 1 : 0);
+  if (e != cudaSuccess) return to_code(e);
+  return to_code(cudaGetLastError());
+}
+
+namespace pq8 {
+namespace {
+// Workspace of pq8_rel_attention: biased queries, content / positional scores,
+// pointer tables of the batched GEMMs and cuBLAS's own workspace.
+struct AttentionPlan {
+  size_t qu, qv, ac, bd, ptrs, blas, total;
+};
+constexpr size_t kBlasWorkspace = size_t(32) << 20;
+AttentionPlan plan_attention(int windows, int t) {
+  AttentionPlan a{};
+  const size_t rows = static_cast<size_t>(windows) * t, b = static_cast<size_t>(windows) * 8;
+  size_t off = 0;
+  a.qu = off;
+  off += round256(rows * 1024 * sizeof(float));
+  a.qv = off;
+  off += round256(rows * 1024 * sizeof(float));
+  a.ac = off;
+  off += round256(b * t * t * sizeof(float));
+  a.bd = off;
+  off += round256(b * t * (2 * static_cast<size_t>(t) - 1) * sizeof(float));
+  a.ptrs = off;
+  off += round256(9 * b * sizeof(void*));
+  a.blas = off;
+  off += kBlasWorkspace;
+  a.total = off;
+  return a;
+}
+}  // namespace
+}  // namespace pq8
+
+extern "C" int pq8_attention_workspace_size(int windows, int t, size_t* bytes) {
+  if (bytes == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (windows < 1 || t < 1 || t > 8192) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  *bytes = plan_attention(windows, t).total;
+  return PQ8_OK;
+}
+
+extern "C" int pq8_rel_attention(const float* qkv, const float* pos, const float* pos_bias_u,
+                                 const float* pos_bias_v, float* ctx, int windows, int t, int flags, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (windows < 1 || t < 1 || t > 8192) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (qkv == nullptr || pos == nullptr || pos_bias_u == nullptr || pos_bias_v == nullptr || ctx == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  if (flags & ~(PQ8_FLAG_OUT_TF32 | PQ8_ATTN_FP32)) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(qkv, 16) || !aligned(pos, 16) || !aligned(pos_bias_u, 16) || !aligned(pos_bias_v, 16) ||
+      !aligned(ctx, 16))
+    return PQ8_ERR_MISALIGNED;
+  const AttentionPlan a = plan_attention(windows, t);
+  if (workspace == nullptr || workspace_bytes < a.total) return PQ8_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* base = static_cast<unsigned char*>(workspace);
+  float* qu = reinterpret_cast<float*>(base + a.qu);
+  float* qv = reinterpret_cast<float*>(base + a.qv);
+  float* ac = reinterpret_cast<float*>(base + a.ac);
+  float* bd = reinterpret_cast<float*>(base + a.bd);
+  const int nb = windows * 8;
+  void** ptrs = reinterpret_cast<void**>(base + a.ptrs);
+  // nine tables of nb pointers: A, B, C of the content, positional and context products
+  float** tables = reinterpret_cast<float**>(ptrs);
+
+  const long long rows = static_cast<long long>(windows) * t;
+  cudaError_t e = launch_pdl(attention_query_bias_kernel,
+                             dim3(static_cast<unsigned>(std::min<long long>((rows * 256 + 255) / 256, 8LL * ds->sms))),
+                             dim3(256), 0, st, qkv, pos_bias_u, pos_bias_v, qu, qv, rows);
+  if (e != cudaSuccess) return to_code(e);
+  attention_pointers_kernel<<<(nb + 127) / 128, 128, 0, st>>>(qkv, qu, qv, pos, ac, bd, ctx, windows, t, tables);
+  if ((e = cudaGetLastError()) != cudaSuccess) return to_code(e);
+
+  std::lock_guard<std::mutex> lock(ds->blas_mutex);
+  if (ds->blas == nullptr && cublasCreate(&ds->blas) != CUBLAS_STATUS_SUCCESS) return PQ8_ERR_LIBRARY;
+  cublasHandle_t h = ds->blas;
+  if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS ||
+      cublasSetWorkspace(h, base + a.blas, kBlasWorkspace) != CUBLAS_STATUS_SUCCESS)
+    return PQ8_ERR_LIBRARY;
+  const cublasComputeType_t ct = (flags & PQ8_ATTN_FP32) ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_FAST_TF32;
+  const float one = 1.0f, zero = 0.0f;
+  // Column-major view of the row-major buffers: a row-major [r][c] matrix with
+  // row stride ld is the column-major c x r matrix with leading dimension ld.
+  // Content scores ac[i][j] = qu_i . k_j  (columns i, rows j).
+  cublasStatus_t bs = cublasGemmBatchedEx(h, CUBLAS_OP_T, CUBLAS_OP_N, t, t, 128, &one,
+                                          (const void* const*)(ptrs + 0 * nb), CUDA_R_32F, 3072,
+                                          (const void* const*)(ptrs + 1 * nb), CUDA_R_32F, 1024, &zero,
+                                          (void* const*)(ptrs + 2 * nb), CUDA_R_32F, t, nb, ct,
+                                          CUBLAS_GEMM_DEFAULT);
+  // Positional scores bd[i][p] = qv_i . pos_p over all 2t - 1 positional rows.
+  if (bs == CUBLAS_STATUS_SUCCESS)
+    bs = cublasGemmBatchedEx(h, CUBLAS_OP_T, CUBLAS_OP_N, 2 * t - 1, t, 128, &one,
+                             (const void* const*)(ptrs + 3 * nb), CUDA_R_32F, 1024,
+                             (const void* const*)(ptrs + 4 * nb), CUDA_R_32F, 1024, &zero,
+                             (void* const*)(ptrs + 5 * nb), CUDA_R_32F, 2 * t - 1, nb, ct,
+                             CUBLAS_GEMM_DEFAULT);
+  if (bs != CUBLAS_STATUS_SUCCESS) return PQ8_ERR_LIBRARY;
+  const long long n_rows = static_cast<long long>(nb) * t;
+  const unsigned sm_grid = static_cast<unsigned>((n_rows + 7) / 8);
+  const int lanes_j = (t + 31) / 32;  // shifted scores per lane
+  if (lanes_j <= 4) rel_shift_softmax_kernel<4><<<sm_grid, 256, 0, st>>>(ac, bd, t, n_rows);
+  else if (lanes_j <= 8) rel_shift_softmax_kernel<8><<<sm_grid, 256, 0, st>>>(ac, bd, t, n_rows);
+  else if (lanes_j <= 12) rel_shift_softmax_kernel<12><<<sm_grid, 256, 0, st>>>(ac, bd, t, n_rows);
+  else if (lanes_j <= 16) rel_shift_softmax_kernel<16><<<sm_grid, 256, 0, st>>>(ac, bd, t, n_rows);
+  else rel_shift_softmax_kernel<0><<<sm_grid, 256, 0, st>>>(ac, bd, t, n_rows);
+  if ((e = cudaGetLastError()) != cudaSuccess) return to_code(e);
+  // Context ctx[i][h*128 + d] = sum_j prob[i][j] v_j[d], heads merged in place.
+  bs = cublasGemmBatchedEx(h, CUBLAS_OP_N, CUBLAS_OP_N, 128, t, t, &one,
+                           (const void* const*)(ptrs + 6 * nb), CUDA_R_32F, 3072,
+                           (const void* const*)(ptrs + 7 * nb), CUDA_R_32F, t, &zero,
+                           (void* const*)(ptrs + 8 * nb), CUDA_R_32F, 1024, nb, ct, CUBLAS_GEMM_DEFAULT);
+  if (bs != CUBLAS_STATUS_SUCCESS) return PQ8_ERR_LIBRARY;
+  if (flags & PQ8_FLAG_OUT_TF32) {
+    const long long n = rows * 1024;
+    round_tf32_kernel<<<static_cast<unsigned>(std::min<long long>((n / 4 + 255) / 256 + 1, 8LL * ds->sms)), 256, 0,
+                        st>>>(reinterpret_cast<uint32_t*>(ctx), n);
+  }
+  return to_code(cudaGetLastError());
+}

@@ -28,10 +28,11 @@ ERR_WORKSPACE = 1005
 ERR_LAYOUT = 1006
 ERR_TIMEOUT = 1007
 ERR_DRIVER = 1008
+ERR_LIBRARY = 1009
 
 LAYOUT_ROWS, LAYOUT_GLU, LAYOUT_GATES4 = 0, 1, 2
 EPI_NONE, EPI_RELU, EPI_SILU, EPI_GLU, EPI_RESIDUAL = 0, 1, 2, 3, 4
-FLAG_X_TF32, FLAG_OUT_TF32 = 1, 2
+FLAG_X_TF32, FLAG_OUT_TF32, ATTN_FP32 = 1, 2, 4
 HEADER_BYTES, TILE_ROWS, RECORD_BYTES = 256, 128, 4352
 GEMV_MAX_M = 64          # rows the GEMV entry points take (row groups of 8 run in one launch)
 LINEAR_GEMV_MAX_M = 8    # pq8_linear's GEMV/GEMM dispatch threshold
@@ -45,6 +46,10 @@ SIGNATURES = {
     'pq8_pack_q8_0': ([_P, _I, _I, _I, _P], _I),
     'pq8_pack_q8_0_part': ([_P, _I, _I, _I, _I, _I, _P], _I),
     'pq8_pack_q8_0_device': ([_P, _I, _I, _I, _P, _P], _I),
+    'pq8_layer_norm': ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
+    'pq8_conv_depthwise_bn_silu': ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
+    'pq8_attention_workspace_size': ([_I, _I, C.POINTER(_SZ)], _I),
+    'pq8_rel_attention': ([_P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P], _I),
     'pq8_pack_q8_0_part_device': ([_P, _I, _I, _I, _I, _I, _P, _P], _I),
     'pq8_dequant_q8_0': ([_P, _P, _LL, _P], _I),
     'pq8_round_tf32': ([_P, _LL, _P], _I),
@@ -103,6 +108,11 @@ class Library:
     def gemv_workspace_size(self, m: int, n: int, k: int) -> int:
         out = _SZ()
         self.call('pq8_gemv_workspace_size', m, n, k, C.byref(out))
+        return out.value
+
+    def attention_workspace_size(self, windows: int, t: int) -> int:
+        out = _SZ()
+        self.call('pq8_attention_workspace_size', windows, t, C.byref(out))
         return out.value
 
     def device_status(self, stream=None) -> int:

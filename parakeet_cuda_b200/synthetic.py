@@ -34,6 +34,13 @@ ENCODER_SCALE = (1e-3, 2e-2)
 # implementations with different summation orders could agree on a long token
 # sequence. U[2e-4, 1.2e-3] gives O(1) pre-activations, like a trained LSTM.
 DECODER_SCALE = (2e-4, 1.2e-3)
+# Scale range for the encoder linears of a model built for whole FastConformer
+# blocks (``block=True``): weight std ~ 1/sqrt(1024) as in a trained layer, so
+# the residual stream, the attention scores and the softmax stay O(1) through
+# the block instead of saturating (with the config-0 range a 1024 -> 4096
+# linear alone multiplies the RMS by ~25).
+BLOCK_SCALE = (2e-4, 6e-4)
+POS_EMB_MAX_LEN = 5000  # asr.encoder.pos_emb_max_len (gguf.py:95); pe has 2 * 5000 - 1 rows
 
 
 def q8_0_blocks(rng: np.random.Generator, n: int, k: int, scale_lo: float = 1e-3,
@@ -107,6 +114,34 @@ def _encoder_layer_schema(layer: int):
     return s
 
 
+def _encoder_block_schema(layer: int):
+    """The non-linear parameters of one block (gguf.py:113-124): LayerNorms,
+    rel-pos attention biases, the conv module's depthwise kernel and BatchNorm."""
+    base = f'encoder.layers.{layer}.'
+    s = {}
+    for n in ('norm_feed_forward1', 'norm_self_att', 'norm_conv', 'norm_feed_forward2', 'norm_out'):
+        for suffix in ('weight', 'bias'):
+            s[base + n + '.' + suffix] = ((1024,), 0)
+    for n in ('u', 'v'):
+        s[base + 'self_attn.pos_bias_' + n] = ((128, 8), 0)
+    s[base + 'conv.depthwise_conv.weight'] = ((9, 1, 1024), 1)
+    for n in ('weight', 'bias', 'running_mean', 'running_var'):
+        s[base + 'conv.batch_norm.' + n] = ((1024,), 0)
+    return s
+
+
+def relative_sinusoids(max_len: int, d: int) -> np.ndarray:
+    """Relative positional table ``[2 max_len - 1, d]``: row i encodes the
+    relative position ``max_len - 1 - i`` with interleaved sin / cos of
+    geometrically spaced frequencies (the FastConformer rel-pos encoding)."""
+    pos = (max_len - 1 - np.arange(2 * max_len - 1, dtype=np.float64))[:, None]
+    freq = np.exp(-np.log(10000.0) * np.arange(0, d, 2, dtype=np.float64) / d)[None, :]
+    pe = np.empty((2 * max_len - 1, d), np.float64)
+    pe[:, 0::2] = np.sin(pos * freq)
+    pe[:, 1::2] = np.cos(pos * freq)
+    return pe.astype(np.float32)
+
+
 class SyntheticParakeet:
     """Random-weight stand-in for ``gguf.Model`` with the Parakeet TDT schema.
 
@@ -118,16 +153,24 @@ class SyntheticParakeet:
     """
 
     def __init__(self, seed: int = 0, encoder_layers: int = 24, decoder: bool = True,
-                 blank_bias: float = 0.0, duration0_bias: float = 0.0):
+                 blank_bias: float = 0.0, duration0_bias: float = 0.0, block: bool = False):
+        """``block``: also the non-linear block parameters and the positional
+        table, with ``BLOCK_SCALE`` encoder weights, for whole-block runs."""
         self.seed = seed
+        self.block = block
         # Optional offsets on the joint bias so that random weights also exercise
         # blank emissions and zero-duration steps of the greedy loop.
         self.blank_bias, self.duration0_bias = blank_bias, duration0_bias
         self.metadata = {'asr.tdt.durations': list(DURATIONS),
-                         'asr.tokenizer.vocab': [f'<{i}>' for i in range(BLANK)]}
+                         'asr.tokenizer.vocab': [f'<{i}>' for i in range(BLANK)],
+                         'asr.encoder.pos_emb_max_len': POS_EMB_MAX_LEN}
         schema = {}
+        if block:
+            schema['encoder.pos_enc.pe'] = ((1024, 2 * POS_EMB_MAX_LEN - 1), 0)
         for layer in range(encoder_layers):
             schema.update(_encoder_layer_schema(layer))
+            if block:
+                schema.update(_encoder_block_schema(layer))
         if decoder:
             schema.update(_decoder_schema())
         self.tensors, offset = {}, 0
@@ -149,12 +192,21 @@ class SyntheticParakeet:
             rng = self._rng(name)
             if t.kind == 8:
                 n, k = t.shape
-                lo, hi = ENCODER_SCALE if name.startswith('encoder.') else DECODER_SCALE
+                lo, hi = ((BLOCK_SCALE if self.block else ENCODER_SCALE) if name.startswith('encoder.')
+                          else DECODER_SCALE)
                 data = q8_0_blocks(rng, n, k, lo, hi).reshape(-1)
             elif t.kind == 1:
-                data = rng.normal(size=t.elements).astype('<f2').view(np.uint8)
+                scale = 1.0 / 3.0 if name.endswith('depthwise_conv.weight') else 1.0  # fan-in 9
+                data = (scale * rng.normal(size=t.elements)).astype('<f2').view(np.uint8)
+            elif name == 'encoder.pos_enc.pe':
+                data = relative_sinusoids(POS_EMB_MAX_LEN, 1024).astype('<f4').view(np.uint8).reshape(-1)
             else:
                 values = 0.1 * rng.normal(size=t.elements)
+                if name.endswith(('norm_feed_forward1.weight', 'norm_self_att.weight', 'norm_conv.weight',
+                                  'norm_feed_forward2.weight', 'norm_out.weight', 'batch_norm.weight')):
+                    values += 1.0
+                elif name.endswith('batch_norm.running_var'):
+                    values = rng.uniform(0.5, 1.5, size=t.elements)
                 if name == 'joint.joint_net.2.bias':
                     values[BLANK] += self.blank_bias
                     values[VOCAB] += self.duration0_bias

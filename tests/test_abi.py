@@ -32,7 +32,7 @@ def test_library_exports_every_header_symbol(lib):
 
 def test_error_strings(lib):
     assert lib.error_string(0) == 'PQ8_OK'
-    for code in range(1001, 1009):
+    for code in range(1001, 1010):
         assert lib.error_string(code).startswith('PQ8_ERR_')
     assert 'unknown' in lib.error_string(4242)
 

@@ -1,0 +1,160 @@
+"""GPU parity of the block around the linears: LayerNorm, the conv module's
+depthwise/BatchNorm/SiLU, the relative-position attention, and whole blocks
+against the reference's own block outputs (tests/golden/block.npz) and the
+float64 oracle (oracle/block.py).
+
+Tolerances: the LayerNorm and the depthwise kernel are FP32 arithmetic
+(1e-5 absolute on O(1) values, 1 TF32 ulp when the output is TF32-rounded).
+The attention with FP32 products is checked at 2e-5; with TF32 products at
+the north-star GEMM bar (max |err| <= 2e-3 x RMS). A whole block chains 11
+TF32 GEMMs and the attention, then LayerNorms the result: its bar is
+max |err| <= 1e-2 and RMS error <= 2e-3 on the unit-RMS output.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import block as ob
+from parakeet_cuda_b200 import pq8
+from parakeet_cuda_b200.block import EncoderBlocks
+from parakeet_cuda_b200.runtime import Runtime
+from parakeet_cuda_b200.synthetic import SyntheticParakeet
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def rt():
+    return Runtime(0)
+
+
+@pytest.fixture(scope='module')
+def model():
+    return SyntheticParakeet(seed=31, encoder_layers=2, decoder=False, block=True)
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def tf32_rna(a):
+    """Round float32 to TF32, ties away from zero (the kernels' output rounding)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return ((u + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+@pytest.mark.parametrize('rows,width', [(37, 1024), (5, 256), (300, 640)])
+@pytest.mark.parametrize('flags', [0, pq8.FLAG_OUT_TF32])
+def test_layer_norm(rt, rows, width, flags):
+    rng = np.random.default_rng(rows + width)
+    x = (3.0 * rng.normal(size=(rows, width)) + 0.5).astype(np.float32)
+    w = (1 + 0.1 * rng.normal(size=width)).astype(np.float32)
+    b = (0.1 * rng.normal(size=width)).astype(np.float32)
+    xd, wd, bd = dev(x), dev(w), dev(b)
+    y = torch.empty_like(xd)
+    rt.lib.call('pq8_layer_norm', xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), y.data_ptr(), rows, width, flags,
+                rt.stream())
+    gold = ob.layer_norm(x, w, b)
+    got = y.cpu().numpy()
+    if flags:
+        assert np.array_equal(got, tf32_rna(got))
+        np.testing.assert_allclose(got, gold, atol=2e-5, rtol=2 ** -10)
+    else:
+        np.testing.assert_allclose(got, gold, atol=2e-5, rtol=0)
+
+
+def test_layer_norm_in_place(rt):
+    x = np.random.default_rng(1).normal(size=(64, 1024)).astype(np.float32)
+    w, b = np.ones(1024, np.float32), np.zeros(1024, np.float32)
+    xd, wd, bd = dev(x), dev(w), dev(b)
+    rt.lib.call('pq8_layer_norm', xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), xd.data_ptr(), 64, 1024, 0, rt.stream())
+    np.testing.assert_allclose(xd.cpu().numpy(), ob.layer_norm(x, w, b), atol=2e-5)
+
+
+@pytest.mark.parametrize('windows,t', [(3, 50), (1, 7), (2, 33)])
+def test_conv_depthwise_bn_silu(rt, model, windows, t):
+    wts = ob.BlockWeights(model, 0)
+    x = np.random.default_rng(windows * t).normal(size=(windows * t, 1024)).astype(np.float32)
+    raw = np.ascontiguousarray(model.raw('encoder.layers.0.conv.depthwise_conv.weight')).view(np.int16)
+    wd = torch.from_numpy(raw.copy()).cuda()
+    bn = [dev(wts.bn[n]) for n in ('weight', 'bias', 'running_mean', 'running_var')]
+    xd = dev(x)
+    y = torch.empty_like(xd)
+    rt.lib.call('pq8_conv_depthwise_bn_silu', xd.data_ptr(), wd.data_ptr(), *[p.data_ptr() for p in bn], y.data_ptr(),
+                windows, t, 1024, 0, rt.stream())
+    gold = np.concatenate([ob.conv_module_depthwise(wts, x[i * t:(i + 1) * t]) for i in range(windows)])
+    np.testing.assert_allclose(y.cpu().numpy(), gold, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize('fp32', [True, False])
+# t = 200 / 300 / 500 take the register softmax with 8 / 12 / 16 scores per
+# lane, t = 600 the three-pass form
+@pytest.mark.parametrize('windows,t', [(2, 40), (1, 9), (3, 64), (1, 200), (2, 300), (1, 500), (1, 600)])
+def test_rel_attention(rt, windows, t, fp32):
+    rng = np.random.default_rng(7 * windows + t)
+    qkv = (0.5 * rng.normal(size=(windows * t, 3072))).astype(np.float32)
+    pos = (0.5 * rng.normal(size=(2 * t - 1, 1024))).astype(np.float32)
+    u, v = (0.1 * rng.normal(size=1024)).astype(np.float32), (0.1 * rng.normal(size=1024)).astype(np.float32)
+    ws = torch.empty(rt.lib.attention_workspace_size(windows, t), dtype=torch.uint8, device='cuda')
+    qd, pd, ud, vd = dev(qkv), dev(pos), dev(u), dev(v)
+    ctx = torch.empty(windows * t, 1024, device='cuda')
+    rt.lib.call('pq8_rel_attention', qd.data_ptr(), pd.data_ptr(), ud.data_ptr(), vd.data_ptr(), ctx.data_ptr(),
+                windows, t, pq8.ATTN_FP32 if fp32 else 0, ws.data_ptr(), ws.numel(), rt.stream())
+    heads = lambda y: y.reshape(-1, 8, 128).transpose(1, 0, 2).astype(np.float64)
+    p = heads(pos)
+    gold = []
+    for w in range(windows):
+        blk = qkv[w * t:(w + 1) * t]
+        q, k, vv = heads(blk[:, :1024]), heads(blk[:, 1024:2048]), heads(blk[:, 2048:])
+        s = ob.rel_shift_scores(q + u.reshape(8, 1, 128), q + v.reshape(8, 1, 128), k, p)
+        gold.append((ob.softmax(s) @ vv).transpose(1, 0, 2).reshape(t, 1024))
+    gold = np.concatenate(gold)
+    got = ctx.cpu().numpy()
+    err = np.abs(got - gold).max() / np.sqrt((gold ** 2).mean())
+    assert err <= (2e-5 if fp32 else 2e-3), err
+    assert rt.device_status() == 0
+
+
+def _block_errors(got, gold):
+    d = got.astype(np.float64) - gold
+    return float(np.abs(d).max()), float(np.sqrt((d ** 2).mean()))
+
+
+@pytest.mark.parametrize('t,layers', [(40, 1), (40, 2), (7, 1)])
+def test_blocks_match_reference_golden(rt, model, golden_dir, t, layers):
+    d = np.load(golden_dir / 'block.npz')
+    gold = d[f't{t}_layer{layers - 1}'].astype(np.float64)
+    blocks = EncoderBlocks(model, rt, 1, t, layers=layers)
+    got = blocks.forward(dev(d[f't{t}_x'])).cpu().numpy()
+    mx, rms = _block_errors(got, gold)
+    print(f't={t} layers={layers}: max {mx:.2e} rms {rms:.2e}')
+    assert mx <= 1e-2 and rms <= 2e-3, (mx, rms)
+    assert rt.device_status() == 0
+
+
+def test_blocks_windows_are_independent(rt, model):
+    """Three windows in one stream give each window's own result: the depthwise
+    convolution and the attention stop at window boundaries."""
+    t = 50
+    x = np.random.default_rng(9).normal(size=(3 * t, 1024)).astype(np.float32)
+    many = EncoderBlocks(model, rt, 3, t, layers=1).forward(dev(x)).cpu().numpy()
+    one = EncoderBlocks(model, rt, 1, t, layers=1)
+    for w in range(3):
+        single = one.forward(dev(x[w * t:(w + 1) * t])).cpu().numpy()
+        np.testing.assert_allclose(many[w * t:(w + 1) * t], single, atol=1e-5, rtol=0)
+    gold = ob.blocks(x, model, [0], windows=3)
+    mx, rms = _block_errors(many, gold)
+    assert mx <= 1e-2 and rms <= 2e-3, (mx, rms)
+
+
+def test_blocks_graph_replay_matches_eager(rt, model):
+    t = 40
+    x = dev(np.random.default_rng(10).normal(size=(2 * t, 1024)))
+    blocks = EncoderBlocks(model, rt, 2, t, layers=2)
+    eager = blocks.forward(x).clone()
+    blocks.buf['x'].copy_(x)
+    graph = blocks.capture()
+    blocks.buf['x'].copy_(x)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(blocks.buf['x'], eager)
