@@ -490,11 +490,35 @@ def block_measure(torch, rt, args, linear_ms):
     LayerNorms, rel-pos attention and the conv module on the device around the same Q8_0
     linears, 8 windows x 375 frames per GPU; one CUDA-graph replay per step. Random
     block-scale weights (SyntheticParakeet(block=True))."""
-    from parakeet_cuda_b200.block import EncoderBlocks
+    from parakeet_cuda_b200.block import EncoderBlocks, EncoderStem
     from parakeet_cuda_b200.synthetic import SyntheticParakeet
     model = SyntheticParakeet(seed=5, encoder_layers=args.layers, decoder=False, block=True)
     blocks = EncoderBlocks(model, rt, args.windows_per_gpu, WINDOW_FRAMES, layers=args.layers)
+    mel_frames = 8 * WINDOW_FRAMES  # 10 ms mel hop, 8x subsampling
+    stem = EncoderStem(model, rt, args.windows_per_gpu, mel_frames)
     del model
+    mel = torch.randn(args.windows_per_gpu, mel_frames, 128, device=rt.device)
+    stem.forward(mel)
+    torch.cuda.synchronize()
+    sg = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(rt.device)
+    side.wait_stream(torch.cuda.current_stream(rt.device))
+    with torch.cuda.stream(side):
+        sg.capture_begin()
+        stem.forward(mel)
+        sg.capture_end()
+    torch.cuda.current_stream(rt.device).wait_stream(side)
+    for _ in range(3):
+        sg.replay()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(10):
+        sg.replay()
+    s1.record()
+    torch.cuda.synchronize()
+    stem_ms = s0.elapsed_time(s1) / 10
+    del sg
     blocks.buf['x'].normal_()
     blocks.step()
     torch.cuda.synchronize()
@@ -514,6 +538,8 @@ def block_measure(torch, rt, args, linear_ms):
     frames = args.windows_per_gpu * WINDOW_FRAMES
     return {'layers': args.layers, 'windows': args.windows_per_gpu, 'frames_per_window': WINDOW_FRAMES,
             'ms_per_step': ms, 'frames_per_s': frames / ms * 1e3,
+            'stem_ms_per_step': stem_ms, 'stem_mel_frames_per_window': mel_frames,
+            'encoder_with_stem_frames_per_s': frames / (ms + stem_ms) * 1e3,
             'tflops_algorithmic': blocks.flops_per_step() / ms / 1e9,
             'linear_stack_ms_per_step': linear_ms,
             'attention_products': 'cuBLAS TF32 batched GEMMs; shift + softmax, LayerNorm, depthwise conv: pq8 kernels',

@@ -75,7 +75,8 @@ extern "C" {
 /* ---- flags ---- */
 #define PQ8_FLAG_X_TF32 1   /* x already holds TF32-rounded values: skip the in-kernel rounding pass */
 #define PQ8_FLAG_OUT_TF32 2 /* round y to TF32 (nearest) so that it can feed another GEMM with PQ8_FLAG_X_TF32 */
-#define PQ8_ATTN_FP32 4     /* pq8_rel_attention: FP32 products instead of TF32 tensor-core products */
+#define PQ8_FLAG_FP32_PRODUCTS 4 /* pq8_rel_attention, pq8_stem: cuBLAS products in FP32 instead of TF32 */
+#define PQ8_ATTN_FP32 PQ8_FLAG_FP32_PRODUCTS
 
 #define PQ8_HEADER_BYTES 256
 #define PQ8_TILE_ROWS 128
@@ -285,6 +286,24 @@ PQ8_API int pq8_attention_workspace_size(int windows, int t, size_t* bytes);
 PQ8_API int pq8_rel_attention(const float* qkv, const float* pos, const float* pos_bias_u, const float* pos_bias_v,
                               float* ctx, int windows, int t, int flags, void* workspace, size_t workspace_bytes,
                               void* stream);
+
+/* Subsampling stem (reference.py:11-30, encoder.py:38-66) for `windows`
+ * windows of `frames` mel frames: mel float[windows][frames][128]. Three
+ * 3x3 stride-2 stages (full convolution to 256 channels + ReLU; twice
+ * depthwise + pointwise 256 x 256 + ReLU), flattened channel-major to 4096 and
+ * projected by the Q8_0 output linear: out float[windows * t][1024] with
+ * t = ceil(ceil(ceil(frames / 2) / 2) / 2) rows per window. w0, w2, w5:
+ * float[256][9] (the GGUF's fp16 kernels as float); w3, w6: float[256][256]
+ * (output channel major); b*: float[256]; w_out: packed Q8_0 [1024, 4096]
+ * (ROWS), b_out: float[1024]. The pointwise products go to cuBLAS (TF32, or
+ * FP32 with PQ8_FLAG_FP32_PRODUCTS); everything else is pq8 kernels and
+ * pq8_gemm. Replaces conv_first, conv_dw2, the stem SGEMMs, bias_act and
+ * flatten_stem (runtime.cu:73-101). */
+PQ8_API int pq8_stem_workspace_size(int windows, int frames, size_t* bytes);
+PQ8_API int pq8_stem(const float* mel, int windows, int frames, const float* w0, const float* b0, const float* w2,
+                     const float* b2, const float* w3, const float* b3, const float* w5, const float* b5,
+                     const float* w6, const float* b6, const void* w_out, const float* b_out, float* out, int flags,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

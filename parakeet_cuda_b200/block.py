@@ -157,3 +157,40 @@ class EncoderBlocks:
         pos = (2 * self.t - 1) * D_MODEL * D_MODEL * 2
         att = self.windows * 8 * 128 * 2 * (self.t * self.t * 2 + self.t * (2 * self.t - 1))
         return self.layers * (lin + pos + att)
+
+
+class EncoderStem:
+    """The subsampling stem (``parakeet_cuda/reference.py:11-30``) for ``windows`` windows of
+    ``frames`` mel frames: ``forward(mel [windows, frames, 128])`` returns the encoder input
+    ``[windows * t, 1024]`` (t = frames / 8, rounded up per stage) for ``EncoderBlocks``."""
+
+    def __init__(self, model, runtime: Runtime, windows: int, frames: int, fp32_products: bool = False):
+        from .pq8 import FLAG_FP32_PRODUCTS
+        self.rt, self.windows, self.frames = runtime, windows, frames
+        self.flags = FLAG_FP32_PRODUCTS if fp32_products else 0
+        dev = runtime.device
+        to_dev = lambda a: torch.from_numpy(np.ascontiguousarray(np.asarray(a, np.float32))).to(dev)
+        name = 'encoder.pre_encode.'
+        self.w = {i: to_dev(np.asarray(model.array(f'{name}conv.{i}.weight')).reshape(256, -1)) for i in (0, 2, 3, 5, 6)}
+        self.b = {i: to_dev(np.asarray(model.array(f'{name}conv.{i}.bias')).reshape(-1)) for i in (0, 2, 3, 5, 6)}
+        up = runtime.uploader()
+        self.w_out = up.pack([(model.raw(name + 'out.weight'), 4096)], 1024)
+        up.finish()
+        self.b_out = to_dev(np.asarray(model.array(name + 'out.bias')).reshape(-1))
+        t = frames
+        for _ in range(3):
+            t = (t + 1) // 2
+        self.t = t
+        self.ws = torch.empty(runtime.lib.stem_workspace_size(windows, frames), dtype=torch.uint8, device=dev)
+        self.out = torch.empty(windows * t, D_MODEL, dtype=torch.float32, device=dev)
+
+    def forward(self, mel: torch.Tensor) -> torch.Tensor:
+        if tuple(mel.shape) != (self.windows, self.frames, 128) or mel.dtype != torch.float32:
+            raise ValueError(f'mel must be float32 [{self.windows}, {self.frames}, 128]')
+        mel = mel.contiguous()
+        w, b = self.w, self.b
+        self.rt.lib.call('pq8_stem', mel.data_ptr(), self.windows, self.frames, w[0].data_ptr(), b[0].data_ptr(),
+                         w[2].data_ptr(), b[2].data_ptr(), w[3].data_ptr(), b[3].data_ptr(), w[5].data_ptr(),
+                         b[5].data_ptr(), w[6].data_ptr(), b[6].data_ptr(), self.w_out.pointer, self.b_out.data_ptr(),
+                         self.out.data_ptr(), self.flags, self.ws.data_ptr(), self.ws.numel(), self.rt.stream())
+        return self.out

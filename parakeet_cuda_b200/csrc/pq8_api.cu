@@ -991,3 +991,110 @@ extern "C" int pq8_rel_attention(const float* qkv, const float* pos, const float
   }
   return to_code(cudaGetLastError());
 }
+
+// ---------------------------------------------------------------- subsampling stem
+namespace pq8 {
+namespace {
+struct StemPlan {
+  int t1, t2, t3;
+  size_t a, b, c, d, z, flat, blas, total;
+};
+StemPlan plan_stem(int windows, int frames) {
+  StemPlan p{};
+  p.t1 = (frames + 1) / 2;
+  p.t2 = (p.t1 + 1) / 2;
+  p.t3 = (p.t2 + 1) / 2;
+  const size_t w = windows, ch = kStemChannels * sizeof(float);
+  size_t off = 0;
+  p.a = off;
+  off += round256(w * p.t1 * 64 * ch);
+  p.b = off;
+  off += round256(w * p.t2 * 32 * ch);
+  p.c = off;
+  off += round256(w * p.t2 * 32 * ch);
+  p.d = off;
+  off += round256(w * p.t3 * 16 * ch);
+  p.z = off;
+  off += round256(w * p.t3 * 16 * ch);
+  p.flat = off;
+  off += round256(w * p.t3 * 4096 * sizeof(float));
+  p.blas = off;
+  off += kBlasWorkspace;
+  p.total = off;
+  return p;
+}
+unsigned stem_grid(long long positions, int sms) {
+  return static_cast<unsigned>(std::max<long long>(1, std::min<long long>(positions, 16LL * sms)));
+}
+}  // namespace
+}  // namespace pq8
+
+extern "C" int pq8_stem_workspace_size(int windows, int frames, size_t* bytes) {
+  if (bytes == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (windows < 1 || frames < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  *bytes = plan_stem(windows, frames).total;
+  return PQ8_OK;
+}
+
+extern "C" int pq8_stem(const float* mel, int windows, int frames, const float* w0, const float* b0, const float* w2,
+                        const float* b2, const float* w3, const float* b3, const float* w5, const float* b5,
+                        const float* w6, const float* b6, const void* w_out, const float* b_out, float* out, int flags,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (windows < 1 || frames < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (mel == nullptr || w0 == nullptr || b0 == nullptr || w2 == nullptr || b2 == nullptr || w3 == nullptr ||
+      b3 == nullptr || w5 == nullptr || b5 == nullptr || w6 == nullptr || b6 == nullptr || w_out == nullptr ||
+      out == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  if (flags & ~PQ8_FLAG_FP32_PRODUCTS) return PQ8_ERR_INVALID_ARGUMENT;
+  const StemPlan sp = plan_stem(windows, frames);
+  if (workspace == nullptr || workspace_bytes < sp.total) return PQ8_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(out, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* base = static_cast<unsigned char*>(workspace);
+  float* a = reinterpret_cast<float*>(base + sp.a);
+  float* b = reinterpret_cast<float*>(base + sp.b);
+  float* c = reinterpret_cast<float*>(base + sp.c);
+  float* d = reinterpret_cast<float*>(base + sp.d);
+  float* z = reinterpret_cast<float*>(base + sp.z);
+  float* flat = reinterpret_cast<float*>(base + sp.flat);
+  const long long p1 = static_cast<long long>(windows) * sp.t1 * 64, p2 = static_cast<long long>(windows) * sp.t2 * 32,
+                  p3 = static_cast<long long>(windows) * sp.t3 * 16;
+  const float* no_bias = nullptr;
+  cudaError_t e = launch_pdl(stem_conv_first_kernel, dim3(stem_grid(p1, ds->sms)), dim3(kStemChannels), 0, st, mel, w0,
+                             b0, a, frames, 128, sp.t1, 64, p1);
+  if (e == cudaSuccess)
+    e = launch_pdl(stem_depthwise_kernel, dim3(stem_grid(p2, ds->sms)), dim3(kStemChannels), 0, st,
+                   static_cast<const float*>(a), no_bias, w2, b2, b, sp.t1, 64, sp.t2, 32, p2);
+  if (e != cudaSuccess) return to_code(e);
+  {
+    std::lock_guard<std::mutex> lock(ds->blas_mutex);
+    if (ds->blas == nullptr && cublasCreate(&ds->blas) != CUBLAS_STATUS_SUCCESS) return PQ8_ERR_LIBRARY;
+    cublasHandle_t h = ds->blas;
+    if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS ||
+        cublasSetWorkspace(h, base + sp.blas, kBlasWorkspace) != CUBLAS_STATUS_SUCCESS)
+      return PQ8_ERR_LIBRARY;
+    const cublasComputeType_t ct =
+        (flags & PQ8_FLAG_FP32_PRODUCTS) ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_FAST_TF32;
+    const float one = 1.0f, zero = 0.0f;
+    // pointwise 256 x 256: out[p][n] = sum_k in[p][k] w[n][k] (row-major), bias and ReLU applied by the reader
+    if (cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, 256, static_cast<int>(p2), 256, &one, w3, CUDA_R_32F, 256, b,
+                     CUDA_R_32F, 256, &zero, c, CUDA_R_32F, 256, ct, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+      return PQ8_ERR_LIBRARY;
+    e = launch_pdl(stem_depthwise_kernel, dim3(stem_grid(p3, ds->sms)), dim3(kStemChannels), 0, st,
+                   static_cast<const float*>(c), b3, w5, b5, d, sp.t2, 32, sp.t3, 16, p3);
+    if (e != cudaSuccess) return to_code(e);
+    if (cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, 256, static_cast<int>(p3), 256, &one, w6, CUDA_R_32F, 256, d,
+                     CUDA_R_32F, 256, &zero, z, CUDA_R_32F, 256, ct, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
+      return PQ8_ERR_LIBRARY;
+  }
+  const long long rows = static_cast<long long>(windows) * sp.t3;
+  e = launch_pdl(stem_flatten_kernel, dim3(stem_grid(rows, ds->sms)), dim3(kStemChannels), 0, st,
+                 static_cast<const float*>(z), b6, flat, rows);
+  if (e != cudaSuccess) return to_code(e);
+  // the output linear, Q8_0 [1024, 4096] + bias, on the TF32-rounded flattened rows
+  return pq8_gemm(w_out, flat, out, b_out, nullptr, static_cast<int>(rows), 1024, 4096, PQ8_EPI_NONE, 1.0f,
+                  PQ8_FLAG_X_TF32, stream);
+}

@@ -226,4 +226,112 @@ __global__ void attention_pointers_kernel(const float* qkv, const float* qu, con
   for (int i = 0; i < 9; ++i) tables[i * nb + b] = p[i];
 }
 
+// ---------------------------------------------------------------------------
+// Subsampling stem (reference.py:11-30; conv_first, conv_dw2, flatten_stem in
+// runtime.cu:73-101). Windows are independent: every stage pads each window's
+// own edges. Activations are [window][time][frequency][256 channels]; a CTA of
+// 256 threads gives thread c channel c (so its 9 taps stay in registers) and
+// walks output positions, reading its inputs coalesced across channels.
+constexpr int kStemChannels = 256;
+
+// First stage: 3x3, stride 2, one input plane -> 256 channels, + bias, ReLU.
+__global__ void __launch_bounds__(kStemChannels)
+    stem_conv_first_kernel(const float* __restrict__ mel, const float* __restrict__ w9,
+                           const float* __restrict__ bias, float* __restrict__ out, int t_in, int f_in, int t_out,
+                           int f_out, long long positions) {
+  griddep_launch();
+  const int c = threadIdx.x;
+  float wk[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) wk[k] = w9[c * 9 + k];
+  const float b = bias[c];
+  griddep_wait();
+  for (long long pos = blockIdx.x; pos < positions; pos += gridDim.x) {
+    const int f = static_cast<int>(pos % f_out);
+    const long long wt = pos / f_out;
+    const int t = static_cast<int>(wt % t_out);
+    const long long win = wt / t_out;
+    const float* m = mel + win * t_in * f_in;
+    float acc = b;
+#pragma unroll
+    for (int kt = 0; kt < 3; ++kt) {
+      const int it = 2 * t + kt - 1;
+      if (it < 0 || it >= t_in) continue;
+#pragma unroll
+      for (int kf = 0; kf < 3; ++kf) {
+        const int jf = 2 * f + kf - 1;
+        if (jf >= 0 && jf < f_in) acc = fmaf(m[static_cast<size_t>(it) * f_in + jf], wk[kt * 3 + kf], acc);
+      }
+    }
+    out[pos * kStemChannels + c] = fmaxf(acc, 0.0f);
+  }
+}
+
+// Depthwise stage: 3x3 per channel, stride 2, + bias. With bias_in != NULL the
+// input is the raw output of the previous pointwise convolution and becomes
+// ReLU(x + bias_in) on load (the previous stage's bias and ReLU, fused here);
+// padding taps contribute zero either way.
+__global__ void __launch_bounds__(kStemChannels)
+    stem_depthwise_kernel(const float* __restrict__ in, const float* __restrict__ bias_in,
+                          const float* __restrict__ w9, const float* __restrict__ bias, float* __restrict__ out,
+                          int t_in, int f_in, int t_out, int f_out, long long positions) {
+  griddep_launch();
+  const int c = threadIdx.x;
+  float wk[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) wk[k] = w9[c * 9 + k];
+  const float b = bias[c];
+  const float bi = bias_in != nullptr ? bias_in[c] : 0.0f;
+  const bool relu_in = bias_in != nullptr;
+  griddep_wait();
+  for (long long pos = blockIdx.x; pos < positions; pos += gridDim.x) {
+    const int f = static_cast<int>(pos % f_out);
+    const long long wt = pos / f_out;
+    const int t = static_cast<int>(wt % t_out);
+    const long long win = wt / t_out;
+    const float* x = in + win * t_in * f_in * kStemChannels;
+    float acc = b;
+#pragma unroll
+    for (int kt = 0; kt < 3; ++kt) {
+      const int it = 2 * t + kt - 1;
+      if (it < 0 || it >= t_in) continue;
+#pragma unroll
+      for (int kf = 0; kf < 3; ++kf) {
+        const int jf = 2 * f + kf - 1;
+        if (jf < 0 || jf >= f_in) continue;
+        float v = x[(static_cast<size_t>(it) * f_in + jf) * kStemChannels + c];
+        if (relu_in) v = fmaxf(v + bi, 0.0f);
+        acc = fmaf(v, wk[kt * 3 + kf], acc);
+      }
+    }
+    out[pos * kStemChannels + c] = acc;
+  }
+}
+
+// ReLU(z + bias) of the last pointwise convolution, flattened channel-major:
+// flat[row][c * 16 + f] = relu(z[row][f][c] + bias[c]), TF32-rounded for the
+// output linear. One CTA per row through a padded shared-memory tile.
+__global__ void __launch_bounds__(kStemChannels)
+    stem_flatten_kernel(const float* __restrict__ z, const float* __restrict__ bias, float* __restrict__ flat,
+                        long long rows) {
+  griddep_launch();
+  __shared__ float tile[16][kStemChannels + 1];
+  const int c = threadIdx.x;
+  const float b = bias[c];
+  griddep_wait();
+  for (long long row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* zr = z + row * 16 * kStemChannels;
+#pragma unroll
+    for (int f = 0; f < 16; ++f) tile[f][c] = fmaxf(zr[f * kStemChannels + c] + b, 0.0f);
+    __syncthreads();
+    float* fr = flat + row * 16 * kStemChannels;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int j = i * kStemChannels + c;  // output index c' * 16 + f'
+      fr[j] = tf32_round(tile[j & 15][j >> 4]);
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace pq8

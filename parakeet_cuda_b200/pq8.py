@@ -32,7 +32,8 @@ ERR_LIBRARY = 1009
 
 LAYOUT_ROWS, LAYOUT_GLU, LAYOUT_GATES4 = 0, 1, 2
 EPI_NONE, EPI_RELU, EPI_SILU, EPI_GLU, EPI_RESIDUAL = 0, 1, 2, 3, 4
-FLAG_X_TF32, FLAG_OUT_TF32, ATTN_FP32 = 1, 2, 4
+FLAG_X_TF32, FLAG_OUT_TF32, FLAG_FP32_PRODUCTS = 1, 2, 4
+ATTN_FP32 = FLAG_FP32_PRODUCTS
 HEADER_BYTES, TILE_ROWS, RECORD_BYTES = 256, 128, 4352
 GEMV_MAX_M = 64          # rows the GEMV entry points take (row groups of 8 run in one launch)
 LINEAR_GEMV_MAX_M = 8    # pq8_linear's GEMV/GEMM dispatch threshold
@@ -50,6 +51,8 @@ SIGNATURES = {
     'pq8_conv_depthwise_bn_silu': ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P], _I),
     'pq8_attention_workspace_size': ([_I, _I, C.POINTER(_SZ)], _I),
     'pq8_rel_attention': ([_P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P], _I),
+    'pq8_stem_workspace_size': ([_I, _I, C.POINTER(_SZ)], _I),
+    'pq8_stem': ([_P, _I, _I] + [_P] * 13 + [_I, _P, _SZ, _P], _I),
     'pq8_pack_q8_0_part_device': ([_P, _I, _I, _I, _I, _I, _P, _P], _I),
     'pq8_dequant_q8_0': ([_P, _P, _LL, _P], _I),
     'pq8_round_tf32': ([_P, _LL, _P], _I),
@@ -108,6 +111,11 @@ class Library:
     def gemv_workspace_size(self, m: int, n: int, k: int) -> int:
         out = _SZ()
         self.call('pq8_gemv_workspace_size', m, n, k, C.byref(out))
+        return out.value
+
+    def stem_workspace_size(self, windows: int, frames: int) -> int:
+        out = _SZ()
+        self.call('pq8_stem_workspace_size', windows, frames, C.byref(out))
         return out.value
 
     def attention_workspace_size(self, windows: int, t: int) -> int:

@@ -40,6 +40,7 @@ DECODER_SCALE = (2e-4, 1.2e-3)
 # the block instead of saturating (with the config-0 range a 1024 -> 4096
 # linear alone multiplies the RMS by ~25).
 BLOCK_SCALE = (2e-4, 6e-4)
+STEM_OUT_SCALE = (1e-4, 3e-4)  # fan-in 4096: weight std ~ 1/64
 POS_EMB_MAX_LEN = 5000  # asr.encoder.pos_emb_max_len (gguf.py:95); pe has 2 * 5000 - 1 rows
 
 
@@ -130,6 +131,22 @@ def _encoder_block_schema(layer: int):
     return s
 
 
+def _stem_schema():
+    """Subsampling stem (gguf.py:104-111): a 3x3 convolution from the single mel
+    plane to 256 channels, two depthwise 3x3 + pointwise 256 x 256 stages (all
+    stride 2 in time and frequency), and the Q8_0 4096 -> 1024 output linear."""
+    s = {}
+    for i in (0, 2, 5):
+        s[f'encoder.pre_encode.conv.{i}.weight'] = ((3, 3, 1, 256), 1)
+        s[f'encoder.pre_encode.conv.{i}.bias'] = ((256,), 0)
+    for i in (3, 6):
+        s[f'encoder.pre_encode.conv.{i}.weight'] = ((1, 1, 256, 256), 1)
+        s[f'encoder.pre_encode.conv.{i}.bias'] = ((256,), 0)
+    s['encoder.pre_encode.out.weight'] = ((4096, 1024), 8)
+    s['encoder.pre_encode.out.bias'] = ((1024,), 0)
+    return s
+
+
 def relative_sinusoids(max_len: int, d: int) -> np.ndarray:
     """Relative positional table ``[2 max_len - 1, d]``: row i encodes the
     relative position ``max_len - 1 - i`` with interleaved sin / cos of
@@ -167,6 +184,7 @@ class SyntheticParakeet:
         schema = {}
         if block:
             schema['encoder.pos_enc.pe'] = ((1024, 2 * POS_EMB_MAX_LEN - 1), 0)
+            schema.update(_stem_schema())
         for layer in range(encoder_layers):
             schema.update(_encoder_layer_schema(layer))
             if block:
@@ -194,9 +212,13 @@ class SyntheticParakeet:
                 n, k = t.shape
                 lo, hi = ((BLOCK_SCALE if self.block else ENCODER_SCALE) if name.startswith('encoder.')
                           else DECODER_SCALE)
+                if name == 'encoder.pre_encode.out.weight':
+                    lo, hi = STEM_OUT_SCALE
                 data = q8_0_blocks(rng, n, k, lo, hi).reshape(-1)
             elif t.kind == 1:
-                scale = 1.0 / 3.0 if name.endswith('depthwise_conv.weight') else 1.0  # fan-in 9
+                # fan-in 9 (3 x 3 and depthwise kernels), 256 (stem pointwise), 1 (embedding)
+                scale = (1.0 / 16.0 if name.endswith(('conv.3.weight', 'conv.6.weight'))
+                         else 1.0 / 3.0 if name.endswith('.weight') and 'conv' in name else 1.0)
                 data = (scale * rng.normal(size=t.elements)).astype('<f2').view(np.uint8)
             elif name == 'encoder.pos_enc.pe':
                 data = relative_sinusoids(POS_EMB_MAX_LEN, 1024).astype('<f4').view(np.uint8).reshape(-1)

@@ -8,7 +8,9 @@ Run where the reference checkout is present (it is never read at test time):
 
 Cases (seed 31, two layers): T = 40 frames through layer 0, then layer 1 on
 layer 0's output; and T = 7 (fewer frames than the depthwise kernel's 9 taps)
-through layer 0. Inputs are N(0, 1) float32. Output: ``block.npz``.
+through layer 0. The subsampling stem (``reference.py:11-30``, ``stem``) on
+N(0, 1) mel features of 50, 17 and 1 frames. Inputs are N(0, 1) float32.
+Output: ``block.npz``.
 """
 from __future__ import annotations
 
@@ -38,6 +40,10 @@ def main(ref_root: str) -> None:
         out[f't{t}_layer0'] = y0.astype(np.float32)
         if t == 40:
             out[f't{t}_layer1'] = ref.block(y0, model, 1).astype(np.float32)
+    for frames in (50, 17, 1):
+        mel = np.random.default_rng(200 + frames).normal(size=(frames, 128)).astype(np.float32)
+        out[f'stem{frames}_mel'] = mel
+        out[f'stem{frames}_out'] = np.asarray(ref.stem(mel, model), np.float32)
     np.savez_compressed(HERE / 'block.npz', **out)
     print({k: (v.shape, float(np.sqrt((v.astype(np.float64) ** 2).mean()))) for k, v in out.items()})
 

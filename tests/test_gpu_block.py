@@ -158,3 +158,36 @@ def test_blocks_graph_replay_matches_eager(rt, model):
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(blocks.buf['x'], eager)
+
+
+def _rel_max(got, gold):
+    return float(np.abs(got.astype(np.float64) - gold).max() / np.sqrt((gold.astype(np.float64) ** 2).mean()))
+
+
+@pytest.mark.parametrize('fp32', [False, True])
+def test_stem_matches_reference_golden(rt, model, golden_dir, fp32):
+    """The reference's own stem on 50, 17 and 1 mel frames. Bar: the GEMM
+    north-star bar on the output (TF32 pointwise products and output linear),
+    max |err| <= 2e-3 x RMS; the output linear alone is TF32 with FP32 products."""
+    from parakeet_cuda_b200.block import EncoderStem
+    d = np.load(golden_dir / 'block.npz')
+    for frames in (50, 17, 1):
+        stem = EncoderStem(model, rt, 1, frames, fp32_products=fp32)
+        got = stem.forward(dev(d[f'stem{frames}_mel'])[None]).cpu().numpy()
+        err = _rel_max(got, d[f'stem{frames}_out'])
+        print(f'stem frames={frames} fp32={fp32}: max err / rms {err:.2e}')
+        assert err <= 2e-3, err
+    assert rt.device_status() == 0
+
+
+def test_stem_windows_are_independent(rt, model):
+    from oracle import stem as ostem
+    from parakeet_cuda_b200.block import EncoderStem
+    frames = 45
+    mel = np.random.default_rng(11).normal(size=(3, frames, 128)).astype(np.float32)
+    many = EncoderStem(model, rt, 3, frames).forward(dev(mel)).cpu().numpy()
+    t = many.shape[0] // 3
+    for w in range(3):
+        one = EncoderStem(model, rt, 1, frames).forward(dev(mel[w:w + 1])).cpu().numpy()
+        np.testing.assert_allclose(many[w * t:(w + 1) * t], one, atol=1e-6, rtol=0)
+        assert _rel_max(one, ostem.stem(mel[w], model)) <= 2e-3

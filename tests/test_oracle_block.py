@@ -32,3 +32,10 @@ def test_rel_shift_index():
     bd = qv @ p.transpose(0, 2, 1)
     trick = np.pad(bd, ((0, 0), (0, 0), (1, 0))).reshape(h, 2 * t, t)[:, 1:, :].reshape(h, t, 2 * t - 1)[:, :, :t]
     np.testing.assert_allclose(s, (qu @ k.transpose(0, 2, 1) + trick) / np.sqrt(128), atol=1e-12)
+
+
+def test_stem_oracle_matches_reference(model, golden_dir):
+    from oracle import stem as ostem
+    d = np.load(golden_dir / 'block.npz')
+    for frames in (50, 17, 1):
+        np.testing.assert_allclose(ostem.stem(d[f'stem{frames}_mel'], model), d[f'stem{frames}_out'], atol=5e-6, rtol=0)
