@@ -1040,7 +1040,7 @@ extern "C" int pq8_stem(const float* mel, int windows, int frames, const float* 
                         const float* b2, const float* w3, const float* b3, const float* w5, const float* b5,
                         const float* w6, const float* b6, const void* w_out, const float* b_out, float* out, int flags,
                         void* workspace, size_t workspace_bytes, void* stream) {
-  if (windows < 1 || frames < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (windows < 1 || windows > 65535 || frames < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
   if (mel == nullptr || w0 == nullptr || b0 == nullptr || w2 == nullptr || b2 == nullptr || w3 == nullptr ||
       b3 == nullptr || w5 == nullptr || b5 == nullptr || w6 == nullptr || b6 == nullptr || w_out == nullptr ||
       out == nullptr)
@@ -1060,14 +1060,16 @@ extern "C" int pq8_stem(const float* mel, int windows, int frames, const float* 
   float* d = reinterpret_cast<float*>(base + sp.d);
   float* z = reinterpret_cast<float*>(base + sp.z);
   float* flat = reinterpret_cast<float*>(base + sp.flat);
-  const long long p1 = static_cast<long long>(windows) * sp.t1 * 64, p2 = static_cast<long long>(windows) * sp.t2 * 32,
-                  p3 = static_cast<long long>(windows) * sp.t3 * 16;
+  // positions of the two pointwise products
+  const long long p2 = static_cast<long long>(windows) * sp.t2 * 32, p3 = static_cast<long long>(windows) * sp.t3 * 16;
   const float* no_bias = nullptr;
-  cudaError_t e = launch_pdl(stem_conv_first_kernel, dim3(stem_grid(p1, ds->sms)), dim3(kStemChannels), 0, st, mel, w0,
-                             b0, a, frames, 128, sp.t1, 64, p1);
+  auto frame_tiles = [](int t) { return static_cast<unsigned>((t + kStemFrames - 1) / kStemFrames); };
+  cudaError_t e = launch_pdl(stem_conv_first_kernel, dim3(frame_tiles(sp.t1), windows), dim3(kStemChannels),
+                             sizeof(float) * (2 * kStemFrames + 1) * (128 + 2), st, mel, w0, b0, a, frames, 128, sp.t1,
+                             64);
   if (e == cudaSuccess)
-    e = launch_pdl(stem_depthwise_kernel, dim3(stem_grid(p2, ds->sms)), dim3(kStemChannels), 0, st,
-                   static_cast<const float*>(a), no_bias, w2, b2, b, sp.t1, 64, sp.t2, 32, p2);
+    e = launch_pdl(stem_depthwise_kernel, dim3(frame_tiles(sp.t2) * 32, windows), dim3(kStemChannels), 0, st,
+                   static_cast<const float*>(a), no_bias, w2, b2, b, sp.t1, 64, sp.t2, 32);
   if (e != cudaSuccess) return to_code(e);
   {
     std::lock_guard<std::mutex> lock(ds->blas_mutex);
@@ -1083,8 +1085,8 @@ extern "C" int pq8_stem(const float* mel, int windows, int frames, const float* 
     if (cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, 256, static_cast<int>(p2), 256, &one, w3, CUDA_R_32F, 256, b,
                      CUDA_R_32F, 256, &zero, c, CUDA_R_32F, 256, ct, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
       return PQ8_ERR_LIBRARY;
-    e = launch_pdl(stem_depthwise_kernel, dim3(stem_grid(p3, ds->sms)), dim3(kStemChannels), 0, st,
-                   static_cast<const float*>(c), b3, w5, b5, d, sp.t2, 32, sp.t3, 16, p3);
+    e = launch_pdl(stem_depthwise_kernel, dim3(frame_tiles(sp.t3) * 16, windows), dim3(kStemChannels), 0, st,
+                   static_cast<const float*>(c), b3, w5, b5, d, sp.t2, 32, sp.t3, 16);
     if (e != cudaSuccess) return to_code(e);
     if (cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, 256, static_cast<int>(p3), 256, &one, w6, CUDA_R_32F, 256, d,
                      CUDA_R_32F, 256, &zero, z, CUDA_R_32F, 256, ct, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)

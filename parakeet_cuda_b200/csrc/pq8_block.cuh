@@ -234,77 +234,106 @@ __global__ void attention_pointers_kernel(const float* qkv, const float* qu, con
 // walks output positions, reading its inputs coalesced across channels.
 constexpr int kStemChannels = 256;
 
+// Output frames per CTA (first stage) or per thread (depthwise stages).
+constexpr int kStemFrames = 8;
+
 // First stage: 3x3, stride 2, one input plane -> 256 channels, + bias, ReLU.
+// A CTA covers kStemFrames output frames x all f_out frequencies of one window:
+// it stages the 2 kStemFrames + 1 mel rows they read in shared memory, then
+// thread c computes channel c at every position (taps read as broadcasts) and
+// the CTA writes 1 KB per position.
 __global__ void __launch_bounds__(kStemChannels)
     stem_conv_first_kernel(const float* __restrict__ mel, const float* __restrict__ w9,
                            const float* __restrict__ bias, float* __restrict__ out, int t_in, int f_in, int t_out,
-                           int f_out, long long positions) {
+                           int f_out) {
   griddep_launch();
+  extern __shared__ float rows_s[];  // [2 kStemFrames + 1][f_in + 2], zero-padded
   const int c = threadIdx.x;
+  const int win = blockIdx.y, t0 = blockIdx.x * kStemFrames;
   float wk[9];
 #pragma unroll
   for (int k = 0; k < 9; ++k) wk[k] = w9[c * 9 + k];
   const float b = bias[c];
   griddep_wait();
-  for (long long pos = blockIdx.x; pos < positions; pos += gridDim.x) {
-    const int f = static_cast<int>(pos % f_out);
-    const long long wt = pos / f_out;
-    const int t = static_cast<int>(wt % t_out);
-    const long long win = wt / t_out;
-    const float* m = mel + win * t_in * f_in;
-    float acc = b;
+  const int width = f_in + 2;
+  const float* m = mel + static_cast<size_t>(win) * t_in * f_in;
+  for (int i = c; i < (2 * kStemFrames + 1) * width; i += kStemChannels) {
+    const int rr = i / width, jf = i % width - 1, it = 2 * t0 - 1 + rr;
+    rows_s[i] = (it >= 0 && it < t_in && jf >= 0 && jf < f_in) ? m[static_cast<size_t>(it) * f_in + jf] : 0.0f;
+  }
+  __syncthreads();
+  const int t1 = min(t_out, t0 + kStemFrames);
+  for (int t = t0; t < t1; ++t) {
+    const float* r0 = rows_s + (2 * (t - t0)) * width;  // input row 2t - 1
+    float* o = out + ((static_cast<size_t>(win) * t_out + t) * f_out) * kStemChannels + c;
+    for (int f = 0; f < f_out; ++f) {
+      float acc = b;
 #pragma unroll
-    for (int kt = 0; kt < 3; ++kt) {
-      const int it = 2 * t + kt - 1;
-      if (it < 0 || it >= t_in) continue;
+      for (int kt = 0; kt < 3; ++kt)
 #pragma unroll
-      for (int kf = 0; kf < 3; ++kf) {
-        const int jf = 2 * f + kf - 1;
-        if (jf >= 0 && jf < f_in) acc = fmaf(m[static_cast<size_t>(it) * f_in + jf], wk[kt * 3 + kf], acc);
-      }
+        for (int kf = 0; kf < 3; ++kf) acc = fmaf(r0[kt * width + 2 * f + kf], wk[kt * 3 + kf], acc);
+      o[static_cast<size_t>(f) * kStemChannels] = fmaxf(acc, 0.0f);
     }
-    out[pos * kStemChannels + c] = fmaxf(acc, 0.0f);
   }
 }
 
 // Depthwise stage: 3x3 per channel, stride 2, + bias. With bias_in != NULL the
 // input is the raw output of the previous pointwise convolution and becomes
 // ReLU(x + bias_in) on load (the previous stage's bias and ReLU, fused here);
-// padding taps contribute zero either way.
+// padding taps contribute zero either way. Thread c of a CTA computes channel
+// c of kStemFrames consecutive output frames at one frequency: it issues the
+// loads of all 3 x (2 kStemFrames + 1) input taps it needs before using any.
 __global__ void __launch_bounds__(kStemChannels)
     stem_depthwise_kernel(const float* __restrict__ in, const float* __restrict__ bias_in,
                           const float* __restrict__ w9, const float* __restrict__ bias, float* __restrict__ out,
-                          int t_in, int f_in, int t_out, int f_out, long long positions) {
+                          int t_in, int f_in, int t_out, int f_out) {
   griddep_launch();
   const int c = threadIdx.x;
+  const int f = blockIdx.x % f_out, t0 = (blockIdx.x / f_out) * kStemFrames, win = blockIdx.y;
   float wk[9];
 #pragma unroll
   for (int k = 0; k < 9; ++k) wk[k] = w9[c * 9 + k];
   const float b = bias[c];
-  const float bi = bias_in != nullptr ? bias_in[c] : 0.0f;
   const bool relu_in = bias_in != nullptr;
+  const float bi = relu_in ? bias_in[c] : 0.0f;
   griddep_wait();
-  for (long long pos = blockIdx.x; pos < positions; pos += gridDim.x) {
-    const int f = static_cast<int>(pos % f_out);
-    const long long wt = pos / f_out;
-    const int t = static_cast<int>(wt % t_out);
-    const long long win = wt / t_out;
-    const float* x = in + win * t_in * f_in * kStemChannels;
-    float acc = b;
+  const float* x = in + static_cast<size_t>(win) * t_in * f_in * kStemChannels + c;
+  constexpr int kRows = 2 * kStemFrames + 1;
+  float v[kRows][3];
 #pragma unroll
-    for (int kt = 0; kt < 3; ++kt) {
-      const int it = 2 * t + kt - 1;
-      if (it < 0 || it >= t_in) continue;
+  for (int rr = 0; rr < kRows; ++rr) {
+    const int it = 2 * t0 - 1 + rr;
+#pragma unroll
+    for (int kf = 0; kf < 3; ++kf) {
+      const int jf = 2 * f + kf - 1;
+      v[rr][kf] = (it >= 0 && it < t_in && jf >= 0 && jf < f_in)
+                      ? x[(static_cast<size_t>(it) * f_in + jf) * kStemChannels]
+                      : 0.0f;
+    }
+  }
+  if (relu_in) {
+#pragma unroll
+    for (int rr = 0; rr < kRows; ++rr) {
+      const int it = 2 * t0 - 1 + rr;
 #pragma unroll
       for (int kf = 0; kf < 3; ++kf) {
         const int jf = 2 * f + kf - 1;
-        if (jf < 0 || jf >= f_in) continue;
-        float v = x[(static_cast<size_t>(it) * f_in + jf) * kStemChannels + c];
-        if (relu_in) v = fmaxf(v + bi, 0.0f);
-        acc = fmaf(v, wk[kt * 3 + kf], acc);
+        const bool inside = it >= 0 && it < t_in && jf >= 0 && jf < f_in;
+        v[rr][kf] = inside ? fmaxf(v[rr][kf] + bi, 0.0f) : 0.0f;
       }
     }
-    out[pos * kStemChannels + c] = acc;
+  }
+  float* o = out + ((static_cast<size_t>(win) * t_out) * f_out + f) * kStemChannels + c;
+#pragma unroll
+  for (int q = 0; q < kStemFrames; ++q) {
+    const int t = t0 + q;
+    if (t >= t_out) break;
+    float acc = b;
+#pragma unroll
+    for (int kt = 0; kt < 3; ++kt)
+#pragma unroll
+      for (int kf = 0; kf < 3; ++kf) acc = fmaf(v[2 * q + kt][kf], wk[kt * 3 + kf], acc);
+    o[static_cast<size_t>(t) * f_out * kStemChannels] = acc;
   }
 }
 
