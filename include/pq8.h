@@ -277,10 +277,12 @@ PQ8_API int pq8_conv_depthwise_bn_silu(const float* x, const uint16_t* w9_f16, c
  * the positional rows pe[limit - t : limit + t - 1], shared by all windows;
  * pos_bias_u / _v: float[1024] (head-major); ctx: float[windows * t][1024],
  * heads merged. Scores ((q + u) k + (q + v) p_{t-1+j-i}) / sqrt(128), softmax
- * over keys, context = probabilities x V. The three batched products go to
- * cuBLAS (TF32 tensor cores, or FP32 with PQ8_ATTN_FP32); the biases, the
- * shift and the softmax are pq8 kernels. PQ8_FLAG_OUT_TF32 rounds ctx for
- * linear_out. Replaces query_bias, rel_scores, softmax and the attention
+ * over keys, context = probabilities x V. By default one fused kernel does
+ * everything on chip (tensor-core products with FP16 operands, which keep
+ * TF32's 11-bit significand, FP32 accumulation, online softmax); with
+ * PQ8_FLAG_FP32_PRODUCTS the three products are FP32 cuBLAS GEMMs around pq8
+ * bias / shift / softmax kernels (an exactness reference, slower).
+ * PQ8_FLAG_OUT_TF32 rounds ctx for linear_out. Replaces query_bias, rel_scores, softmax and the attention
  * GEMMs of encoder.py:95-112 (runtime.cu:115-137). */
 PQ8_API int pq8_attention_workspace_size(int windows, int t, size_t* bytes);
 PQ8_API int pq8_rel_attention(const float* qkv, const float* pos, const float* pos_bias_u, const float* pos_bias_v,

@@ -913,7 +913,7 @@ extern "C" int pq8_attention_workspace_size(int windows, int t, size_t* bytes) {
 extern "C" int pq8_rel_attention(const float* qkv, const float* pos, const float* pos_bias_u,
                                  const float* pos_bias_v, float* ctx, int windows, int t, int flags, void* workspace,
                                  size_t workspace_bytes, void* stream) {
-  if (windows < 1 || t < 1 || t > 8192) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (windows < 1 || windows > 65535 || t < 1 || t > 8192) return PQ8_ERR_UNSUPPORTED_SHAPE;
   if (qkv == nullptr || pos == nullptr || pos_bias_u == nullptr || pos_bias_v == nullptr || ctx == nullptr)
     return PQ8_ERR_INVALID_ARGUMENT;
   if (flags & ~(PQ8_FLAG_OUT_TF32 | PQ8_ATTN_FP32)) return PQ8_ERR_INVALID_ARGUMENT;
@@ -927,6 +927,23 @@ extern "C" int pq8_rel_attention(const float* qkv, const float* pos, const float
   int rc = device_state(&ds);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!(flags & PQ8_FLAG_FP32_PRODUCTS)) {
+    // Fused kernel: scores and probabilities stay on chip.
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      if (!ds->attr_set[12]) {
+        cudaError_t e = cudaFuncSetAttribute(rel_attention_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kAttSmemBytes));
+        if (e != cudaSuccess) return to_code(e);
+        ds->attr_set[12] = true;
+      }
+    }
+    const dim3 grid((t + kAttQ - 1) / kAttQ, 8, windows);
+    cudaError_t e = launch_pdl(rel_attention_fused_kernel, grid, dim3(128), kAttSmemBytes, st, qkv, pos, pos_bias_u,
+                               pos_bias_v, ctx, t, (flags & PQ8_FLAG_OUT_TF32) ? 1 : 0);
+    if (e != cudaSuccess) return to_code(e);
+    return to_code(cudaGetLastError());
+  }
   auto* base = static_cast<unsigned char*>(workspace);
   float* qu = reinterpret_cast<float*>(base + a.qu);
   float* qv = reinterpret_cast<float*>(base + a.qv);

@@ -5,8 +5,9 @@ float64 oracle (oracle/block.py).
 
 Tolerances: the LayerNorm and the depthwise kernel are FP32 arithmetic
 (1e-5 absolute on O(1) values, 1 TF32 ulp when the output is TF32-rounded).
-The attention with FP32 products is checked at 2e-5; with TF32 products at
-the north-star GEMM bar (max |err| <= 2e-3 x RMS). A whole block chains 11
+The attention with FP32 products (cuBLAS) is checked at 2e-5; the fused
+kernel (FP16 operands: TF32's significand, FP32 accumulation) at the
+north-star GEMM bar (max |err| <= 2e-3 x RMS). A whole block chains 11
 TF32 GEMMs and the attention, then LayerNorms the result: its bar is
 max |err| <= 1e-2 and RMS error <= 2e-3 on the unit-RMS output.
 """
