@@ -219,11 +219,10 @@ __global__ void rel_shift_softmax_kernel(float* __restrict__ ac, const float* __
 // no score or probability touches HBM.
 constexpr int kAttQ = 64, kAttK = 64, kAttD = 128;
 constexpr int kAttBand = 128;             // positional rows of one (query tile, key tile): 2 * 64 - 1, padded
-constexpr int kAttLd = kAttD + 8;         // fp16 row stride of K and the band (16-byte pad)
-constexpr int kAttVtLd = kAttK + 8;       // fp16 row stride of V transposed
+constexpr int kAttLd = kAttD + 8;         // fp16 row stride of K, V and the band (16-byte pad)
 constexpr int kAttWarpBand = 80;          // band columns one warp needs (16 queries x 64 keys)
 constexpr int kAttScratchLd = kAttWarpBand + 4;
-constexpr size_t kAttSmemBytes = sizeof(__half) * (kAttK * kAttLd + kAttD * kAttVtLd + kAttBand * kAttLd) +
+constexpr size_t kAttSmemBytes = sizeof(__half) * (2 * kAttK * kAttLd + kAttBand * kAttLd) +
                                  sizeof(float) * 4 * 16 * kAttScratchLd;
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
@@ -238,6 +237,16 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// B fragment (16 x 8, k = rows of a row-major [k][n] shared-memory tile) via
+// ldmatrix with transpose: lanes 0-15 give the addresses of rows k0 .. k0+15
+// at column n0 (16-byte aligned); lane l receives M[k0+2(l%4)+{0,1}][n0+l/4]
+// and M[k0+8+2(l%4)+{0,1}][n0+l/4].
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& b0, uint32_t& b1, const __half* row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(b0), "=r"(b1)
+               : "r"(smem_addr(row_addr)));
+}
+
 __global__ void __launch_bounds__(128)
     rel_attention_fused_kernel(const float* __restrict__ qkv, const float* __restrict__ pos,
                                const float* __restrict__ pos_bias_u, const float* __restrict__ pos_bias_v,
@@ -245,8 +254,8 @@ __global__ void __launch_bounds__(128)
   griddep_launch();
   extern __shared__ __align__(16) unsigned char att_smem[];
   __half* k_s = reinterpret_cast<__half*>(att_smem);               // [64 keys][136]
-  __half* vt_s = k_s + kAttK * kAttLd;                              // [128 d][72]
-  __half* band_s = vt_s + kAttD * kAttVtLd;                         // [128 band rows][136]
+  __half* v_s = k_s + kAttK * kAttLd;                               // [64 keys][136]
+  __half* band_s = v_s + kAttK * kAttLd;                            // [128 band rows][136]
   float* scratch = reinterpret_cast<float*>(band_s + kAttBand * kAttLd);  // [4 warps][16][84]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
   const int i0 = blockIdx.x * kAttQ, h = blockIdx.y, win = blockIdx.z;
@@ -285,7 +294,7 @@ __global__ void __launch_bounds__(128)
 
   for (int j0 = 0; j0 < t; j0 += kAttK) {
     __syncthreads();  // the previous tile's operands are no longer read
-    // Stage K [key][d], V transposed [d][key] and the positional band [row][d] as FP16.
+    // Stage K, V [key][d] and the positional band [row][d] as FP16.
     for (int idx = tid; idx < kAttK * (kAttD / 4); idx += 128) {
       const int key = idx >> 5, d = (idx & 31) * 4, j = j0 + key;
       float4 kv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vv = kv;
@@ -295,10 +304,7 @@ __global__ void __launch_bounds__(128)
         vv = *reinterpret_cast<const float4*>(r + 2048);
       }
       *reinterpret_cast<uint2*>(k_s + key * kAttLd + d) = make_uint2(pack_half2(kv.x, kv.y), pack_half2(kv.z, kv.w));
-      vt_s[(d + 0) * kAttVtLd + key] = __float2half_rn(vv.x);
-      vt_s[(d + 1) * kAttVtLd + key] = __float2half_rn(vv.y);
-      vt_s[(d + 2) * kAttVtLd + key] = __float2half_rn(vv.z);
-      vt_s[(d + 3) * kAttVtLd + key] = __float2half_rn(vv.w);
+      *reinterpret_cast<uint2*>(v_s + key * kAttLd + d) = make_uint2(pack_half2(vv.x, vv.y), pack_half2(vv.z, vv.w));
     }
     const int pb = t - 64 + j0 - i0;  // position of band row 0 (query i0 + 63, key j0)
     for (int idx = tid; idx < kAttBand * (kAttD / 4); idx += 128) {
@@ -379,12 +385,14 @@ __global__ void __launch_bounds__(128)
       pa[n >> 1][(n & 1) * 2] = pack_half2(p0, p1);
       pa[n >> 1][(n & 1) * 2 + 1] = pack_half2(p2, p3);
     }
+    const int lrow = lane & 15;  // ldmatrix row address of this lane (lanes 16-31: ignored, kept valid)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
-        const __half* vr = vt_s + (8 * n + g) * kAttVtLd + kk * 16 + 2 * q;
-        mma_16816(o[n], pa[kk], *reinterpret_cast<const uint32_t*>(vr), *reinterpret_cast<const uint32_t*>(vr + 8));
+        uint32_t b0, b1;
+        ldmatrix_x2_trans(b0, b1, v_s + (kk * 16 + lrow) * kAttLd + 8 * n);
+        mma_16816(o[n], pa[kk], b0, b1);
       }
     __syncwarp();  // the scratch is rewritten by the next tile
   }
