@@ -12,7 +12,7 @@ FFN1 / FFN2            ``pq8_gemm`` + SiLU, ``pq8_gemm`` with ``x += 0.5 y``
 Q, K, V                one ``pq8_gemm`` on the packed ``[3072, 1024]`` weight
 linear_pos             one ``pq8_gemm`` on the ``2t - 1`` positional rows, once per
                        layer for all windows (their positions are identical)
-attention              ``pq8_rel_attention`` (biases, shift, softmax; products on cuBLAS)
+attention              ``pq8_rel_attention`` (one fused kernel: products, shift, softmax)
 linear_out             ``pq8_gemm`` with ``x += y``
 conv module            ``pq8_gemm`` + GLU, ``pq8_conv_depthwise_bn_silu``,
                        ``pq8_gemm`` with ``x += y``

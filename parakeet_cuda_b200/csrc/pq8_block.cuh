@@ -1,11 +1,12 @@
 // The FastConformer block around the Q8_0 linears (parakeet_cuda/reference.py:33-66):
 // LayerNorm, the conv module's depthwise convolution with BatchNorm and SiLU,
-// and the relative-position attention's query biases and shifted softmax. The
-// attention's three batched products are plain GEMMs and go to cuBLAS
-// (pq8_api.cu); the linears are pq8_gemm.
+// the relative-position attention (fused; with FP32 products the three
+// batched products go to cuBLAS around the bias / shift-softmax kernels), and
+// the subsampling stem. The linears are pq8_gemm.
 //
-// All of these are HBM-bound elementwise / row-reduction kernels: each reads
-// its input once and writes its output once, with 16-byte accesses.
+// LayerNorm, the depthwise convolution and the stem's stages are HBM-bound:
+// each reads its input once and writes its output once, coalesced across
+// channels.
 #pragma once
 
 #include <cuda_fp16.h>
