@@ -32,50 +32,58 @@ __device__ __forceinline__ float4 tf32_round4(float4 v) {
 }
 __device__ __forceinline__ float silu_exact(float z) { return z / (1.0f + expf(-z)); }
 
-// LayerNorm over rows of width 128 * V: one warp per row, V float4 per lane
-// (a warp reads 512 contiguous bytes per access). Two passes over the values
-// held in registers: mean, then the mean of squared deviations
-// (runtime.cu:38-48 sums the deviations the same way). Optionally rounds the
-// output to TF32 (to nearest, ties away) so that the GEMM reading it skips
-// its own rounding pass (PQ8_FLAG_X_TF32).
+// LayerNorm over rows of width 128 * V: a warp per row at a time, V float4
+// per lane (a warp reads 512 contiguous bytes per access). The weight and
+// bias are loaded once per warp, before waiting for the previous kernel, and
+// the warp walks rows with a grid stride, so only the row itself is on the
+// critical path. Two passes over the values held in registers: mean, then the
+// mean of squared deviations (runtime.cu:38-48 sums the deviations the same
+// way). Optionally rounds the output to TF32 (to nearest, ties away) so that
+// the GEMM reading it skips its own rounding pass (PQ8_FLAG_X_TF32).
 template <int V>
 __global__ void layer_norm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                   const float* __restrict__ b, float* __restrict__ y, int rows, int round_out) {
   griddep_launch();
-  griddep_wait();  // x is the previous kernel's output
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
   constexpr int kWidth = 128 * V;
-  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * kWidth);
-  float4 v[V];
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < V; ++i) {
-    v[i] = xr[i * 32 + lane];
-    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  }
-  const float mean = warp_sum(s) * (1.0f / kWidth);
-  float q = 0.0f;
-#pragma unroll
-  for (int i = 0; i < V; ++i) {
-    v[i].x -= mean;
-    v[i].y -= mean;
-    v[i].z -= mean;
-    v[i].w -= mean;
-    q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
-  }
-  const float inv = rsqrtf(warp_sum(q) * (1.0f / kWidth) + kLayerNormEps);
+  float4 g[V], h[V];
   const float4* w4 = reinterpret_cast<const float4*>(w);
   const float4* b4 = reinterpret_cast<const float4*>(b);
-  float4* yr = reinterpret_cast<float4*>(y + static_cast<size_t>(row) * kWidth);
 #pragma unroll
   for (int i = 0; i < V; ++i) {
-    const float4 g = w4[i * 32 + lane], h = b4[i * 32 + lane];
-    float4 o = make_float4(v[i].x * inv * g.x + h.x, v[i].y * inv * g.y + h.y, v[i].z * inv * g.z + h.z,
-                           v[i].w * inv * g.w + h.w);
-    if (round_out) o = tf32_round4(o);
-    yr[i * 32 + lane] = o;
+    g[i] = w4[i * 32 + lane];
+    h[i] = b4[i * 32 + lane];
+  }
+  griddep_wait();  // x is the previous kernel's output
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * kWidth);
+    float4 v[V];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      v[i] = xr[i * 32 + lane];
+      s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+    const float mean = warp_sum(s) * (1.0f / kWidth);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      v[i].x -= mean;
+      v[i].y -= mean;
+      v[i].z -= mean;
+      v[i].w -= mean;
+      q += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+    }
+    const float inv = rsqrtf(warp_sum(q) * (1.0f / kWidth) + kLayerNormEps);
+    float4* yr = reinterpret_cast<float4*>(y + static_cast<size_t>(row) * kWidth);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float4 o = make_float4(v[i].x * inv * g[i].x + h[i].x, v[i].y * inv * g[i].y + h[i].y,
+                             v[i].z * inv * g[i].z + h[i].z, v[i].w * inv * g[i].w + h[i].w);
+      if (round_out) o = tf32_round4(o);
+      yr[i * 32 + lane] = o;
+    }
   }
 }
 
