@@ -192,3 +192,25 @@ def test_stem_windows_are_independent(rt, model):
         one = EncoderStem(model, rt, 1, frames).forward(dev(mel[w:w + 1])).cpu().numpy()
         np.testing.assert_allclose(many[w * t:(w + 1) * t], one, atol=1e-6, rtol=0)
         assert _rel_max(one, ostem.stem(mel[w], model)) <= 2e-3
+
+
+@pytest.mark.parametrize('windows,t', [(1, 1), (2, 1), (1, 2), (3, 65)])
+def test_blocks_edge_lengths(rt, model, windows, t):
+    """One-frame windows (one key, one positional row), two frames, and a window
+    one frame past a 64-query tile, against the float64 oracle."""
+    x = np.random.default_rng(40 + t).normal(size=(windows * t, 1024)).astype(np.float32)
+    got = EncoderBlocks(model, rt, windows, t, layers=1).forward(dev(x)).cpu().numpy()
+    mx, rms = _block_errors(got, ob.blocks(x, model, [0], windows=windows))
+    assert mx <= 1e-2 and rms <= 2e-3, (mx, rms)
+    assert rt.device_status() == 0
+
+
+@pytest.mark.parametrize('frames', [2, 3, 8, 9])
+def test_stem_edge_lengths(rt, model, frames):
+    from oracle import stem as ostem
+    from parakeet_cuda_b200.block import EncoderStem
+    mel = np.random.default_rng(60 + frames).normal(size=(2, frames, 128)).astype(np.float32)
+    got = EncoderStem(model, rt, 2, frames).forward(dev(mel)).cpu().numpy()
+    t = got.shape[0] // 2
+    for w in range(2):
+        assert _rel_max(got[w * t:(w + 1) * t], ostem.stem(mel[w], model)) <= 2e-3
