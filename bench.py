@@ -50,6 +50,7 @@ def parse():
     ap.add_argument('--layers', type=int, default=24)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
+    ap.add_argument('--tdt-batches', default='1,64', help='decode batch sizes of the tdt extra')
     ap.add_argument('--extras', default='gemv,cublas,tdt,sweep,load,block',
                     help='comma list of side measurements to run (gemv, cublas, tdt, sweep, load, block)')
     return ap.parse_args()
@@ -299,7 +300,7 @@ def run_gpu(args):
         if 'cublas' in wanted:
             extras['tf32_cublas_tflops'] = cublas_tf32(torch)
         if 'tdt' in wanted:
-            extras['tdt'] = tdt_measure(torch, rt)
+            extras['tdt'] = tdt_measure(torch, rt, [int(b) for b in args.tdt_batches.split(',')])
         if 'sweep' in wanted:
             extras['sweep'] = sweep_measure(torch, rt)
         if 'load' in wanted:
@@ -431,7 +432,7 @@ def gemv_measure(torch, rt, stack):
     return out
 
 
-def tdt_measure(torch, rt):
+def tdt_measure(torch, rt, batches=(1, 64)):
     """greedy TDT loop with random weights, ~1000 decode steps per stream,
     batch 1 and batch 64 (lock-step; one joint launch for all streams per step)."""
     import time
@@ -445,7 +446,7 @@ def tdt_measure(torch, rt):
     w_enc, b_enc = rt.weight('joint.enc.weight'), rt.weight('joint.enc.bias').reshape(-1)
     frames = 1150   # ~1000 joint calls per stream with these weights
     out = {'frames_per_stream': frames, 'durations': [0, 1, 2, 3, 4]}
-    for batch in (1, 64):
+    for batch in batches:
         enc = torch.randn(batch * frames, 1024, device=rt.device)      # encoder outputs ~ N(0, 1)
         t0 = time.perf_counter()
         projected = rt.gemm(enc, w_enc, bias=b_enc, epilogue=EPI_NONE)  # joint.enc projection (Encoder.project)
