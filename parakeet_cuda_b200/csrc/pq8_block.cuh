@@ -302,6 +302,10 @@ __global__ void __launch_bounds__(128)
   const float kScaleLog2 = 1.4426950408889634f * rsqrtf(128.0f);  // 1/sqrt(128) in base 2
 
   for (int j0 = 0; j0 < t; j0 += kAttK) {
+    // The positional band is a ring of 128 rows: band row b of this tile is in
+    // slot (ring + b) % 128, and the first 64 rows of a tile are the last 64 of
+    // the tile before, so after the first tile only 64 rows are loaded.
+    const int ring = j0 & (kAttBand - 1);
     __syncthreads();  // the previous tile's operands are no longer read
     // Stage K, V [key][d] and the positional band [row][d] as FP16.
     for (int idx = tid; idx < kAttK * (kAttD / 4); idx += 128) {
@@ -316,11 +320,13 @@ __global__ void __launch_bounds__(128)
       *reinterpret_cast<uint2*>(v_s + key * kAttLd + d) = make_uint2(pack_half2(vv.x, vv.y), pack_half2(vv.z, vv.w));
     }
     const int pb = t - 64 + j0 - i0;  // position of band row 0 (query i0 + 63, key j0)
-    for (int idx = tid; idx < kAttBand * (kAttD / 4); idx += 128) {
+    const int first_row = j0 == 0 ? 0 : kAttBand - kAttK;  // rows not already in the ring
+    for (int idx = tid + first_row * (kAttD / 4); idx < kAttBand * (kAttD / 4); idx += 128) {
       const int r = idx >> 5, d = (idx & 31) * 4, p = pb + r;
       float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (p >= 0 && p < 2 * t - 1) pv = *reinterpret_cast<const float4*>(pos + static_cast<size_t>(p) * 1024 + h * kAttD + d);
-      *reinterpret_cast<uint2*>(band_s + r * kAttLd + d) = make_uint2(pack_half2(pv.x, pv.y), pack_half2(pv.z, pv.w));
+      *reinterpret_cast<uint2*>(band_s + ((ring + r) & (kAttBand - 1)) * kAttLd + d) =
+          make_uint2(pack_half2(pv.x, pv.y), pack_half2(pv.z, pv.w));
     }
     __syncthreads();
 
@@ -333,7 +339,7 @@ __global__ void __launch_bounds__(128)
       for (int ks = 0; ks < 8; ++ks)
 #pragma unroll
         for (int n = 0; n < 10; ++n) {
-          const __half* br = band_s + (q0w + 8 * n + g) * kAttLd + ks * 16 + 2 * q;
+          const __half* br = band_s + ((ring + q0w + 8 * n + g) & (kAttBand - 1)) * kAttLd + ks * 16 + 2 * q;
           mma_16816(bd[n], qv[ks], *reinterpret_cast<const uint32_t*>(br), *reinterpret_cast<const uint32_t*>(br + 8));
         }
 #pragma unroll
