@@ -22,8 +22,7 @@ import numpy as np
 import torch
 
 from . import pq8
-from .pq8 import (EPI_GLU, EPI_NONE, EPI_RESIDUAL, FLAG_X_TF32, LINEAR_GEMV_MAX_M, LAYOUT_GATES4, LAYOUT_GLU,
-                  LAYOUT_ROWS)
+from .pq8 import EPI_GLU, EPI_NONE, LINEAR_GEMV_MAX_M, LAYOUT_GATES4, LAYOUT_GLU, LAYOUT_ROWS
 
 MIB = 1 << 20
 
