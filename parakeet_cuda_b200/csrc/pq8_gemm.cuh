@@ -393,14 +393,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
       const int n_tile = (tile / p.m_tiles) * C::kCtas + static_cast<int>(rank), m_tile = tile % p.m_tiles;
       const int acc = local % ACC;
-      if (!mbar_wait(&acc_full[acc], (local / ACC) & 1, abort_flag, p.status)) break;
-      tc_fence_after();
       RowMap rm;
       const bool valid = map_row(p.layout, p.n, n_tile * kTileRows + r, rm);
       const float b = (p.bias != nullptr && valid) ? p.bias[rm.src] : 0.0f;
       const bool store_lane = valid && (!glu || lane < 16);
       float* ycol = p.y + rm.col;
       const float* rcol = p.resid + rm.col;
+      const bool resid = p.epi == PQ8_EPI_RESIDUAL;
+      // Residual rows are loaded into out[] one chunk ahead: the tile's first
+      // chunk before the accumulator is waited for, each next chunk as soon as
+      // the previous one has been staged, so their latency is off the critical
+      // path (they are other rows than any store still in flight).
+      float out[E];
+      auto load_resid = [&](int m0) {
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+          out[j] = (store_lane && m0 + j < p.m) ? rcol[(size_t)(m0 + j) * p.out_cols] : 0.0f;
+      };
+      if (resid) load_resid(m_tile * BN + half * kChunks * E);
+      if (!mbar_wait(&acc_full[acc], (local / ACC) & 1, abort_flag, p.status)) break;
+      tc_fence_after();
 #pragma unroll 1
       for (int cc = 0; cc < kChunks; ++cc, ++chunk_seq) {
         const int c = half * kChunks + cc;
@@ -410,11 +422,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
         tmem_wait_ld();
         const int cnt = min(E, p.m - m0);  // warp-uniform
-        float out[E];
-        if (p.epi == PQ8_EPI_RESIDUAL) {
-#pragma unroll
-          for (int j = 0; j < E; ++j)
-            out[j] = (store_lane && j < cnt) ? rcol[(size_t)(m0 + j) * p.out_cols] : 0.0f;
+        if (resid) {
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = fmaf(p.alpha, __uint_as_float(v[j]) + b, out[j]);
         } else if (glu) {
@@ -460,6 +468,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
           for (int j = 0; j < E; ++j)
             if (j < cnt) yp[(size_t)j * p.out_cols] = out[j];
         }
+        if (resid && cc + 1 < kChunks) load_resid(m0 + E);
       }
       tc_fence_before();
       __syncwarp();  // every lane's accumulator loads are complete: one arrival per warp
