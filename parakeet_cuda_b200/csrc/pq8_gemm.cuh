@@ -118,7 +118,18 @@ struct GemmCfg {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory overflow");
   static_assert((kXStageBytes / 16) % kGroupThreads == 0, "X stage must split evenly over a group");
   static_assert(kRowsPerCta % 8 == 0, "activation rows per CTA must fill 8-row swizzle atoms");
-  static_assert(ASLOTS % kGroups == 0, "each converter group owns whole tensor-memory slots");
+  // A converter's parity wait on a weight-record stage must not pass on the
+  // phase before last, i.e. the stage's previous record must have landed.
+  // Either the same group consumed that record (WSTAGES a multiple of the
+  // group count), or the group's previous tensor-memory slot wait proved
+  // MMA(i - kGroups - ASLOTS) complete, and with it every record up to there
+  // consumed (WSTAGES >= kGroups + ASLOTS).
+  // Tensor-memory slots need no such rule: a group's previous slot wait saw
+  // the slot's use before last complete (kGroups <= ASLOTS). Nor do activation
+  // stages: the slot wait of block i proves every block up to i - ASLOTS
+  // vouched for, which covers the stage's previous use when STAGES >= ASLOTS.
+  static_assert(WSTAGES % kGroups == 0 || WSTAGES >= kGroups + ASLOTS, "weight-record stage reuse must be covered");
+  static_assert(STAGES >= ASLOTS, "activation stage reuse is covered by the slot waits");
   static_assert(GROUP_WARPS_ == 4 || GROUP_WARPS_ == 8, "a converter group covers the 4 TMEM lane quarters");
   static_assert(kEpiCols == 32, "the staged epilogue writes 32 activation rows per chunk");
   static_assert(kRendezvousBlocks >= 1, "need at least two tensor-memory slots");
