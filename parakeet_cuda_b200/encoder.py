@@ -181,3 +181,61 @@ class EncoderStack:
             self.step()
         out_host.copy_(self.buffers['resid'], non_blocking=True)
         return out_host
+
+    def run_host_pipelined(self, inputs, outputs, graph=None):
+        """One step per (``inputs[i]``, ``outputs[i]``) pair of pinned host buffers,
+        as ``run_host`` does for each, with the copies overlapped: step i+1's
+        host-to-device copy and step i-1's device-to-host copy run on two copy
+        streams while step i computes. Two device staging buffers per direction
+        decouple the copies from the step's own buffers (a device-to-device copy
+        at each end of the step). Every step still moves its whole input and
+        result across PCIe; only the waiting is gone. Returns ``outputs``; the
+        current stream waits for the last copy, so the caller synchronizes as
+        for ``run_host``."""
+        if len(inputs) != len(outputs):
+            raise ValueError('inputs and outputs must pair up')
+        dev = self.rt.device
+        compute = torch.cuda.current_stream(dev)
+        if not hasattr(self, '_pipe'):
+            shape = self.buffers['resid'].shape
+            self._pipe = {
+                'h2d': torch.cuda.Stream(dev), 'd2h': torch.cuda.Stream(dev),
+                'in': [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)],
+                'out': [torch.empty(shape, dtype=torch.float32, device=dev) for _ in range(2)],
+            }
+        pipe = self._pipe
+        h2d, d2h = pipe['h2d'], pipe['d2h']
+        ev = {name: [torch.cuda.Event() for _ in range(2)]
+              for name in ('in_ready', 'in_free', 'out_ready', 'out_free')}
+        used = [False, False]
+        h2d.wait_stream(compute)
+        d2h.wait_stream(compute)
+        for i, (x_host, out_host) in enumerate(zip(inputs, outputs)):
+            s = i & 1
+            with torch.cuda.stream(h2d):
+                if used[s]:
+                    h2d.wait_event(ev['in_free'][s])  # step i-2 has taken its input out of this buffer
+                pipe['in'][s].copy_(x_host, non_blocking=True)
+                ev['in_ready'][s].record(h2d)
+            compute.wait_event(ev['in_ready'][s])
+            self.buffers['norm'].copy_(pipe['in'][s], non_blocking=True)
+            self.buffers['resid'].copy_(pipe['in'][s], non_blocking=True)
+            ev['in_free'][s].record(compute)
+            if self.producer_tf32:
+                self.round_buffer('norm')
+            if graph is not None:
+                graph.replay()
+            else:
+                self.step()
+            if used[s]:
+                compute.wait_event(ev['out_free'][s])  # step i-2's result has left this buffer
+            pipe['out'][s].copy_(self.buffers['resid'], non_blocking=True)
+            ev['out_ready'][s].record(compute)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev['out_ready'][s])
+                out_host.copy_(pipe['out'][s], non_blocking=True)
+                ev['out_free'][s].record(d2h)
+            used[s] = True
+        compute.wait_stream(h2d)
+        compute.wait_stream(d2h)
+        return outputs
