@@ -51,8 +51,8 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
     ap.add_argument('--tdt-batches', default='1,64', help='decode batch sizes of the tdt extra')
-    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep,load,block',
-                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep, load, block)')
+    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep,load,block,refgpu',
+                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep, load, block, refgpu)')
     return ap.parse_args()
 
 
@@ -222,6 +222,9 @@ def run_gpu(args):
                               'gbs': rt.uploader().bytes_uploaded / stack.load_seconds / 1e9}}
     if sched.rank == 0 and not args.no_extras and 'load' in args.extras.split(','):
         load.update(load_measure(torch, rt, model))
+    ref_raw = None
+    if not args.no_extras and 'refgpu' in args.extras.split(','):
+        ref_raw = upload_raw_layers(torch, model, args.layers, dev)
     del model
     torch.cuda.synchronize()
 
@@ -317,6 +320,9 @@ def run_gpu(args):
             extras['sweep'] = sweep_measure(torch, rt)
         if 'load' in wanted:
             extras['weight_load'] = load
+        if 'refgpu' in wanted:
+            extras['reference_gpu_method'] = reference_gpu_method(torch, rt, ref_raw, stack)
+        ref_raw = None
         if 'block' in wanted:
             extras['full_block'] = block_measure(torch, rt, args, ms)
     sched.barrier()
@@ -641,6 +647,85 @@ def sweep_measure(torch, rt):
                         'bound': 'hbm' if flops / nbytes * bw < p_tf32 else 'tensor'})
             del x, y
     return out
+
+
+def upload_raw_layers(torch, model, layers, dev):
+    """Raw GGUF Q8_0 bytes of every encoder linear on the device (Q, K, V stacked along N)."""
+    import numpy as np
+    from parakeet_cuda_b200.encoder import LAYER_PLAN
+    raw = []
+    for l in range(layers):
+        base = f'encoder.layers.{l}.'
+        raw.append({name: torch.from_numpy(np.concatenate(
+            [np.asarray(model.raw(base + key + '.weight'), np.uint8).reshape(-1) for key in keys])).to(dev)
+            for name, keys, *_ in LAYER_PLAN})
+    return raw
+
+
+def reference_gpu_method(torch, rt, raw, stack, steps=3):
+    """Context, not the product: config 2 by the reference's GPU method on this B200,
+    restated with library calls on the same shapes and buffers as the timed step.
+    For every layer (``encoder.py:204``, ``gpu.py:169-184``) each Q8_0 weight of
+    the layer is expanded to FP32 (``pq8_dequant_q8_0``, bit-identical to
+    ``dequant_q8``, ``runtime.cu:26-33``), each linear is one cuBLAS GEMM on the
+    FP32 weights (``torch.mm``; TF32 off is the reference's ``cublasSgemm_v2``,
+    ``gpu.py:87-90``) and each epilogue a separate elementwise pass
+    (``runtime.cu:49-62``). Timed again with TF32 allowed: a library TF32 port of
+    the same method. Both are captured in CUDA graphs (no host launch cost)."""
+    from parakeet_cuda_b200.encoder import LAYER_PLAN
+    from parakeet_cuda_b200.pq8 import EPI_GLU, EPI_RESIDUAL, EPI_SILU
+    dev = rt.device
+    rows = stack.rows
+    b = stack.buffers
+    wf = {name: torch.empty(n, k, device=dev) for name, _, n, k, *_ in LAYER_PLAN}
+    y = {name: torch.empty(rows, n, device=dev) for name, _, n, _, epi, *_ in LAYER_PLAN
+         if epi in (EPI_RESIDUAL, EPI_GLU)}
+    sig = torch.empty(rows, LAYER_PLAN[5][2] // 2, device=dev)
+
+    def step():
+        for layer in raw:
+            for name, _, n, k, *_ in LAYER_PLAN:  # the whole layer is expanded first, as gpu.py does
+                rt.lib.call('pq8_dequant_q8_0', layer[name].data_ptr(), wf[name].data_ptr(), n * k, rt.stream())
+            for name, _, n, k, epi, alpha, src, dst, _ in LAYER_PLAN:
+                if epi == EPI_RESIDUAL:  # x += alpha * y
+                    torch.mm(b[src], wf[name].t(), out=y[name])
+                    b[dst].add_(y[name], alpha=alpha)
+                elif epi == EPI_GLU:     # a * sigmoid(b) over the two halves of N
+                    torch.mm(b[src], wf[name].t(), out=y[name])
+                    half = n // 2
+                    torch.sigmoid(y[name][:, half:], out=sig)
+                    torch.mul(y[name][:, :half], sig, out=b[dst])
+                else:                    # written in place, SiLU applied over it
+                    torch.mm(b[src], wf[name].t(), out=b[dst])
+                    if epi == EPI_SILU:
+                        torch.nn.functional.silu(b[dst], inplace=True)
+
+    res = {'method': 'pq8_dequant_q8_0 per layer + torch.mm (cuBLAS) per linear + elementwise epilogues',
+           'layers': len(raw), 'rows': rows, 'steps': steps}
+    flops = stack.flops_per_step()
+    for key, tf32 in (('fp32_sgemm', False), ('tf32', True)):
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+        step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        res[key] = {'ms_per_step': ms, 'frames_per_s': rows / (ms / 1e3), 'tflops': flops / (ms / 1e3) / 1e12}
+        del g
+    torch.backends.cuda.matmul.allow_tf32 = False
+    return res
 
 
 def cublas_tf32(torch):
