@@ -502,7 +502,7 @@ def tdt_measure(torch, rt, batches=(1, 64)):
             'joint_calls_per_s': calls_dev / ddev.loop_seconds,
             'call_seconds': t_dev, 'call_joint_calls_per_s': calls_dev / t_dev,
             'same_result_as_host_loop': res_dev == res,
-            'loop': 'device (pq8_tdt_control; CUDA graph of 16 steps, host polls the remaining count); '
+            'loop': 'device (pq8_tdt_advance; CUDA graph of 16 steps, host polls the remaining count); '
                     'steps_per_s over the replay loop, call_* over the whole call (frame table, graph capture, '
                     'results to host lists)'}
     return out

@@ -230,6 +230,19 @@ PQ8_API int pq8_tdt_control(const int* ids, const int* durations, int n_duration
                             int enc_stride, int* tokens, int* enc_rows, int* commit_mask, int* emitted,
                             int emitted_capacity, int* trace, int trace_capacity, int* remaining, void* stream);
 
+/* pq8_tdt_control followed by pq8_tdt_commit, in one launch (one fewer kernel
+ * per decode step; same arguments as the two, hidden a multiple of 4 and the
+ * state buffers 16-byte aligned). One difference: the commit takes the
+ * candidate state of every stream whose joint token is not blank, including
+ * streams already done, whose state no later result reads; pq8_tdt_commit
+ * with the mask written by pq8_tdt_control leaves those unchanged. Like
+ * pq8_tdt_control it has no counterpart in the reference (decoder.py:74-97
+ * runs on the host). */
+PQ8_API int pq8_tdt_advance(const int* ids, const int* durations, int n_durations, int* state, int m,
+                            int enc_stride, int* tokens, int* enc_rows, int* commit_mask, int* emitted,
+                            int emitted_capacity, int* trace, int trace_capacity, int* remaining, float* h,
+                            float* c, const float* h_new, const float* c_new, int layers, int hidden, void* stream);
+
 /* pq8_gemv without a workspace argument, for callers that cannot allocate
  * device memory: a host that keeps all device memory in its own pre-reserved
  * pool, or a latency-critical loop where cudaMalloc would synchronize the

@@ -731,6 +731,33 @@ extern "C" int pq8_tdt_control(const int* ids, const int* durations, int n_durat
   return to_code(cudaGetLastError());
 }
 
+extern "C" int pq8_tdt_advance(const int* ids, const int* durations, int n_durations, int* state, int m,
+                               int enc_stride, int* tokens, int* enc_rows, int* commit_mask, int* emitted,
+                               int emitted_capacity, int* trace, int trace_capacity, int* remaining, float* h,
+                               float* c, const float* h_new, const float* c_new, int layers, int hidden,
+                               void* stream) {
+  if (m < 1 || m > 1024 || n_durations < 1 || enc_stride < 0 || emitted_capacity < 0 || trace_capacity < 0 ||
+      layers < 1 || hidden < 4 || hidden % 4)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (ids == nullptr || durations == nullptr || state == nullptr || tokens == nullptr || enc_rows == nullptr ||
+      commit_mask == nullptr || remaining == nullptr || (emitted_capacity > 0 && emitted == nullptr) ||
+      (trace_capacity > 0 && trace == nullptr) || h == nullptr || c == nullptr || h_new == nullptr ||
+      c_new == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(h, 16) || !aligned(c, 16) || !aligned(h_new, 16) || !aligned(c_new, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  const long long vecs = (long long)layers * m * (hidden / 4);
+  const int grid = (int)std::max<long long>(1, std::min<long long>((vecs + 255) / 256, ds->sms));
+  cudaError_t e = launch_pdl(tdt_advance_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), ids,
+                             durations, n_durations, state, m, enc_stride, tokens, enc_rows, commit_mask, emitted,
+                             emitted_capacity, trace, trace_capacity, remaining, h, c, h_new, c_new, layers, hidden,
+                             ds->status);
+  if (e != cudaSuccess) return to_code(e);
+  return to_code(cudaGetLastError());
+}
+
 extern "C" int pq8_device_status(int* status, void* stream) {
   if (status == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
   DeviceState* ds;

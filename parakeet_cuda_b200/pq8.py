@@ -66,6 +66,7 @@ SIGNATURES = {
     'pq8_joint_argmax': ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P], _I),
     'pq8_tdt_commit': ([_P, _P, _P, _P, _P, _I, _I, _I, _P], _I),
     'pq8_tdt_control': ([_P, _P, _I, _P, _I, _I, _P, _P, _P, _P, _I, _P, _I, _P, _P], _I),
+    'pq8_tdt_advance': ([_P, _P, _I, _P, _I, _I, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _I, _P], _I),
     'pq8_device_status': ([C.POINTER(_I), _P], _I),
 }
 

@@ -12,8 +12,8 @@ per step for all streams, one predict for all streams whenever any stream
 needs it (a stream whose inputs did not change gets bit-identical candidates
 again, so this is equivalent to predicting it alone), and a masked commit.
 ``greedy_decode_device`` runs the same loop without the host: the control
-rules run in a kernel (``pq8_tdt_control``), so a step is a fixed launch
-sequence (predict, joint, control, commit) replayed from a CUDA graph of
+rules and the commit run in one kernel (``pq8_tdt_advance``), so a step is a
+fixed launch sequence (predict, joint, advance) replayed from a CUDA graph of
 several steps, and the host only polls how many streams remain between
 replays. It predicts every step: a stream that emitted nothing recomputes
 bit-identical candidates, so the results equal ``greedy_decode_batch``'s.
@@ -25,6 +25,8 @@ import time
 
 import numpy as np
 import torch
+
+from .decoder import HIDDEN, LAYERS
 
 BLANK = 8192
 MAX_SYMBOLS = 10
@@ -164,10 +166,11 @@ def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 1
     def step():
         decoder.predict_device()
         decoder.joint_device(enc, decoder.enc_rows)
-        lib.call('pq8_tdt_control', decoder.ids.data_ptr(), dur.data_ptr(), dur.numel(), state.data_ptr(), b,
+        # control and commit in one launch
+        lib.call('pq8_tdt_advance', decoder.ids.data_ptr(), dur.data_ptr(), dur.numel(), state.data_ptr(), b,
                  t_max, decoder.tokens.data_ptr(), decoder.enc_rows.data_ptr(), decoder.commit_mask.data_ptr(),
-                 emitted.data_ptr(), cap, trace.data_ptr(), cap, remaining.data_ptr(), rt.stream())
-        decoder.commit_rows(decoder.commit_mask)
+                 emitted.data_ptr(), cap, trace.data_ptr(), cap, remaining.data_ptr(), decoder.h.data_ptr(),
+                 decoder.c.data_ptr(), decoder.hn.data_ptr(), decoder.cn.data_ptr(), LAYERS, HIDDEN, rt.stream())
 
     # Kernel attributes and workspaces are set up outside the capture: this
     # predict/joint pair computes exactly what the first step will compute.

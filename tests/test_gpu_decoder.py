@@ -198,6 +198,68 @@ def test_tdt_device_loop_step_limit(rt):
     assert r['decode_trace'] == ref['decode_trace'][:37]
 
 
+@pytest.mark.parametrize('m', [1, 7, 300])
+def test_tdt_advance_equals_control_then_commit(rt, m):
+    """pq8_tdt_advance (one launch) against pq8_tdt_control + pq8_tdt_commit on
+    the same random step: streams done and live, blanks and tokens, every
+    duration, a stream at the 10-symbol cap, a trace buffer that is full for
+    some streams (m = 300 also runs block 0's stream loop past 256 threads).
+    All control outputs must be identical; the LSTM state too, except that
+    advance also commits done streams that drew a token."""
+    rng = np.random.default_rng(400 + m)
+    layers, hidden, stride, cap = 2, 640, 50, 6
+    frames = rng.integers(0, 12, size=m)
+    state = np.zeros((m, 8), np.int32)
+    state[:, 0] = frames
+    state[:, 1] = rng.integers(0, 13, size=m)             # t; some already past the end
+    state[:, 2] = rng.integers(0, 10, size=m)             # symbols (9 = one call from the cap)
+    state[:, 3] = rng.integers(0, 8193, size=m)
+    state[:, 4] = rng.integers(0, cap + 1, size=m)        # emitted so far; cap = full
+    state[:, 5] = rng.integers(0, cap + 1, size=m)        # joint calls so far; cap = full trace
+    state[:, 6] = (state[:, 1] >= frames).astype(np.int32)
+    ids = np.stack([np.where(rng.random(m) < 0.5, 8192, rng.integers(0, 8192, size=m)),
+                    rng.integers(0, 5, size=m)], axis=1).astype(np.int32)
+    h0 = rng.normal(size=(layers, m, hidden)).astype(np.float32)
+    c0 = rng.normal(size=(layers, m, hidden)).astype(np.float32)
+    hn = rng.normal(size=(layers, m, hidden)).astype(np.float32)
+    cn = rng.normal(size=(layers, m, hidden)).astype(np.float32)
+    dur = dev(np.asarray(DURATIONS, np.int32))
+
+    def run(fused):
+        out = {'state': dev(state), 'tokens': torch.zeros(m, dtype=torch.int32, device='cuda'),
+               'enc_rows': torch.zeros(m, dtype=torch.int32, device='cuda'),
+               'mask': torch.zeros(m, dtype=torch.int32, device='cuda'),
+               'emitted': torch.full((m, cap, 3), -1, dtype=torch.int32, device='cuda'),
+               'trace': torch.full((m, cap, 3), -1, dtype=torch.int32, device='cuda'),
+               'remaining': torch.zeros(1, dtype=torch.int32, device='cuda'),
+               'h': dev(h0), 'c': dev(c0)}
+        g_ids, g_hn, g_cn = dev(ids), dev(hn), dev(cn)
+        ctl = (g_ids.data_ptr(), dur.data_ptr(), len(DURATIONS), out['state'].data_ptr(), m, stride,
+               out['tokens'].data_ptr(), out['enc_rows'].data_ptr(), out['mask'].data_ptr(),
+               out['emitted'].data_ptr(), cap, out['trace'].data_ptr(), cap, out['remaining'].data_ptr())
+        if fused:
+            rt.lib.call('pq8_tdt_advance', *ctl, out['h'].data_ptr(), out['c'].data_ptr(), g_hn.data_ptr(),
+                        g_cn.data_ptr(), layers, hidden, rt.stream())
+        else:
+            rt.lib.call('pq8_tdt_control', *ctl, rt.stream())
+            rt.lib.call('pq8_tdt_commit', out['h'].data_ptr(), out['c'].data_ptr(), g_hn.data_ptr(),
+                        g_cn.data_ptr(), out['mask'].data_ptr(), m, layers, hidden, rt.stream())
+        torch.cuda.synchronize()
+        return {k: v.cpu().numpy() for k, v in out.items()}
+
+    want, got = run(False), run(True)
+    for key in ('state', 'tokens', 'enc_rows', 'mask', 'emitted', 'trace', 'remaining'):
+        np.testing.assert_array_equal(got[key], want[key], err_msg=key)
+    done_token = (state[:, 6] == 1) & (ids[:, 0] != 8192)
+    for key, new in (('h', hn), ('c', cn)):
+        np.testing.assert_array_equal(got[key][:, ~done_token], want[key][:, ~done_token], err_msg=key)
+        np.testing.assert_array_equal(got[key][:, done_token], new[:, done_token], err_msg=key)
+    if m > 1:
+        assert want['mask'].any() and not want['mask'].all()
+    # full trace or token buffers make both runs record PQ8_ERR_WORKSPACE; reading the status clears it
+    assert rt.device_status() in (0, pq8.ERR_WORKSPACE)
+
+
 def test_status_clean(rt):
     torch.cuda.synchronize()
     assert rt.device_status() == 0
