@@ -135,11 +135,25 @@ def ncu_traffic():
 
 
 # ------------------------------------------------------------------ CPU legs
+def host_cores() -> int:
+    """CPUs this process may run on."""
+    return len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else (os.cpu_count() or 1)
+
+
+def all_blas_threads():
+    """BLAS thread pool raised to every usable host core for the CPU legs
+    (torchrun starts each rank with OMP_NUM_THREADS=1)."""
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=host_cores(), user_api='blas')
+
+
 def cpu_sample(model, rows=WINDOW_FRAMES, repeats=3):
     from oracle.cpu_path import blas_threads, time_layer_window
-    times = [time_layer_window(model, rows, layer=0, seed=i) for i in range(repeats)]
+    with all_blas_threads():
+        times = [time_layer_window(model, rows, layer=0, seed=i) for i in range(repeats)]
+        cores = blas_threads()
     t = min(times)
-    return {'value': rows / (t * 24), 'unit': UNIT, 'cores': blas_threads(), 'kind': 'port',
+    return {'value': rows / (t * 24), 'unit': UNIT, 'cores': cores, 'kind': 'port',
             'sample': (f'NumPy restatement of the reference CPU path (gguf.array Q8_0 decode + FP32 x @ W.T, '
                        f'reference.py:37): one layer x one {rows}-frame window, best of {repeats} '
                        f'({t:.3f} s), scaled to 24 layers')}
@@ -152,9 +166,11 @@ def run_reference(args):
     from parakeet_cuda_b200.synthetic import SyntheticParakeet
     model = SyntheticParakeet(seed=0, encoder_layers=1, decoder=False)
     from oracle.cpu_path import blas_threads, time_layer_window
-    for i in range(args.warmup):
-        time_layer_window(model, WINDOW_FRAMES, 0, seed=i)
-    times = [time_layer_window(model, WINDOW_FRAMES, 0, seed=100 + i) for i in range(args.steps)]
+    with all_blas_threads():
+        for i in range(args.warmup):
+            time_layer_window(model, WINDOW_FRAMES, 0, seed=i)
+        times = [time_layer_window(model, WINDOW_FRAMES, 0, seed=100 + i) for i in range(args.steps)]
+        cores = blas_threads()
     t = sum(times) / len(times)
     value = WINDOW_FRAMES / (t * 24)
     n = args.gpus
@@ -162,7 +178,7 @@ def run_reference(args):
             'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': t * 1000, 'higher_is_better': True,
             'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
             'config': config(args, n),
-            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': blas_threads(), 'kind': 'port',
+            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': 'port',
                              'sample': (f'each step: one encoder layer (Q8_0 decode + 9 FP32 linears) over one '
                                         f'{WINDOW_FRAMES}-frame window; frames/s = {WINDOW_FRAMES} / '
                                         f'(24 x step time)')},
