@@ -525,7 +525,7 @@ def tdt_measure(torch, rt, batches=(1, 64)):
 
 
 def block_measure(torch, rt, args, linear_ms):
-    """Whole FastConformer blocks (SURVEY-(f)2): every layer of config 2's shapes with
+    """Whole FastConformer blocks (the rest of the block on the device): every layer of config 2's shapes with
     LayerNorms, rel-pos attention and the conv module on the device around the same Q8_0
     linears, 8 windows x 375 frames per GPU; one CUDA-graph replay per step. Random
     block-scale weights (SyntheticParakeet(block=True))."""
@@ -586,7 +586,7 @@ def block_measure(torch, rt, args, linear_ms):
 
 
 def load_measure(torch, rt, model):
-    """Weight upload, SURVEY-(f)3: GGUF bytes -> resident packed weights.
+    """Weight upload: GGUF bytes -> resident packed weights.
     device_upload (measured by the caller on the full stack): pinned staging,
     async H2D, repack kernel. Here: the same for 2 layers packed on the host
     (pq8_pack_q8_0, then the packed bytes copied), the pinned H2D copy rate

@@ -15,6 +15,7 @@ Output: ``block.npz``.
 from __future__ import annotations
 
 import importlib.util
+import os
 from pathlib import Path
 import sys
 
@@ -49,4 +50,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    if len(sys.argv) < 2 and 'PARAKEET_CUDA_REFERENCE' not in os.environ:
+        raise SystemExit('usage: make_block_golden.py <parakeet_cuda checkout> (or set PARAKEET_CUDA_REFERENCE)')
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ['PARAKEET_CUDA_REFERENCE'])

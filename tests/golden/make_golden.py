@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import hashlib
 import json
+import os
 from pathlib import Path
 import struct
 import sys
@@ -167,7 +168,9 @@ def tdt_cases(ref: Path, meta: dict) -> dict:
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference').resolve()
+    if len(sys.argv) < 2 and 'PARAKEET_CUDA_REFERENCE' not in os.environ:
+        raise SystemExit('usage: make_golden.py <parakeet_cuda checkout> (or set PARAKEET_CUDA_REFERENCE)')
+    ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ['PARAKEET_CUDA_REFERENCE']).resolve()
     if not (ref / 'parakeet_cuda' / 'decoder.py').is_file():
         raise SystemExit(f'reference checkout not found at {ref}')
     install_txir_stub()
