@@ -72,8 +72,15 @@ def config(args, n_gpus):
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
+    """nvidia-smi sampling every 50 ms. It is started before the warm-up (the
+    tool takes a moment to come up, longer with several GPUs); ``wait_ready``
+    waits for its first samples and ``mark`` notes where the timed region
+    starts, so that ``stop`` summarises the samples taken during it."""
+
     def __init__(self, gpus: int):
         self.proc = None
+        self.gpus = gpus
+        self.start = 0
         self.path = Path(os.environ.get('TMPDIR', '/tmp')) / f'pq8_clocks_{os.getpid()}.csv'
         q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
@@ -86,6 +93,22 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def _lines(self):
+        try:
+            return [l for l in self.path.read_text().splitlines() if l.strip()]
+        except OSError:
+            return []
+
+    def wait_ready(self, timeout_s: float = 10.0):
+        t0 = time.time()
+        while self.proc is not None and self.proc.poll() is None and time.time() - t0 < timeout_s:
+            if len(self._lines()) >= self.gpus:
+                return
+            time.sleep(0.05)
+
+    def mark(self):
+        self.start = len(self._lines())
+
     def stop(self):
         if self.proc is None:
             return None
@@ -97,7 +120,10 @@ class ClockSampler:
         self.f.close()
         sm, mx, reasons = [], 0, set()
         names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
-        for line in self.path.read_text().splitlines():
+        lines = self._lines()
+        during = lines[self.start:]
+        # a timed region shorter than one sampling period: the last sample of each GPU
+        for line in (during if len(during) >= self.gpus else lines[-self.gpus:]):
             parts = [p.strip() for p in line.split(',')]
             if len(parts) < 9:
                 continue
@@ -248,15 +274,19 @@ def run_gpu(args):
     stack.step()
     torch.cuda.synchronize()
     graph = stack.capture()
+    clocks = ClockSampler(n) if sched.rank == 0 else None
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
+    if clocks:
+        clocks.wait_ready()
     sched.barrier()
 
-    clocks = ClockSampler(n) if sched.rank == 0 else None
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     sched.barrier()
+    if clocks:
+        clocks.mark()
     start.record()
     for _ in range(args.steps):
         graph.replay()
