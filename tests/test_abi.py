@@ -101,3 +101,55 @@ def test_host_packer_k_concat(lib):
     both = np.concatenate([a.reshape(256, 2, 34), b.reshape(256, 3, 34)], axis=1).reshape(-1, 34)
     np.testing.assert_array_equal(pack_concat_host([(a, 64), (b, 96)], 256, pq8.LAYOUT_GATES4),
                                   pack_host(both, 256, 160, pq8.LAYOUT_GATES4))
+
+
+C_PROGRAM = r'''
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include "pq8.h"
+
+int main(void) {
+  const int n = 130, k = 64; /* two 128-row tiles, two 32-wide K blocks */
+  size_t bytes = 0;
+  unsigned char *gguf, *packed;
+  int r, b, i;
+  if (pq8_version() <= 0) return 1;
+  if (strncmp(pq8_error_string(PQ8_ERR_WORKSPACE), "PQ8_ERR_WORKSPACE", 17) != 0) return 2;
+  if (pq8_packed_size(n, k, PQ8_LAYOUT_ROWS, &bytes) != PQ8_OK) return 3;
+  if (bytes != 256 + 2 * 2 * 4352) return 4; /* header + tiles x K blocks x record */
+  gguf = calloc((size_t)n * (k / 32), 34);
+  packed = malloc(bytes);
+  if (!gguf || !packed) return 5;
+  for (r = 0; r < n; ++r)
+    for (b = 0; b < k / 32; ++b) {
+      unsigned char* blk = gguf + ((size_t)r * (k / 32) + b) * 34;
+      blk[0] = 0x00; blk[1] = 0x3c; /* fp16 1.0 */
+      for (i = 0; i < 32; ++i) blk[2 + i] = (unsigned char)(r + i);
+    }
+  if (pq8_pack_q8_0(gguf, n, k, PQ8_LAYOUT_ROWS, packed) != PQ8_OK) return 6;
+  if (memcmp(packed, "PQ8P", 4) != 0) return 7;
+  /* a bad shape is rejected before any device is touched */
+  if (pq8_gemm(NULL, NULL, NULL, NULL, NULL, 4, 128, 33, 0, 1.0f, 0, NULL) != PQ8_ERR_UNSUPPORTED_SHAPE) return 8;
+  printf("ok %d\n", pq8_version());
+  free(gguf);
+  free(packed);
+  return 0;
+}
+'''
+
+
+def test_header_is_plain_c_and_links(lib, tmp_path):
+    """include/pq8.h compiles as strict C99 and a C program linked against
+    libpq8.so calls the host-side entry points (no GPU involved): the boundary
+    is a C ABI, not a C++ or Python one."""
+    src = tmp_path / 'abi.c'
+    src.write_text(C_PROGRAM)
+    exe = tmp_path / 'abi'
+    libdir = str(lib.path.parent)
+    include = str(lib.path.parents[1] / 'include')
+    r = subprocess.run(['gcc', '-std=c99', '-Wall', '-Wextra', '-Werror', '-pedantic', '-I', include, str(src), '-o',
+                        str(exe), '-L', libdir, '-lpq8', f'-Wl,-rpath,{libdir}'], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.startswith('ok '), (run.returncode, run.stdout, run.stderr)
