@@ -354,6 +354,7 @@ def run_gpu(args):
     del graph
 
     extras = {}
+    sweep_points = None
     if not args.no_extras:
         wanted = set(args.extras.split(','))
         if 'gemv' in wanted:
@@ -363,7 +364,7 @@ def run_gpu(args):
         if 'tdt' in wanted:
             extras['tdt'] = tdt_measure(torch, rt, [int(b) for b in args.tdt_batches.split(',')])
         if 'sweep' in wanted:
-            extras['sweep'] = sweep_measure(torch, rt)
+            sweep_points = sweep_measure(torch, rt, sched.rank, n)
         if 'load' in wanted:
             extras['weight_load'] = load
         if 'refgpu' in wanted:
@@ -372,6 +373,10 @@ def run_gpu(args):
         if 'block' in wanted:
             extras['full_block'] = block_measure(torch, rt, args, ms)
     sched.barrier()
+    if sweep_points is not None:  # every rank ran its share (the arguments are the same on every rank)
+        parts = sched.gather([sweep_points])
+        if sched.rank == 0:
+            extras['sweep'] = merge_sweep(parts, measured_peaks()[0])
 
     if sched.rank == 0:
         peaks, peak_src = measured_peaks()
@@ -663,36 +668,78 @@ def load_measure(torch, rt, model):
     return out
 
 
-def sweep_measure(torch, rt):
-    """BASELINE config 4 roofline sweep on one GPU: M x (N, K) through pq8_linear.
-    Roofline per point = min(TF32 peak, AI x HBM), AI = 2MNK / (1.0625 NK + 4MK + 4MN)."""
+SWEEP_SHAPES = ((1024, 1024), (4096, 1024), (1024, 4096), (2560, 640), (8197, 640))
+SWEEP_M = (1, 16, 128, 1024, 8192, 65536)
+
+
+def shard_rows(m, rank, world):
+    """This rank's contiguous, balanced share of m rows: (first row, count)."""
+    start = m * rank // world
+    return start, m * (rank + 1) // world - start
+
+
+def sweep_local(rank, world, time_point):
+    """BASELINE config 4, M-sharded: for every (N, K) and M, this rank times its
+    share of the M rows with ``time_point(n, k, rows) -> seconds`` (no work and
+    0 s for an empty share). The points come in the same order on every rank."""
+    out = []
+    for n, k in SWEEP_SHAPES:
+        for m in SWEEP_M:
+            _, rows = shard_rows(m, rank, world)
+            out.append({'m': m, 'n': n, 'k': k, 'rows': rows, 's': time_point(n, k, rows) if rows else 0.0})
+    return out
+
+
+def merge_sweep(parts, peaks):
+    """Whole-job sweep from every rank's ``sweep_local`` points: a point takes as
+    long as its slowest rank. Roofline of a point = the larger of its FLOPs over
+    the active GPUs' TF32 peak and its bytes (each active GPU reads the whole
+    Q8_0 matrix, 1.0625 N K, plus its rows of X and Y) over their HBM
+    bandwidth; AI = FLOPs / bytes."""
+    p_tf32, bw = peaks['bf16_tflops_sustained'] / 2 * 1e12, peaks['hbm_gbs'] * 1e9
+    res = []
+    for pts in zip(*parts):
+        m, n, k = pts[0]['m'], pts[0]['n'], pts[0]['k']
+        gpus = sum(1 for p in pts if p['rows'])
+        s_ = max(p['s'] for p in pts)
+        if gpus == 0 or s_ <= 0:  # no rank had rows (only when some ranks' points are missing)
+            res.append({'m': m, 'n': n, 'k': k, 'gpus': gpus, 'us': None})
+            continue
+        flops = 2 * m * n * k
+        nbytes = gpus * 1.0625 * n * k + 4 * m * k + 4 * m * n
+        t_tensor, t_hbm = flops / (gpus * p_tf32), nbytes / (gpus * bw)
+        res.append({'m': m, 'n': n, 'k': k, 'gpus': gpus, 'us': s_ * 1e6, 'tflops': flops / s_ / 1e12,
+                    'gbs': nbytes / s_ / 1e9, 'frac_of_roofline': max(t_tensor, t_hbm) / s_,
+                    'bound': 'hbm' if t_hbm > t_tensor else 'tensor'})
+    return res
+
+
+def sweep_measure(torch, rt, rank=0, world=1):
+    """This rank's config-4 points through pq8_linear (CUDA events, 10 launches
+    per point after one untimed); ``merge_sweep`` combines the ranks."""
     import numpy as np
     from parakeet_cuda_b200.synthetic import q8_0_blocks
-    peaks, _ = measured_peaks()
-    p_tf32, bw = peaks['bf16_tflops_sustained'] / 2 * 1e12, peaks['hbm_gbs'] * 1e9
-    out = []
-    for n, k in ((1024, 1024), (4096, 1024), (1024, 4096), (2560, 640), (8197, 640)):
-        w = rt.pack(q8_0_blocks(np.random.default_rng(n + k), n, k), n, k)
-        for m in (1, 16, 128, 1024, 8192, 65536):
-            x = torch.randn(m, k, device=rt.device)
-            y = torch.empty(m, n, device=rt.device)
+    weights = {}
+
+    def time_point(n, k, rows):
+        if (n, k) not in weights:
+            weights.clear()
+            weights[(n, k)] = rt.pack(q8_0_blocks(np.random.default_rng(n + k), n, k), n, k)
+        w = weights[(n, k)]
+        x = torch.randn(rows, k, device=rt.device)
+        y = torch.empty(rows, n, device=rt.device)
+        rt.linear(x, w, out=y)
+        torch.cuda.synchronize()
+        reps = 10
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
             rt.linear(x, w, out=y)
-            torch.cuda.synchronize()
-            reps = 10
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for _ in range(reps):
-                rt.linear(x, w, out=y)
-            b.record()
-            torch.cuda.synchronize()
-            s_ = a.elapsed_time(b) / reps / 1e3
-            flops, nbytes = 2 * m * n * k, 1.0625 * n * k + 4 * m * k + 4 * m * n
-            roof = min(p_tf32, flops / nbytes * bw)
-            out.append({'m': m, 'n': n, 'k': k, 'us': s_ * 1e6, 'tflops': flops / s_ / 1e12,
-                        'gbs': nbytes / s_ / 1e9, 'frac_of_roofline': flops / s_ / roof,
-                        'bound': 'hbm' if flops / nbytes * bw < p_tf32 else 'tensor'})
-            del x, y
-    return out
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps / 1e3
+
+    return sweep_local(rank, world, time_point)
 
 
 def upload_raw_layers(torch, model, layers, dev):

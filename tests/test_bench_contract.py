@@ -81,3 +81,61 @@ def test_clock_sampler_short_region_uses_last_samples(tmp_path):
     s.mark()
     info = s.stop()
     assert info is not None and info['samples'] == 2 and info['sm_mhz'] == 1905.0
+
+
+def test_sweep_shards_partition_the_rows():
+    bench = _bench_module()
+    for m in bench.SWEEP_M + (0, 3, 7):
+        for world in (1, 2, 3, 4, 8):
+            spans = [bench.shard_rows(m, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and sum(c for _, c in spans) == m
+            assert all(s + c == spans[i + 1][0] for i, (s, c) in enumerate(spans[:-1]))
+            assert max(c for _, c in spans) - min(c for _, c in spans) <= 1
+
+
+def _sweep_worker(rank, world, port, q):
+    import os
+    os.environ.update({'RANK': str(rank), 'WORLD_SIZE': str(world), 'LOCAL_RANK': str(rank),
+                       'MASTER_ADDR': '127.0.0.1', 'MASTER_PORT': str(port)})
+    from parakeet_cuda_b200.scheduler import WindowScheduler
+    bench = _bench_module()
+    sched = WindowScheduler(backend='gloo', timeout_s=60)
+    # fake timer: 1 ns per row, rank r runs (r + 1) times slower
+    pts = bench.sweep_local(sched.rank, sched.world, lambda n, k, rows: rows * 1e-9 * (sched.rank + 1))
+    parts = sched.gather([pts])
+    peaks = {'bf16_tflops_sustained': 1000.0, 'hbm_gbs': 5000.0}
+    q.put((sched.rank, bench.merge_sweep(parts, peaks) if sched.rank == 0 else None))
+    sched.close()
+
+
+def test_sweep_m_sharded_over_two_gloo_ranks():
+    """Each rank times only its share of M; rank 0 merges the gathered points,
+    a point lasting as long as its slowest rank, with the roofline over the
+    GPUs that had rows."""
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        port = s.getsockname()[1]
+    bench = _bench_module()
+    world = 2
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_sweep_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    merged = out[0]
+    assert out[1] is None
+    assert [(p['n'], p['k'], p['m']) for p in merged] == [(n, k, m) for n, k in bench.SWEEP_SHAPES
+                                                         for m in bench.SWEEP_M]
+    for p in merged:
+        shares = [bench.shard_rows(p['m'], r, world)[1] for r in range(world)]
+        assert p['gpus'] == sum(1 for c in shares if c)
+        assert abs(p['us'] - max(c * 1e-3 * (r + 1) for r, c in enumerate(shares))) < 1e-9
+        assert p['bound'] in ('hbm', 'tensor') and p['frac_of_roofline'] > 0
+    one = [p for p in merged if p['m'] == 1]
+    assert all(p['gpus'] == 1 for p in one)
