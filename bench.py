@@ -51,8 +51,9 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
     ap.add_argument('--tdt-batches', default='1,64', help='decode batch sizes of the tdt extra')
-    ap.add_argument('--extras', default='gemv,cublas,tdt,sweep,load,block,refgpu',
-                    help='comma list of side measurements to run (gemv, cublas, tdt, sweep, load, block, refgpu)')
+    ap.add_argument('--extras', default='config0,gemv,cublas,tdt,sweep,load,block,refgpu,cpu',
+                    help=('comma list of side measurements to run (config0, gemv, cublas, tdt, sweep, load, block, '
+                          'refgpu, cpu)'))
     return ap.parse_args()
 
 
@@ -173,16 +174,77 @@ def all_blas_threads():
     return threadpool_limits(limits=host_cores(), user_api='blas')
 
 
+def one_blas_thread():
+    from threadpoolctl import threadpool_limits
+    return threadpool_limits(limits=1, user_api='blas')
+
+
 def cpu_sample(model, rows=WINDOW_FRAMES, repeats=3):
+    """Config 2 on the host: the reference's NumPy path with the BLAS pool at every
+    usable core (the reported baseline) and at one thread (``single_thread``)."""
     from oracle.cpu_path import blas_threads, time_layer_window
     with all_blas_threads():
         times = [time_layer_window(model, rows, layer=0, seed=i) for i in range(repeats)]
         cores = blas_threads()
+    with one_blas_thread():
+        t1 = time_layer_window(model, rows, layer=0, seed=9)
     t = min(times)
     return {'value': rows / (t * 24), 'unit': UNIT, 'cores': cores, 'kind': 'port',
             'sample': (f'NumPy restatement of the reference CPU path (gguf.array Q8_0 decode + FP32 x @ W.T, '
                        f'reference.py:37): one layer x one {rows}-frame window, best of {repeats} '
-                       f'({t:.3f} s), scaled to 24 layers')}
+                       f'({t:.3f} s), scaled to 24 layers'),
+            'single_thread': {'value': rows / (t1 * 24), 'unit': UNIT, 'cores': 1,
+                              'sample': f'the same layer x window once at OPENBLAS threads = 1 ({t1:.3f} s)'},
+            'host_cpus': host_cores(), 'cpu_model': cpu_model()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path('/proc/cpuinfo').read_text().splitlines():
+            if line.startswith('model name'):
+                return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    return 'unknown'
+
+
+def cpu_other_configs():
+    """CPU baselines of the other BASELINE configs (reference NumPy path restated in
+    oracle/cpu_path.py), each at every usable core and at one BLAS thread, on
+    bounded samples: config 0 (one Q8_0 linear, M=128, K=1024, N=4096), config 3
+    (the reference's float32 CPUDecoder driven by its greedy loop; the reference
+    decodes streams one after another, so batch 64 runs at the batch-1 rate per
+    joint call) and config 4 (the sweep shapes at M up to 1024; larger M is a
+    proportionally longer matmul)."""
+    import numpy as np
+    from oracle.cpu_path import blas_threads, time_decode, time_linear
+    from parakeet_cuda_b200.synthetic import DECODER_SCALE, SyntheticParakeet, q8_0_blocks
+    out = {}
+    raw0 = q8_0_blocks(np.random.default_rng(0), 4096, 1024)
+    model = SyntheticParakeet(seed=11, encoder_layers=0)
+    proj = np.random.default_rng(2026).normal(size=(400, 640)).astype(np.float32)
+    for label, ctx in (('all_cores', all_blas_threads), ('one_thread', one_blas_thread)):
+        with ctx():
+            cores = blas_threads()
+            t0 = time_linear(raw0, 4096, 1024, 128, repeats=5)
+            td, calls = time_decode(model, [proj], [0, 1, 2, 3, 4])
+            sweep = []
+            for n, k in SWEEP_SHAPES:
+                raw = q8_0_blocks(np.random.default_rng(n + k), n, k)
+                for m in (1, 16, 128, 1024):
+                    t = time_linear(raw, n, k, m, repeats=3)
+                    sweep.append({'m': m, 'n': n, 'k': k, 'us': t * 1e6, 'gflops': 2 * m * n * k / t / 1e9,
+                                  'gbs': (1.0625 * n * k + 4 * m * (n + k)) / t / 1e9})
+        out[label] = {
+            'cores': cores,
+            'config0': {'us': t0 * 1e6, 'gflops': 2 * 128 * 4096 * 1024 / t0 / 1e9,
+                        'sample': 'x @ W.T, M=128 K=1024 N=4096, weight decoded beforehand, best of 5'},
+            'config3': {'joint_calls': calls, 'seconds': td, 'joint_calls_per_s': calls / td,
+                        'sample': ('one stream of 400 projected frames through the greedy loop with the float32 '
+                                   'CPUDecoder restatement; steps/s at batch 1 = joint calls/s')},
+            'config4': sweep,
+        }
+    return out
 
 
 def run_reference(args):
@@ -241,6 +303,7 @@ class LaunchTimer:
 
 
 def run_gpu(args):
+    import numpy as np
     import torch
     from parakeet_cuda_b200.encoder import LAYER_PLAN, EncoderStack
     from parakeet_cuda_b200.runtime import Runtime
@@ -267,6 +330,10 @@ def run_gpu(args):
     ref_raw = None
     if not args.no_extras and 'refgpu' in args.extras.split(','):
         ref_raw = upload_raw_layers(torch, model, args.layers, dev)
+    # the same stack on the torch-free host layer (driver API + ctypes): the e2e path
+    from parakeet_cuda_b200.host import EncoderStackHost, HostRuntime
+    hrt = HostRuntime(dev)
+    hstack = EncoderStackHost(model, hrt, rows, layers=args.layers, seed=1 + sched.rank)
     del model
     torch.cuda.synchronize()
 
@@ -325,10 +392,48 @@ def run_gpu(args):
     del graph_rnd
     status = rt.device_status()
 
-    # e2e: public host API, pinned H2D of each step's input and D2H of its result in the timed
-    # region. The headline uses run_host_pipelined (copies of neighbouring steps overlap the
-    # compute; two host buffers per direction in rotation); one run_host per step, copies and
-    # compute back to back, is reported beside it.
+    # e2e: the public host API without PyTorch (EncoderStackHost: driver-API memory and
+    # streams, a cuStreamBeginCapture graph), page-locked H2D of each step's input and D2H of
+    # its result inside the timed region. The headline uses run_host_pipelined (copies of
+    # neighbouring steps overlap the compute; two host buffers per direction in rotation);
+    # one run_host per step, copies and compute back to back, is reported beside it.
+    from parakeet_cuda_b200.cuda_driver import Event as DrvEvent, PinnedArray
+    hstack.step()
+    hrt.synchronize()
+    hgraph = hstack.capture()
+    hx = [PinnedArray(hrt.drv, (rows, 1024)) for _ in range(2)]
+    hout = [PinnedArray(hrt.drv, (rows, 1024)) for _ in range(2)]
+    for i, a in enumerate(hx):
+        a.array[...] = np.random.default_rng(100 + i).standard_normal((rows, 1024), np.float32)
+    h_in = [hx[i % 2] for i in range(args.steps)]
+    h_out = [hout[i % 2] for i in range(args.steps)]
+    for _ in range(2):
+        hstack.run_host(hx[0], hout[0], hgraph)
+    hstack.run_host_pipelined(h_in[:2], h_out[:2], hgraph)
+    hrt.synchronize()
+    sched.barrier()
+    d0, d1 = DrvEvent(hrt.drv), DrvEvent(hrt.drv)
+    d0.record(hrt.stream)
+    hstack.run_host_pipelined(h_in, h_out, hgraph)
+    d1.record(hrt.stream)
+    d1.synchronize()
+    e2e_host_ms = sched.max_over_ranks(d0.elapsed_ms(d1) / args.steps)
+    sched.barrier()
+    d0.record(hrt.stream)
+    for i in range(args.steps):
+        hstack.run_host(h_in[i], h_out[i], hgraph)
+    d1.record(hrt.stream)
+    d1.synchronize()
+    e2e_host_serial_ms = sched.max_over_ranks(d0.elapsed_ms(d1) / args.steps)
+    h_launches = hstack.launches_per_step
+    hgraph.close()
+    hstack.close()
+    for a in hx + hout:
+        a.close()
+    hrt.close()
+    del hstack, hrt
+
+    # the same public calls on the PyTorch-hosted stack, for comparison
     x_hosts = [torch.randn(rows, 1024).pin_memory() for _ in range(2)]
     out_hosts = [torch.empty(rows, 1024).pin_memory() for _ in range(2)]
     step_in = [x_hosts[i % 2] for i in range(args.steps)]
@@ -361,6 +466,8 @@ def run_gpu(args):
             extras['gemv'] = gemv_measure(torch, rt, stack)
         if 'cublas' in wanted:
             extras['tf32_cublas_tflops'] = cublas_tf32(torch)
+        if 'config0' in wanted:
+            extras['config0'] = config0_measure(torch, rt)
         if 'tdt' in wanted:
             extras['tdt'] = tdt_measure(torch, rt, [int(b) for b in args.tdt_batches.split(',')])
         if 'sweep' in wanted:
@@ -386,7 +493,9 @@ def run_gpu(args):
         # timed region (gaps between launches included).
         launch_ms = ms / stack.launches_per_step
         achieved = flops_step / (ms / 1e3) / 1e12
-        peak = peaks['bf16_tflops_sustained'] / 2
+        # the timed region is args.steps graph replays (a fraction of a second):
+        # the burst peak applies; the sustained one is reported beside it
+        peak = peaks['bf16_tflops'] / 2
         shapes = {}
         for entry in LAYER_PLAN:
             name, _, nn, kk = entry[:4]
@@ -407,9 +516,12 @@ def run_gpu(args):
                 'traffic': traffic.get('bytes_per_launch') if traffic else None,
                 'traffic_unit': 'DRAM bytes per launch (mean of the 9 linears; ncu capture)',
                 'traffic_bytes_per_step': traffic.get('bytes_per_step_24_layers') if traffic else None,
-                'peak_source': (f'{peak_src}: MEASURED_PEAKS.json bf16_tflops_sustained / 2 (dense TF32 is half '
-                                f'the BF16 rate); kernel timed inside a long step'),
-                'frac_of_burst': achieved / (peaks['bf16_tflops'] / 2),
+                'peak_source': (f'{peak_src}: MEASURED_PEAKS.json bf16_tflops / 2 (burst; dense TF32 is half '
+                                f'the BF16 rate; timed region {args.steps * ms / 1e3:.2f} s)'),
+                'frac_of_sustained': achieved / (peaks['bf16_tflops_sustained'] / 2),
+                'cublas_tf32_tflops': extras.get('tf32_cublas_tflops'),
+                'frac_of_cublas_tf32': (achieved / extras['tf32_cublas_tflops']
+                                        if extras.get('tf32_cublas_tflops') else None),
                 'kernel': 'pq8::gemm_tc_kernel (all 9 encoder linears)',
                 'flops_per_step': flops_step, 'launches_per_step': stack.launches_per_step,
                 'launch_ms_mean': launch_ms,
@@ -420,13 +532,16 @@ def run_gpu(args):
                                             'per_shape': shapes},
                 'traffic_source': traffic.get('source') if traffic else None,
             },
-            'e2e': {'value': frames / (e2e_ms / 1e3), 'unit': UNIT, 'h2d_bytes_per_step': rows * 1024 * 4,
-                    'd2h_bytes_per_step': rows * 1024 * 4, 'gpu_launches_per_step': stack.launches_per_step + 1,
-                    'api': ('parakeet_cuda_b200.encoder.EncoderStack.run_host_pipelined (pinned host in/out; '
-                            'each step copies its own input and result, overlapped with the neighbouring '
-                            'steps\' compute)'),
-                    'serial': {'value': frames / (e2e_serial_ms / 1e3),
-                               'api': 'EncoderStack.run_host once per step (copies not overlapped)'}},
+            'e2e': {'value': frames / (e2e_host_ms / 1e3), 'unit': UNIT, 'h2d_bytes_per_step': rows * 1024 * 4,
+                    'd2h_bytes_per_step': rows * 1024 * 4, 'gpu_launches_per_step': h_launches + 1,
+                    'api': ('parakeet_cuda_b200.host.EncoderStackHost.run_host_pipelined: no PyTorch (CUDA driver '
+                            'API through ctypes, page-locked host in/out, cuStreamBeginCapture graph); each step '
+                            'copies its own input and result, overlapped with the neighbouring steps\' compute'),
+                    'serial': {'value': frames / (e2e_host_serial_ms / 1e3),
+                               'api': 'EncoderStackHost.run_host once per step (copies not overlapped)'},
+                    'torch_hosted': {'value': frames / (e2e_ms / 1e3),
+                                     'serial': frames / (e2e_serial_ms / 1e3),
+                                     'api': 'parakeet_cuda_b200.encoder.EncoderStack.run_host_pipelined / run_host'}},
             'gpu_launches': stack.launches_per_step * args.steps,
             'device_status': status,
             'x_rounding': ('GEMM inputs from outside the path (LayerNorm output, attention context, positional '
@@ -439,11 +554,98 @@ def run_gpu(args):
         if clock_info:
             line['clocks'] = clock_info
         line.update(extras)
+        if 'full_block' in extras:
+            fb = extras['full_block']
+            line['model_level'] = {
+                'value': fb['frames_per_s'] * n, 'unit': UNIT, 'with_stem': fb['encoder_with_stem_frames_per_s'] * n,
+                'what': ('whole FastConformer blocks (LayerNorms, rel-pos attention, conv module and the same Q8_0 '
+                         'linears), 24 layers over this GPU\'s windows, one graph replay per step; with_stem adds '
+                         'the subsampling stem from 8x mel frames'),
+                'gpus_measured': 'rank 0 (every rank runs the same shapes)'}
         if n == 1 and not args.no_cpu_baseline:
             from parakeet_cuda_b200.synthetic import SyntheticParakeet as SP
             line['cpu_baseline'] = cpu_sample(SP(seed=0, encoder_layers=1, decoder=False))
+            if not args.no_extras and 'cpu' in args.extras.split(','):
+                line['cpu_baseline']['other_configs'] = cpu_other_configs()
         print(json.dumps(line), flush=True)
     sched.close()
+
+
+# the reference's own GEMM benchmark shapes (M, K, N) and its published GTX 750 Ti
+# times in microseconds, direct q8_gemm and dequant_q8 + cuBLAS SGEMM
+# (analysis/CUDA_RESULTS.md:117-120, analysis/benchmark_dense.py)
+REFERENCE_SHAPES = ((1, 32, 3, 5.216, 4.416), (17, 640, 65, 104.926, 21.688), (33, 1024, 129, 194.363, 40.280),
+                    (441, 1024, 4096, 14971.336, 4701.824))
+
+
+def config0_measure(torch, rt):
+    """BASELINE config 0 (X [128, 1024] ~ N(0, 1), W [4096, 1024] Q8_0, scales
+    U[1e-3, 2e-2]) through pq8_linear, and the reference's own benchmark shapes.
+
+    ``warm``: a CUDA graph of 20 back-to-back launches (the 4.4 MB weight stays in
+    L2), ``cold``: one launch at a time after writing a 256 MB buffer (L2
+    flushed), each bracketed by CUDA events. Roofline time = the larger of the
+    FLOPs over the burst TF32 peak and the algorithmic bytes over HBM bandwidth."""
+    import numpy as np
+    from parakeet_cuda_b200.synthetic import q8_0_blocks
+    peaks, src = measured_peaks()
+    p_tf32, bw = peaks['bf16_tflops'] / 2 * 1e12, peaks['hbm_gbs'] * 1e9
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=rt.device)
+
+    def point(m, k, n, seed):
+        rng = np.random.default_rng(seed)
+        w = rt.pack(q8_0_blocks(rng, n, k), n, k)
+        x = torch.from_numpy(rng.normal(size=(m, k)).astype(np.float32)).to(rt.device)
+        y = torch.empty(m, n, device=rt.device)
+        for _ in range(3):
+            rt.linear(x, w, out=y)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(rt.device)
+        side.wait_stream(torch.cuda.current_stream(rt.device))
+        reps = 20
+        with torch.cuda.stream(side):
+            g.capture_begin()
+            for _ in range(reps):
+                rt.linear(x, w, out=y)
+            g.capture_end()
+        torch.cuda.current_stream(rt.device).wait_stream(side)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(5):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        warm_us = a.elapsed_time(b) * 1e3 / (5 * reps)
+        cold = []
+        for _ in range(10):
+            flush.fill_(1)
+            a.record()
+            rt.linear(x, w, out=y)
+            b.record()
+            torch.cuda.synchronize()
+            cold.append(a.elapsed_time(b) * 1e3)
+        del g
+        flops = 2 * m * n * k
+        nbytes = 1.0625 * n * k + 4 * m * k + 4 * m * n
+        t_roof = max(flops / p_tf32, nbytes / bw) * 1e6
+        cold_us = statistics.median(cold)
+        return {'m': m, 'k': k, 'n': n, 'warm_us': warm_us, 'cold_us': cold_us,
+                'warm_tflops': flops / warm_us / 1e6, 'cold_tflops': flops / cold_us / 1e6,
+                'roofline_us': t_roof, 'frac_warm': t_roof / warm_us, 'frac_cold': t_roof / cold_us,
+                'bound': 'hbm' if nbytes / bw > flops / p_tf32 else 'tensor'}
+
+    out = point(128, 1024, 4096, 0)
+    out['peak_source'] = f'{src}: bf16_tflops / 2 (burst TF32), hbm_gbs'
+    out['reference_benchmark_shapes'] = []
+    for m, k, n, direct_us, sgemm_us in REFERENCE_SHAPES:
+        r = point(m, k, n, 903 + m)
+        r['gtx750ti_us'] = {'q8_gemm_direct': direct_us, 'dequant_sgemm': sgemm_us}
+        out['reference_benchmark_shapes'].append(r)
+    del flush
+    return out
 
 
 def gemv_measure(torch, rt, stack):
@@ -696,7 +898,7 @@ def merge_sweep(parts, peaks):
     the active GPUs' TF32 peak and its bytes (each active GPU reads the whole
     Q8_0 matrix, 1.0625 N K, plus its rows of X and Y) over their HBM
     bandwidth; AI = FLOPs / bytes."""
-    p_tf32, bw = peaks['bf16_tflops_sustained'] / 2 * 1e12, peaks['hbm_gbs'] * 1e9
+    p_tf32, bw = peaks['bf16_tflops'] / 2 * 1e12, peaks['hbm_gbs'] * 1e9  # 10-launch points: burst peak
     res = []
     for pts in zip(*parts):
         m, n, k = pts[0]['m'], pts[0]['n'], pts[0]['k']

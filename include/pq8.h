@@ -254,7 +254,10 @@ PQ8_API int pq8_tdt_advance(const int* ids, const int* durations, int n_duration
  * (cudaGetSymbolAddress) and should come before any stream capture. All calls
  * on a device share the array: calls that overlap on the GPU race, so order
  * them (one stream). Each call clears the array's counters itself, and calls
- * no cudaMalloc/cudaFree. Results equal pq8_gemv's for the same inputs. */
+ * no cudaMalloc/cudaFree. Results equal pq8_gemv's for the same inputs, bit
+ * for bit. The array's address (like the status word every entry point uses)
+ * is cached per device and does not survive cudaDeviceReset or a release of
+ * the primary context: do not call the library on a device after resetting it. */
 PQ8_API int pq8_gemv_static(const void* w, const float* x, float* y, const float* bias, const float* resid,
                             int m, int n, int k, int epilogue, float alpha, void* stream);
 

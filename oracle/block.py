@@ -109,8 +109,9 @@ def conv_module_depthwise(w: BlockWeights, gate):
     return silu(y)
 
 
-def block(x, w: BlockWeights):
-    """One block over one window ``x`` [t, 1024]; float64 throughout."""
+def block(x, w: BlockWeights, final_norm: bool = True):
+    """One block over one window ``x`` [t, 1024]; float64 throughout. With
+    ``final_norm=False`` the residual stream before ``norm_out`` is returned."""
     x = np.asarray(x, np.float64)
     t = x.shape[0]
     lin = w.lin
@@ -125,14 +126,17 @@ def block(x, w: BlockWeights):
     gate = pw[:, :1024] * (1.0 / (1.0 + np.exp(-np.clip(pw[:, 1024:], -80, 80))))
     x = x + conv_module_depthwise(w, gate) @ lin['conv.pointwise_conv2'].T
     x = ff(x, 2)
-    return layer_norm(x, *w.ln['norm_out'])
+    return layer_norm(x, *w.ln['norm_out']) if final_norm else x
 
 
-def blocks(x, model, layers, windows: int = 1):
-    """``layers`` blocks over ``windows`` independent windows stacked in ``x`` [windows * t, 1024]."""
+def blocks(x, model, layers, windows: int = 1, final_norm: bool = True):
+    """``layers`` blocks over ``windows`` independent windows stacked in ``x`` [windows * t, 1024]
+    (the last block stops before its ``norm_out`` when ``final_norm`` is False)."""
     x = np.asarray(x, np.float64)
     t = x.shape[0] // windows
-    for layer in layers:
+    layers = list(layers)
+    for j, layer in enumerate(layers):
         w = BlockWeights(model, layer)
-        x = np.concatenate([block(x[i * t:(i + 1) * t], w) for i in range(windows)])
+        last = final_norm or j + 1 < len(layers)
+        x = np.concatenate([block(x[i * t:(i + 1) * t], w, last) for i in range(windows)])
     return x

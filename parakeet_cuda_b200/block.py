@@ -99,8 +99,10 @@ class EncoderBlocks:
         self.rt.gemm(x, self.linears[l][name], out=out, resid=resid, epilogue=epi, alpha=alpha,
                      flags=flags | FLAG_X_TF32)
 
-    def layer(self, l: int) -> None:
-        """One block on the residual stream ``buf['x']`` (reference.py:33-66)."""
+    def layer(self, l: int, final_norm: bool = True) -> None:
+        """One block on the residual stream ``buf['x']`` (reference.py:33-66).
+        ``final_norm=False`` leaves out the block's last LayerNorm (``norm_out``)
+        and keeps the residual stream as it stands before it."""
         b, p, lib, st = self.buf, self.params[l], self.rt.lib, self.rt.stream()
         self._ln(l, 'norm_feed_forward1', 'x', 'norm')
         self._gemm(l, 'ffn1_up', 'norm', 'hidden')
@@ -122,16 +124,19 @@ class EncoderBlocks:
         self._ln(l, 'norm_feed_forward2', 'x', 'norm')
         self._gemm(l, 'ffn2_up', 'norm', 'hidden')
         self._gemm(l, 'ffn2_down', 'hidden', 'x')
-        self._ln(l, 'norm_out', 'x', 'x', tf32=False)  # the block's output, next block's input
+        if final_norm:
+            self._ln(l, 'norm_out', 'x', 'x', tf32=False)  # the block's output, next block's input
 
-    def step(self) -> None:
+    def step(self, final_norm: bool = True) -> None:
+        """Every layer; ``final_norm=False`` stops the last one before its ``norm_out``."""
         for l in range(self.layers):
-            self.layer(l)
+            self.layer(l, final_norm or l + 1 < self.layers)
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """``x`` [windows * t, 1024] (device) through every layer; returns the output stream."""
+    def forward(self, x: torch.Tensor, final_norm: bool = True) -> torch.Tensor:
+        """``x`` [windows * t, 1024] (device) through every layer; returns the output stream
+        (before the last layer's ``norm_out`` when ``final_norm`` is False)."""
         self.buf['x'].copy_(x)
-        self.step()
+        self.step(final_norm)
         return self.buf['x']
 
     def capture(self) -> torch.cuda.CUDAGraph:

@@ -133,6 +133,34 @@ def test_blocks_match_reference_golden(rt, model, golden_dir, t, layers):
     assert rt.device_status() == 0
 
 
+def test_blocks_config1_length_match_oracle(rt, model):
+    """One and two blocks over 8 windows of T = 375 frames (the config-1 window
+    length, as the benchmark's whole-block leg runs them) against the float64
+    oracle. The residual stream before a block's norm_out is its unit-RMS
+    input plus four branch outputs, each ending in a GEMM (FFN down,
+    linear_out, pointwise_conv2): after one block it is held to the north-star
+    bar, max |err| <= 2e-3 x RMS; after two blocks to twice that, since the
+    second block starts from the first block's output with that error. The
+    LayerNormed outputs are held to the whole-block bar above."""
+    windows, t = 8, 375
+    x = np.random.default_rng(375).normal(size=(windows * t, 1024)).astype(np.float32)
+    gold_in = np.asarray(x, np.float64)
+    for layers, bar in ((1, 2e-3), (2, 4e-3)):
+        blocks = EncoderBlocks(model, rt, windows, t, layers=layers)
+        pre = blocks.forward(dev(x), final_norm=False).cpu().numpy()
+        post = blocks.forward(dev(x)).cpu().numpy()
+        gold_pre = ob.blocks(gold_in, model, [layers - 1], windows=windows, final_norm=False)
+        gold_post = ob.layer_norm(gold_pre, *ob.BlockWeights(model, layers - 1).ln['norm_out'])
+        e_pre = _rel_max(pre, gold_pre)
+        mx, rms = _block_errors(post, gold_post)
+        print(f'8 x 375, {layers} layer(s): before norm_out max err / rms {e_pre:.2e}; '
+              f'output max {mx:.2e} rms {rms:.2e}')
+        assert e_pre <= bar, (layers, e_pre)
+        assert mx <= 1e-2 and rms <= 2e-3, (layers, mx, rms)
+        gold_in = gold_post
+    assert rt.device_status() == 0
+
+
 def test_blocks_windows_are_independent(rt, model):
     """Three windows in one stream give each window's own result: the depthwise
     convolution and the attention stop at window boundaries."""

@@ -187,6 +187,37 @@ def test_tdt_device_loop_matches_host_loop(rt, batch):
         assert g == w
 
 
+# A float32 decode may break a tie the float64 oracle decides by less than
+# this (logits are O(1); their FP32 error is ~1e-6).
+TIE_EPS = 1e-4
+
+
+def test_tdt_device_loop_batch64_1000_steps_matches_oracle(rt):
+    """BASELINE config 3 at batch 64: 64 streams of 1400 frames, at least 1000
+    joint calls each, through the device-resident loop, against the float64
+    oracle (oracle.tdt.greedy_decode_streams, Decoder64 arithmetic per stream).
+    Every call's (frame, token, skip) must agree; a different call is accepted
+    only as a near-tie (the device's token and duration within TIE_EPS of the
+    oracle's best logits), counted, and adopted by the oracle."""
+    model = SyntheticParakeet(seed=11, encoder_layers=0)
+    rng = np.random.default_rng(2027)
+    projected = [rng.normal(size=(1400, 640)).astype(np.float32) for _ in range(64)]
+    got = greedy_decode_device(projected, PQ8Decoder(model, rt, batch=64), DURATIONS, steps_per_graph=16)
+    ref = otdt.greedy_decode_streams(projected, model, DURATIONS, follow=[g['decode_trace'] for g in got],
+                                     tie_eps=TIE_EPS)
+    ties = 0
+    for i, (g, r) in enumerate(zip(got, ref)):
+        assert r['mismatch'] is None, (i, r['mismatch'])
+        assert g['decode_trace'] == r['decode_trace'], i
+        assert g['tokens'] == r['tokens'], i
+        assert g['joint_calls'] == r['joint_calls'] >= 1000, (i, g['joint_calls'])
+        ties += r['ties']
+    calls = sum(g['joint_calls'] for g in got)
+    print(f'batch 64: {calls} joint calls, {ties} near-ties decided by float32 rounding')
+    assert ties <= 8
+    assert rt.device_status() == 0
+
+
 def test_tdt_device_loop_step_limit(rt):
     """max_steps stops the loop after exactly that many lock-step steps."""
     model = SyntheticParakeet(seed=11, encoder_layers=0)

@@ -9,9 +9,11 @@ same bits; a GEMM that touched its input or output too early would not.
 The numerics of each linear against the oracle are covered in
 test_gpu_linear.py.
 """
+import numpy as np
 import pytest
 import torch
 
+from oracle import q8
 from parakeet_cuda_b200.encoder import LAYER_PLAN, EncoderStack
 from parakeet_cuda_b200.runtime import Runtime
 from parakeet_cuda_b200.synthetic import SyntheticParakeet
@@ -82,4 +84,59 @@ def test_pipelined_host_steps_match_serial(use_graph):
             assert torch.equal(got, exp), i
     assert not torch.equal(want[0], want[1])
     del graph
+    assert rt.device_status() == 0
+
+
+def test_chained_stack_rows_match_float64_chain():
+    """Two layers of the config-2 stack (3000 rows, every linear with its fused
+    epilogue, the residual stream carried through 8 residual updates): sampled
+    rows of every output against the same chain in float64 from the decoded
+    Q8_0 weights and the stack's own stand-in inputs. North-star bar on each
+    output, max |err| <= 2e-3 x RMS (the GLU output through its first-order
+    bound, the SiLU hidden state with SiLU's Lipschitz factor 1.1). The hidden
+    state and the GLU output are written TF32-rounded for the next GEMM
+    (PQ8_FLAG_OUT_TF32), which adds up to half a TF32 ulp, 2^-11 |y|, per
+    element on top of the bar."""
+    rt = Runtime(0)
+    model = SyntheticParakeet(seed=7, encoder_layers=2, decoder=False)
+    rows, layers = 3000, 2
+    stack = EncoderStack(model, rt, rows, layers=layers, seed=4)
+    stack.buffers['resid'].zero_()
+    stack.step()
+    torch.cuda.synchronize()
+    got = {k: v.cpu().numpy() for k, v in stack.buffers.items()}
+    pick = np.random.default_rng(3000).choice(rows, 48, replace=False)
+    norm, ctx, pos = (got[k][pick].astype(np.float64) for k in ('norm', 'ctx', 'pos'))
+    weights = {}
+    for name, keys, n, k, *_ in LAYER_PLAN:
+        for l in range(layers):
+            parts = [q8.decode(model.raw(f'encoder.layers.{l}.{key}.weight'), n // len(keys), k) for key in keys]
+            weights[l, name] = np.concatenate(parts)
+    silu = lambda z: z * q8.sigmoid(z)
+    x = np.zeros((len(pick), 1024))
+    for l in range(layers):
+        w = lambda name: weights[l, name]
+        h1 = silu(norm @ w('ffn1_up').T)
+        x = x + 0.5 * (h1 @ w('ffn1_down').T)
+        qkv = norm @ w('qkv').T
+        pos_out = pos @ w('pos').T
+        x = x + ctx @ w('out').T
+        z = norm @ w('pw1_glu').T
+        gate = z[:, :1024] * q8.sigmoid(z[:, 1024:])
+        x = x + gate @ w('pw2').T
+        h2 = silu(norm @ w('ffn2_up').T)
+        x = x + 0.5 * (h2 @ w('ffn2_down').T)
+    ulp = 2.0 ** -11
+    errs = {'resid': q8.max_err_over_rms(got['resid'][pick], x),
+            'qkv': q8.max_err_over_rms(got['qkv'][pick], qkv),
+            'pos_out': q8.max_err_over_rms(got['pos_out'][pick], pos_out)}
+    z_up = norm @ weights[layers - 1, 'ffn2_up'].T
+    bound = 1.1 * 2e-3 * q8.rms(z_up) + ulp * np.abs(h2)
+    errs['hidden (x bound)'] = float(np.max(np.abs(got['hidden'][pick] - h2) / bound)) * 2e-3
+    s = q8.sigmoid(z[:, 1024:])
+    bound = 1.05 * 2e-3 * q8.rms(z) * (s + np.abs(z[:, :1024]) * s * (1 - s)) + ulp * np.abs(gate) + 1e-9 * q8.rms(z)
+    errs['gate (x bound)'] = float(np.max(np.abs(got['gate'][pick] - gate) / bound)) * 2e-3
+    print({k: f'{v:.2e}' for k, v in errs.items()})
+    for name, e in errs.items():
+        assert e <= 2e-3, (name, e)
     assert rt.device_status() == 0

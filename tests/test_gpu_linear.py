@@ -49,7 +49,23 @@ def contract_cases():
 
 # Lipschitz factor of each epilogue with respect to the GEMM output z: the
 # north-star bar applies to z, so an epilogue may scale the error by this much.
+# GLU has no constant factor (its gradient grows with |a|); glu_bar below
+# bounds it element by element.
 LIPSCHITZ = {EPI_NONE: 1.0, EPI_RELU: 1.0, EPI_SILU: 1.1, EPI_RESIDUAL: 1.0, EPI_GLU: None}
+
+
+def glu_bar(z):
+    """North-star bar carried through GLU, per output element: with
+    y = a * sigmoid(b) and |da|, |db| <= 2e-3 * rms(z) (the bar on the GEMM
+    output z = [a | b]), |dy| <= 2e-3 * rms(z) * (sigmoid(b) + |a| sigmoid'(b))
+    to first order; 5 % covers the second-order term at this error size. The
+    floor of 1e-6 of the bar admits FP32's sigmoid underflowing to 0 where
+    b < -88 and the exact output is below 1e-36."""
+    h = z.shape[1] // 2
+    a, b = z[:, :h], z[:, h:]
+    s = q8.sigmoid(b)
+    bar = NORTH_STAR * q8.rms(z)
+    return 1.05 * bar * (s + np.abs(a) * s * (1.0 - s)) + 1e-6 * bar
 
 
 def check_gemm(y, x, raw, n, k, epi=EPI_NONE, bias=None, resid=None, alpha=1.0):
@@ -67,6 +83,9 @@ def check_gemm(y, x, raw, n, k, epi=EPI_NONE, bias=None, resid=None, alpha=1.0):
     assert e_tf <= TF32_EXACT, (e_gold, e_tf)
     if LIPSCHITZ[epi] is not None:
         assert e_gold <= NORTH_STAR * LIPSCHITZ[epi] * (alpha if epi == EPI_RESIDUAL else 1.0), (e_gold, e_tf)
+    else:
+        ratio = float(np.max(np.abs(y - gold) / glu_bar(z_gold)))
+        assert ratio <= 1.0, (ratio, e_gold, e_tf)
     return e_gold, e_tf
 
 
@@ -147,6 +166,18 @@ def test_gemm_epilogues(rt, epi, cfg, monkeypatch):
     y = dev(resid) if epi == EPI_RESIDUAL else None
     y = rt.gemm(dev(x), w, out=y, bias=dev(bias), resid=y, epilogue=epi, alpha=0.5)
     check_gemm(y, x, raw, n, k, epi, bias, resid, 0.5)
+
+
+def test_gemm_glu_pointwise_conv1_shape(rt):
+    """pointwise_conv1 of a config-1 layer (M = 375, N = 2048, K = 1024) with the
+    GLU epilogue, held element by element to the north-star bar carried through
+    GLU, in the tile configuration the library picks."""
+    rng = np.random.default_rng(2048)
+    m, n, k = 375, 2048, 1024
+    raw = q8_0_blocks(rng, n, k)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    y = rt.gemm(dev(x), rt.pack(raw, n, k, LAYOUT_GLU), epilogue=EPI_GLU)
+    check_gemm(y, x, raw, n, k, EPI_GLU)
 
 
 @pytest.mark.parametrize('cfg', CONFIGS)
