@@ -103,7 +103,7 @@ def _sweep_worker(rank, world, port, q):
     # fake timer: 1 ns per row, rank r runs (r + 1) times slower
     pts = bench.sweep_local(sched.rank, sched.world, lambda n, k, rows: rows * 1e-9 * (sched.rank + 1))
     parts = sched.gather([pts])
-    peaks = {'bf16_tflops_sustained': 1000.0, 'hbm_gbs': 5000.0}
+    peaks = {'bf16_tflops': 1200.0, 'bf16_tflops_sustained': 1000.0, 'hbm_gbs': 5000.0}
     q.put((sched.rank, bench.merge_sweep(parts, peaks) if sched.rank == 0 else None))
     sched.close()
 
