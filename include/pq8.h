@@ -261,6 +261,51 @@ PQ8_API int pq8_tdt_advance(const int* ids, const int* durations, int n_duration
 PQ8_API int pq8_gemv_static(const void* w, const float* x, float* y, const float* bias, const float* resid,
                             int m, int n, int k, int epilogue, float alpha, void* stream);
 
+/* ---- GEMM sequences ----------------------------------------------------------
+ * Many pq8_gemm calls as one persistent launch: the encoder issues one
+ * Blas.linear per linear per layer (encoder.py:15-36,75-84,115-127 via
+ * gpu.py:87-90); here a whole list of them becomes one kernel whose CTAs (one
+ * per SM) run the tiles of every GEMM in list order. Tiles of a GEMM start as
+ * soon as the 192-row blocks they read are complete, instead of after the
+ * previous GEMM has finished everywhere, so neither a launch's ramp-up and
+ * drain nor its last partial wave of tiles is paid per GEMM. Each task has
+ * pq8_gemm's arguments and meaning, and all tasks of a sequence carry the
+ * same PQ8_FLAG_X_TF32 setting; every tile runs the BN = 192 single-CTA
+ * configuration. */
+typedef struct pq8_gemm_task {
+  const void* w;      /* packed Q8_0 weight [n, k] */
+  const float* x;     /* activations [m, k], 16-byte aligned */
+  float* y;           /* output [m, n] ([m, n/2] for PQ8_EPI_GLU) */
+  const float* bias;  /* [n] or NULL */
+  const float* resid; /* PQ8_EPI_RESIDUAL: [m, out] (may equal y); else NULL */
+  int m, n, k, epilogue;
+  float alpha;
+  int flags;          /* PQ8_FLAG_X_TF32 | PQ8_FLAG_OUT_TF32 */
+  int after;          /* -1, or an earlier task whose output rows this task's x depends on although the
+                         buffers do not show it (a LayerNorm or attention run outside the sequence) */
+  int after_window;   /* 0: the same rows of `after`; W > 0: all rows of the W-row windows that a tile's
+                         rows belong to (e.g. attention over windows of W frames) */
+} pq8_gemm_task;
+
+/* Bytes of device memory the plan of `tasks` needs. */
+PQ8_API int pq8_sequence_plan_size(const pq8_gemm_task* tasks, int count, size_t* bytes);
+/* Lay out the plan of `tasks` in `plan` (device memory, 256-byte aligned):
+ * parameters, tensor maps and the dependencies between tasks. Dependencies
+ * come from the buffers: a task that reads x or resid rows waits for the last
+ * earlier task that wrote them, and a task that writes y waits for the
+ * earlier tasks that wrote or read those rows. Buffers are identified by
+ * their start address and row width; two that overlap otherwise are refused
+ * (PQ8_ERR_UNSUPPORTED_SHAPE), as is a task with more than 4 dependencies of
+ * either kind. Reads each weight's packed header (PQ8_ERR_LAYOUT on a
+ * mismatch) and synchronizes `stream`; not for stream capture. The plan stays
+ * valid while the buffers and weights it names do. */
+PQ8_API int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* plan, size_t plan_bytes, void* stream);
+/* Run a plan: one launch (one CTA per SM) that computes every task. Runs of
+ * one plan must not overlap on the GPU (its completion counters are shared and
+ * reset by each run's last CTA). A dependency wait that expires records
+ * PQ8_ERR_TIMEOUT (pq8_device_status); the plan is then to be made again. */
+PQ8_API int pq8_sequence_run(const void* plan, void* stream);
+
 /* Read and clear the device-side status word that kernels set on a layout
  * mismatch or an expired bounded wait. Synchronizes `stream`. *status = 0 or
  * PQ8_ERR_LAYOUT / PQ8_ERR_TIMEOUT. */

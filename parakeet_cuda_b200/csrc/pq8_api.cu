@@ -8,6 +8,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "pq8.h"
 #include "pq8_device.cuh"
@@ -111,7 +112,7 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return PQ8_ERR_DRIVER;
   }
-  auto kernel = gemm_tc_kernel<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES>;
+  auto kernel = gemm_tc_kernel<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES, false>;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
     if (!ds->attr_set[cfg_id]) {
@@ -141,7 +142,7 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap, tmap_y, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmap, tmap_y, p, static_cast<const uint8_t*>(nullptr));
   if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }
@@ -567,6 +568,255 @@ extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bi
     case kP192: return launch_gemm<192, 8, 4, 2, true, 2, 8>(ds, kP192, x, p, st);
     default: return launch_gemm<128, 10, 4, 2, true, 2, 8>(ds, kP128, x, p, st);
   }
+}
+
+// ---------------------------------------------------------------- GEMM sequences
+// Every tile of a sequence runs in the single-CTA BN = 192 configuration with
+// two accumulators (the epilogue of one tile overlaps the next tile's MMAs).
+namespace pq8 {
+namespace {
+
+constexpr int kSeqBN = 192, kSeqStages = 5, kSeqSlots = 4, kSeqAcc = 2, kSeqWStages = 8;
+using SeqCfg = GemmCfg<kSeqBN, kSeqStages, kSeqSlots, kSeqAcc, false, 2, 4, 32, kSeqWStages>;
+constexpr int kSeqCfgId = 15;  // DeviceState::attr_set slot of the sequence kernel
+constexpr size_t kSeqHeaderBytes = sizeof(SeqPlanHeader);
+
+struct SeqLayout {
+  size_t tasks_offset, counters_offset, total;
+  int n_counters, total_tiles;
+};
+
+int seq_layout(const pq8_gemm_task* tasks, int count, SeqLayout* out) {
+  if (tasks == nullptr || count < 1) return PQ8_ERR_INVALID_ARGUMENT;
+  long long counters = 0, tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const pq8_gemm_task& t = tasks[i];
+    int rc = check_linear_args(t.w, t.x, t.y, t.resid, t.m, t.n, t.k, t.epilogue);
+    if (rc) return rc;
+    if (t.m < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
+    if (!aligned(t.x, 16)) return PQ8_ERR_MISALIGNED;
+    if (t.flags & ~(PQ8_FLAG_X_TF32 | PQ8_FLAG_OUT_TF32)) return PQ8_ERR_INVALID_ARGUMENT;
+    if (t.after >= i || t.after < -1 || t.after_window < 0) return PQ8_ERR_INVALID_ARGUMENT;
+    // one activation-rounding mode per sequence (the converters and the scheduler share it)
+    if ((t.flags & PQ8_FLAG_X_TF32) != (tasks[0].flags & PQ8_FLAG_X_TF32)) return PQ8_ERR_INVALID_ARGUMENT;
+    const long long m_tiles = (t.m + kSeqBN - 1) / kSeqBN, n_tiles = (t.n + kTileRows - 1) / kTileRows;
+    counters += m_tiles;
+    tiles += m_tiles * n_tiles;
+  }
+  if (tiles > (1LL << 30) || counters > (1LL << 30)) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  // a tile's task, weight tile, row block and K blocks travel as 16-bit fields
+  if (count > 0xFFFF) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  for (int i = 0; i < count; ++i)
+    if ((tasks[i].m + kSeqBN - 1) / kSeqBN > 0xFFFF || (tasks[i].n + kTileRows - 1) / kTileRows > 0xFFFF ||
+        tasks[i].k / 32 > 0xFFFF)
+      return PQ8_ERR_UNSUPPORTED_SHAPE;
+  out->tasks_offset = kSeqHeaderBytes;
+  out->counters_offset = round256(kSeqHeaderBytes + sizeof(SeqTask) * static_cast<size_t>(count));
+  out->n_counters = static_cast<int>(counters);
+  out->total_tiles = static_cast<int>(tiles);
+  out->total = round256(out->counters_offset + sizeof(int) * static_cast<size_t>(counters));
+  return PQ8_OK;
+}
+
+// A buffer as the sequence sees it: rows of `width` floats starting at `base`.
+struct Region {
+  uintptr_t base;
+  size_t bytes;
+  int width;
+};
+bool overlaps(const Region& a, const Region& b) { return a.base < b.base + b.bytes && b.base < a.base + a.bytes; }
+
+int add_dep(SeqDep* deps, int* n, int task, int window) {
+  for (int i = 0; i < *n; ++i)
+    if (deps[i].task == task && deps[i].window == window) return PQ8_OK;
+  if (*n == kSeqMaxDeps) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  deps[(*n)++] = SeqDep{task, window};
+  return PQ8_OK;
+}
+
+// Dependencies from the buffers each task reads (x, resid) and writes (y).
+// A region is identified by its base address and row width; regions that
+// overlap without being the same rows are refused (row blocks would not line
+// up). For each region the last writer and the readers since are tracked:
+// a reader depends on the last writer (read-after-write), a writer on the
+// last writer (write-after-write) and on every reader since (write-after-read).
+int seq_dependencies(const pq8_gemm_task* tasks, int count, std::vector<SeqTask>& out) {
+  struct State {
+    Region r;
+    int writer;
+    std::vector<int> readers;
+  };
+  std::vector<State> regions;
+  auto find = [&](const Region& r, int* idx) -> int {
+    for (size_t i = 0; i < regions.size(); ++i) {
+      if (!overlaps(regions[i].r, r)) continue;
+      if (regions[i].r.base != r.base || regions[i].r.width != r.width) return PQ8_ERR_UNSUPPORTED_SHAPE;
+      if (r.bytes > regions[i].r.bytes) regions[i].r.bytes = r.bytes;
+      *idx = static_cast<int>(i);
+      return PQ8_OK;
+    }
+    regions.push_back(State{r, -1, {}});
+    *idx = static_cast<int>(regions.size()) - 1;
+    return PQ8_OK;
+  };
+  for (int j = 0; j < count; ++j) {
+    const pq8_gemm_task& t = tasks[j];
+    SeqTask& st = out[j];
+    const int out_cols = t.epilogue == PQ8_EPI_GLU ? t.n / 2 : t.n;
+    const Region rx{reinterpret_cast<uintptr_t>(t.x), sizeof(float) * (size_t)t.m * t.k, t.k};
+    const Region ry{reinterpret_cast<uintptr_t>(t.y), sizeof(float) * (size_t)t.m * out_cols, out_cols};
+    int ix, iy, ir = -1, rc;
+    if ((rc = find(rx, &ix))) return rc;
+    if ((rc = find(ry, &iy))) return rc;
+    if (t.epilogue == PQ8_EPI_RESIDUAL) {
+      const Region rr{reinterpret_cast<uintptr_t>(t.resid), ry.bytes, out_cols};
+      if ((rc = find(rr, &ir))) return rc;
+    }
+    if (ix == iy) return PQ8_ERR_UNSUPPORTED_SHAPE;  // a GEMM cannot overwrite its own input rows
+    if (regions[ix].writer >= 0 && (rc = add_dep(st.x_dep, &st.n_x_deps, regions[ix].writer, 0))) return rc;
+    if (t.after >= 0 && (rc = add_dep(st.x_dep, &st.n_x_deps, t.after, t.after_window))) return rc;
+    if (ir >= 0 && regions[ir].writer >= 0 && (rc = add_dep(st.out_dep, &st.n_out_deps, regions[ir].writer, 0)))
+      return rc;
+    if (regions[iy].writer >= 0 && (rc = add_dep(st.out_dep, &st.n_out_deps, regions[iy].writer, 0))) return rc;
+    for (int rd : regions[iy].readers)
+      if (rd != j && (rc = add_dep(st.out_dep, &st.n_out_deps, rd, 0))) return rc;
+    regions[ix].readers.push_back(j);
+    if (ir >= 0 && ir != iy) regions[ir].readers.push_back(j);
+    regions[iy].writer = j;
+    regions[iy].readers.clear();
+  }
+  return PQ8_OK;
+}
+
+}  // namespace
+}  // namespace pq8
+
+extern "C" int pq8_sequence_plan_size(const pq8_gemm_task* tasks, int count, size_t* bytes) {
+  if (bytes == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  SeqLayout L;
+  int rc = seq_layout(tasks, count, &L);
+  if (rc) return rc;
+  *bytes = L.total;
+  return PQ8_OK;
+}
+
+extern "C" int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* plan, size_t plan_bytes,
+                                 void* stream) {
+  SeqLayout L;
+  int rc = seq_layout(tasks, count, &L);
+  if (rc) return rc;
+  if (plan == nullptr || plan_bytes < L.total) return PQ8_ERR_WORKSPACE;
+  if (!aligned(plan, 256)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  if ((rc = device_state(&ds))) return rc;
+  EncodeTiledFn enc;
+  if ((rc = encode_fn(&enc))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<SeqTask> host(count);
+  std::memset(host.data(), 0, sizeof(SeqTask) * host.size());
+  if ((rc = seq_dependencies(tasks, count, host))) return rc;
+  int tile0 = 0, counter = 0;
+  for (int i = 0; i < count; ++i) {
+    const pq8_gemm_task& t = tasks[i];
+    SeqTask& q = host[i];
+    // the packed header must describe this task's weight (checked here, not per tile)
+    PackedHeader h;
+    cudaError_t e = cudaMemcpy(&h, t.w, sizeof(h), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return to_code(e);
+    const int layout = t.epilogue == PQ8_EPI_GLU ? PQ8_LAYOUT_GLU : PQ8_LAYOUT_ROWS;
+    const int n_tiles = (t.n + kTileRows - 1) / kTileRows;
+    if (h.magic != kMagic || h.n != t.n || h.k != t.k || h.layout != layout || h.n_tiles != n_tiles)
+      return PQ8_ERR_LAYOUT;
+    GemmParams& p = q.p;
+    p.w = static_cast<const uint8_t*>(t.w);
+    p.y = t.y;
+    p.bias = t.bias;
+    p.resid = t.resid;
+    p.status = ds->status;
+    p.m = t.m;
+    p.n = t.n;
+    p.k = t.k;
+    p.epi = t.epilogue;
+    p.alpha = t.alpha;
+    p.flags = t.flags;
+    p.layout = layout;
+    p.out_cols = t.epilogue == PQ8_EPI_GLU ? t.n / 2 : t.n;
+    p.n_tiles = n_tiles;
+    p.k_blocks = t.k / 32;
+    p.m_tiles = (t.m + kSeqBN - 1) / kSeqBN;
+    p.tma_store = (p.out_cols % 4 == 0) && aligned(t.y, 16);
+    q.tile0 = tile0;
+    q.n_units = n_tiles;
+    q.counter = counter;
+    tile0 += p.m_tiles * n_tiles;
+    counter += p.m_tiles;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(t.k), static_cast<cuuint64_t>(t.m)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(t.k) * sizeof(float)};
+    const cuuint32_t box[2] = {32, static_cast<cuuint32_t>(kSeqBN)};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&q.tmap_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(t.x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return PQ8_ERR_DRIVER;
+    if (p.tma_store) {
+      const cuuint64_t ydims[2] = {static_cast<cuuint64_t>(p.out_cols), static_cast<cuuint64_t>(t.m)};
+      const cuuint64_t ystrides[1] = {static_cast<cuuint64_t>(p.out_cols) * sizeof(float)};
+      const cuuint32_t ybox[2] = {static_cast<cuuint32_t>(t.epilogue == PQ8_EPI_GLU ? 64 : 128), 32};
+      if (enc(&q.tmap_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, t.y, ydims, ystrides, ybox, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return PQ8_ERR_DRIVER;
+    }
+  }
+  std::vector<uint8_t> blob(L.total, 0);
+  SeqPlanHeader hdr{};
+  hdr.magic = kSeqMagic;
+  hdr.count = count;
+  hdr.total_tiles = L.total_tiles;
+  hdr.n_counters = L.n_counters;
+  hdr.bn = kSeqBN;
+  hdr.finished = 0;
+  hdr.tasks_offset = static_cast<long long>(L.tasks_offset);
+  hdr.counters_offset = static_cast<long long>(L.counters_offset);
+  std::memcpy(blob.data(), &hdr, sizeof(hdr));
+  std::memcpy(blob.data() + L.tasks_offset, host.data(), sizeof(SeqTask) * host.size());
+  cudaError_t e = cudaMemcpyAsync(plan, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return to_code(e);
+}
+
+extern "C" int pq8_sequence_run(const void* plan, void* stream) {
+  if (plan == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(plan, 256)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  auto kernel = gemm_tc_kernel<kSeqBN, kSeqStages, kSeqSlots, kSeqAcc, false, 2, 4, 32, kSeqWStages, true>;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!ds->attr_set[kSeqCfgId]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SeqCfg::kSmemBytes);
+      if (e != cudaSuccess) return to_code(e);
+      ds->attr_set[kSeqCfgId] = true;
+    }
+  }
+  CUtensorMap unused;
+  std::memset(&unused, 0, sizeof(unused));
+  GemmParams p{};
+  p.status = ds->status;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ds->sms);  // one persistent CTA per SM; all must be resident (dependencies span CTAs)
+  cfg.blockDim = dim3(SeqCfg::kThreads);
+  cfg.dynamicSmemBytes = SeqCfg::kSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, unused, unused, p, static_cast<const uint8_t*>(plan));
+  if (e != cudaSuccess) return to_code(e);
+  return to_code(cudaGetLastError());
 }
 
 extern "C" int pq8_gemv_workspace_size(int m, int n, int k, size_t* bytes) {

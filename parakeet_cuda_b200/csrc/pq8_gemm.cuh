@@ -177,12 +177,205 @@ __device__ __forceinline__ void expand16_tf32(const uint4 q, uint32_t sbits, boo
   }
 }
 
+// ---------------------------------------------------------------------------
+// GEMM sequences: one persistent launch runs the tiles of many GEMMs.
+//
+// The host lays a plan out in device memory (pq8_sequence_plan): a header,
+// one SeqTask per GEMM (its parameters, tensor maps and dependencies) and one
+// completion counter per (task, 192-row block). Tiles are numbered task after
+// task, and within a task N-unit fastest, so a task's row blocks complete in
+// order. CTA c runs tiles c, c + grid, c + 2 grid, ... Before a tile's
+// activations are loaded, its X dependencies must have completed the row
+// blocks the tile reads; before its epilogue reads the residual or writes the
+// output, its output dependencies must have (write-after-read,
+// write-after-write, and the residual's read-after-write). Every dependency
+// points to an earlier task and every CTA runs its tiles in order, so the
+// lowest unfinished tile can always make progress while all CTAs are
+// resident (one per SM). Counters are reset by the last CTA to finish.
+constexpr uint32_t kSeqMagic = 0x51455350u;  // "PSEQ"
+constexpr int kSeqMaxDeps = 4;
+
+struct SeqDep {
+  int task;    // producer task (earlier in the sequence)
+  int window;  // 0: the same row block; W > 0: every row block of the producer that holds rows of the W-row
+               // windows that this tile's rows belong to (e.g. attention over windows between two GEMMs)
+};
+
+struct alignas(128) SeqTask {
+  CUtensorMap tmap_x;  // activations [m, k], box 32 x BN rows
+  CUtensorMap tmap_y;  // output [m, out_cols] (when p.tma_store)
+  GemmParams p;
+  int tile0;     // first tile of this task in the sequence
+  int n_units;   // tiles along N
+  int counter;   // index of this task's first row-block counter
+  int n_x_deps, n_out_deps;
+  SeqDep x_dep[kSeqMaxDeps];
+  SeqDep out_dep[kSeqMaxDeps];
+};
+
+struct alignas(128) SeqPlanHeader {
+  uint32_t magic;
+  int count;        // tasks
+  int total_tiles;
+  int n_counters;
+  int bn;           // rows per tile (all tasks)
+  int finished;     // CTAs done with this run (the last one resets the counters)
+  long long tasks_offset, counters_offset;
+};
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Wait (bounded, like mbar_wait) until counter >= target.
+__device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatile int* abort_flag, int* status) {
+  if (ld_acquire(ctr) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      __nanosleep(128);
+      if (ld_acquire(ctr) >= target) return true;
+    }
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, PQ8_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Row blocks of dependency `d`'s producer that tile row block m_tile needs.
+__device__ __forceinline__ void dep_range(const SeqTask& t, const SeqDep& d, int m_tile, int bn, int* lo, int* hi) {
+  *lo = m_tile;
+  *hi = m_tile;
+  if (d.window > 0) {
+    const int r0 = m_tile * bn, r1 = r0 + bn - 1;
+    *lo = (r0 / d.window) * d.window / bn;
+    *hi = ((r1 / d.window) * d.window + d.window - 1) / bn;
+  }
+  *hi = *hi < t.p.m_tiles - 1 ? *hi : t.p.m_tiles - 1;
+}
+
+// Wait for the row blocks that dependency `d` must have completed before tile
+// rows [row0, row0 + bn) of the consumer may be used.
+__device__ __forceinline__ bool wait_dep(const SeqTask* tasks, int* counters, const SeqDep& d, int m_tile, int bn,
+                                         volatile int* abort_flag, int* status) {
+  const SeqTask& t = tasks[d.task];
+  int lo, hi;
+  dep_range(t, d, m_tile, bn, &lo, &hi);
+  const int target = 2 * t.n_units;  // each tile's two epilogue halves signal once
+  for (int r = lo; r <= hi; ++r)
+    if (!wait_counter(counters + t.counter + r, target, abort_flag, status)) return false;
+  return true;
+}
+
+
+// Where a tile of the launch lies: its GEMM (sequences), weight tile, row block and K blocks.
+struct TileRef {
+  const SeqTask* task;  // sequences only
+  int n_tile, m_tile, kb;
+};
+
+// A role warp's view of its tiles (local index i = the CTA's i-th tile,
+// tile blockIdx + i * grid). For a sequence, the lanes look up 32 tiles at
+// once (lane j holds the entry of tile base + j) and each tile's entry is
+// then two shuffles away: looking a task up in the plan is a chain of global
+// loads, which at every tile boundary would otherwise stall the warp that has
+// to start the next tile. The state is four registers; everything else is
+// re-derived from kernel parameters and special registers. Every lane of the
+// warp must call get() with the same index.
+template <int kCtas, bool SEQ>
+struct TileWindow;
+
+template <int kCtas>
+struct TileWindow<kCtas, false> {
+  int m_tiles, k_blocks;
+  __device__ __forceinline__ TileRef get(int local, uint32_t rank, const uint8_t*) const {
+    const int tile = static_cast<int>(blockIdx.x) / kCtas + local * static_cast<int>(gridDim.x / kCtas);
+    return {nullptr, (tile / m_tiles) * kCtas + static_cast<int>(rank), tile % m_tiles, k_blocks};
+  }
+};
+
+// Looks up the tile of lane (threadIdx & 31) of the window starting at local
+// index `local`; out of line, so that its temporaries do not add to the
+// register pressure of the role loops it is called from (once per 32 tiles).
+__device__ __noinline__ void seq_window_entry(const uint8_t* plan, int local, int* cur, uint32_t* task_n,
+                                              uint32_t* m_kb) {
+  const SeqPlanHeader* hdr = reinterpret_cast<const SeqPlanHeader*>(plan);
+  const SeqTask* tasks = reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader));
+  const int tile =
+      static_cast<int>(blockIdx.x) + (local + static_cast<int>(threadIdx.x & 31)) * static_cast<int>(gridDim.x);
+  if (tile >= hdr->total_tiles) return;
+  const int count = hdr->count;
+  int c = *cur;
+  while (c + 1 < count && tasks[c + 1].tile0 <= tile) ++c;
+  *cur = c;
+  const SeqTask* t = tasks + c;
+  const int u = tile - t->tile0, nu = t->n_units;
+  *task_n = (static_cast<uint32_t>(c) << 16) | static_cast<uint32_t>(u % nu);
+  *m_kb = (static_cast<uint32_t>(u / nu) << 16) | static_cast<uint32_t>(t->p.k_blocks);
+}
+
+template <int kCtas>
+struct TileWindow<kCtas, true> {
+  int cur = 0;     // task of this lane's latest lookup
+  int base = -64;  // local index of lane 0's entry
+  uint32_t e_task_n = 0, e_m_kb = 0;  // this lane's entry, two 16-bit fields each
+  __device__ __forceinline__ TileRef get(int local, uint32_t, const uint8_t* plan) {
+    const SeqTask* tasks = reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader));
+    if (local - base >= 32) {
+      base = local;
+      seq_window_entry(plan, local, &cur, &e_task_n, &e_m_kb);
+    }
+    const int i = local - base;
+    const uint32_t tn = __shfl_sync(0xffffffffu, e_task_n, i), mk = __shfl_sync(0xffffffffu, e_m_kb, i);
+    return {tasks + (tn >> 16), static_cast<int>(tn & 0xFFFFu), static_cast<int>(mk >> 16),
+            static_cast<int>(mk & 0xFFFFu)};
+  }
+};
+
+// Per-thread lookup of a tile (the converters, the epilogue and the
+// producers, which reach a tile boundary well before its data is needed).
+template <int kCtas, bool SEQ>
+struct TileCursor {
+  int m_tiles, k_blocks;  // single GEMM
+  int cur = 0;            // sequence: task of the latest lookup
+  __device__ __forceinline__ TileRef at(int tile, uint32_t rank, const uint8_t* plan) {
+    if constexpr (SEQ) {
+      const SeqPlanHeader* hdr = reinterpret_cast<const SeqPlanHeader*>(plan);
+      const SeqTask* tasks = reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader));
+      const int count = hdr->count;
+      while (cur + 1 < count && tasks[cur + 1].tile0 <= tile) ++cur;
+      const SeqTask* t = tasks + cur;
+      const int u = tile - t->tile0, nu = t->n_units;
+      return {t, u % nu, u / nu, t->p.k_blocks};
+    } else {
+      return {nullptr, (tile / m_tiles) * kCtas + static_cast<int>(rank), tile % m_tiles, k_blocks};
+    }
+  }
+};
+
+// A parameter of the tile's GEMM: the sequence task's, or the launch's own
+// (read straight from the kernel parameters).
+#define PQ8_TP(t, field) (SEQ ? (t).task->p.field : p.field)
+
 template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS = 2, int GROUP_WARPS = 4, int EPI_COLS = 32,
-          int WSTAGES = 4>
+          int WSTAGES = 4, bool SEQ = false>
 __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, GROUP_WARPS, EPI_COLS, WSTAGES>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
-                   const GemmParams p) {
+                   const GemmParams p, const uint8_t* plan) {
   using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, GROUP_WARPS, EPI_COLS, WSTAGES>;
+  static_assert(!(SEQ && PAIR), "sequences run single-CTA tiles");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xs = smem + C::kXOff;
@@ -211,13 +404,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   const int unit0 = blockIdx.x / C::kCtas;          // first work unit of this CTA (pair)
   const int unit_stride = gridDim.x / C::kCtas;
 
+  // Tiles of this launch: one GEMM (p), or every task of a sequence plan.
+  const SeqPlanHeader* hdr = SEQ ? reinterpret_cast<const SeqPlanHeader*>(plan) : nullptr;
+  const SeqTask* tasks = SEQ ? reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader)) : nullptr;
+  int* counters = SEQ ? reinterpret_cast<int*>(const_cast<uint8_t*>(plan) + hdr->counters_offset) : nullptr;
+  const int task_count = SEQ ? hdr->count : 1;
+  const int n_units = PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles;
+  const int num_tiles = SEQ ? hdr->total_tiles : n_units * p.m_tiles;
+  int* const status = p.status;
+
   if (threadIdx.x == 0) {
-    const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
-    const bool ok = h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout &&
-                    h->n_tiles == p.n_tiles;
+    bool ok = true;
+    if constexpr (!SEQ) {  // a sequence's headers are checked when its plan is made
+      const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
+      ok = h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout && h->n_tiles == p.n_tiles;
+    }
     *bad_flag = ok ? 0 : 1;
     *abort_flag = 0;
-    if (!ok) atomicCAS(p.status, 0, PQ8_ERR_LAYOUT);
+    if (!ok) atomicCAS(status, 0, PQ8_ERR_LAYOUT);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&xfull[s], 1);
       mbar_init(&xempty[s], 1);
@@ -237,7 +441,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     mbar_init(drain, 1);
     fence_mbar_init();
   }
-  if (warp == C::kTmaWarp && lane == 0) {
+  if (warp == C::kTmaWarp && lane == 0 && !SEQ) {
     prefetch_tmap(&tmap_x);
     if (p.tma_store) prefetch_tmap(&tmap_y);
   }
@@ -261,11 +465,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   // Arrivals that the leader's MMA waits for go to the leader's barriers.
   const uint32_t conv_remote = PAIR ? map_to_rank(conv, 0) : 0;
   const uint32_t acc_empty_remote = PAIR ? map_to_rank(acc_empty, 0) : 0;
-
-  // Work units: 128 * kCtas weight rows x BN activation rows.
-  const int n_units = PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles;
-  const int num_tiles = n_units * p.m_tiles;
-  const int KB = p.k_blocks;
+  TileCursor<C::kCtas, SEQ> src{p.m_tiles, p.k_blocks};
+  const int x_flags = SEQ ? (task_count > 0 ? tasks[0].p.flags : 0) : p.flags;
   bool mma_issued = false;
 
   if (warp >= C::kConvWarp0 && warp < C::kConvWarp0 + C::kConvWarps) {
@@ -277,11 +478,6 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     const int kpart = (cw >> 2) % (GROUP_WARPS / 4);   // which kValuesPerThread of the 32 K values
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const bool round_x = !(p.flags & PQ8_FLAG_X_TF32);
-    // Who vouches for this CTA's activation stage before the MMA: the
-    // converters when they round it in place or when they are the pair peer's
-    // (whose barriers the leader cannot see); otherwise the scheduler.
-    const bool vouch_x = round_x || (PAIR && !leader);
     // Barrier checks are started early (non-blocking tests) and only waited
     // on when they had not completed, so their round trips overlap the
     // conversion arithmetic.
@@ -292,15 +488,29 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     xr.advance(grp);  // this group's first K block is block `grp`
     wr.advance(grp);
     ar.advance(grp);
+    // Who vouches for this CTA's activation stage before the MMA: the
+    // converters when they round it in place or when they are the pair peer's
+    // (whose barriers the leader cannot see); otherwise the scheduler. (All
+    // tasks of a sequence share the X rounding flag.)
+    const bool round_x = !(x_flags & PQ8_FLAG_X_TF32);
+    const bool vouch_x = round_x || (PAIR && !leader);
     bool w_ready = false;
-    int tile = unit0;
+    int tile = unit0, local = 0;
     uint32_t tile_first = 0;  // index of the current tile's first K block
-    bool has_w = tile < num_tiles && (tile / p.m_tiles) * C::kCtas + static_cast<int>(rank) < p.n_tiles;
+    bool has_w = false;
+    uint32_t kb_tile = 0;
+    auto enter = [&]() {
+      const TileRef t = src.at(tile, rank, plan);
+      has_w = t.n_tile < PQ8_TP(t, n_tiles);
+      kb_tile = static_cast<uint32_t>(t.kb);
+    };
+    if (tile < num_tiles) enter();
     for (uint32_t it = grp;; it += G) {
-      while (it >= tile_first + KB) {
+      while (tile < num_tiles && it >= tile_first + kb_tile) {
         tile += unit_stride;
-        tile_first += KB;
-        has_w = (tile / p.m_tiles) * C::kCtas + static_cast<int>(rank) < p.n_tiles;
+        ++local;
+        tile_first += kb_tile;
+        if (tile < num_tiles) enter();
       }
       if (tile >= num_tiles) break;
       const uint32_t stage = xr.idx, wst = wr.idx, slot = ar.idx;
@@ -309,7 +519,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       // order after this warp's shared-memory loads, so the stage is handed
       // back once the conversion has consumed every loaded value. The
       // conversion runs before the tensor-memory slot is waited for.
-      if (!w_ready && !mbar_wait(&wfull[wst], wr.phase, abort_flag, p.status)) goto conv_done;
+      if (!w_ready && !mbar_wait(&wfull[wst], wr.phase, abort_flag, status)) goto conv_done;
       uint32_t a[C::kValuesPerThread];
       bool slot_ready;
       {
@@ -336,7 +546,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&wempty[wst]);
-      if (!slot_ready && !mbar_wait(&afree[slot], ar.phase ^ 1u, abort_flag, p.status)) goto conv_done;
+      if (!slot_ready && !mbar_wait(&afree[slot], ar.phase ^ 1u, abort_flag, status)) goto conv_done;
       tc_fence_after();
 #pragma unroll
       for (int h = 0; h < C::kValuesPerThread / 16; ++h) {
@@ -347,7 +557,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         tmem_st16(tmem + lane_base + C::kAColBase + slot * 32 + khalf * 16, part);
       }
       if (vouch_x) {
-        if (!mbar_wait(&xfull[stage], xr.phase, abort_flag, p.status)) goto conv_done;
+        if (!mbar_wait(&xfull[stage], xr.phase, abort_flag, status)) goto conv_done;
         if (round_x) {
           uint4* xv = reinterpret_cast<uint4*>(xs + stage * C::kXStageBytes);
           constexpr int kPer = C::kXStageBytes / 16 / C::kGroupThreads;
@@ -393,24 +603,39 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     const int r = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const bool elected = q == 0 && lane == 0;      // issues this half's TMA stores
-    const bool glu = p.epi == PQ8_EPI_GLU;
-    const int box_cols = glu ? 64 : 128;           // output columns of one tile
-    const int c_local = glu ? q * 16 + (lane & 15) : r;
     constexpr int E = C::kEpiCols;
     constexpr int kChunks = BN / E / 2;            // E-column chunks per half
     int chunk_seq = 0;                             // chunks issued by this half (selects the buffer)
     int local = 0;
     griddep_wait();  // the residual and the output may be in use by the previous kernel
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
-      const int n_tile = (tile / p.m_tiles) * C::kCtas + static_cast<int>(rank), m_tile = tile % p.m_tiles;
+      const TileRef t = src.at(tile, rank, plan);
+      const int n_tile = t.n_tile, m_tile = t.m_tile;
+      const int m = PQ8_TP(t, m), n = PQ8_TP(t, n), out_cols = PQ8_TP(t, out_cols), layout = PQ8_TP(t, layout);
+      const int epi = PQ8_TP(t, epi), flags = PQ8_TP(t, flags);
+      const float alpha = PQ8_TP(t, alpha);
+      const bool tma_store = PQ8_TP(t, tma_store) != 0;
+      const float* const bias = PQ8_TP(t, bias);
+      const void* ty = SEQ ? static_cast<const void*>(&t.task->tmap_y) : static_cast<const void*>(&tmap_y);
+      const bool glu = epi == PQ8_EPI_GLU;
+      const int box_cols = glu ? 64 : 128;           // output columns of one tile
+      const int c_local = glu ? q * 16 + (lane & 15) : r;
       const int acc = local % ACC;
       RowMap rm;
-      const bool valid = map_row(p.layout, p.n, n_tile * kTileRows + r, rm);
-      const float b = (p.bias != nullptr && valid) ? p.bias[rm.src] : 0.0f;
+      const bool valid = map_row(layout, n, n_tile * kTileRows + r, rm);
+      const float b = (bias != nullptr && valid) ? bias[rm.src] : 0.0f;
       const bool store_lane = valid && (!glu || lane < 16);
-      float* ycol = p.y + rm.col;
-      const float* rcol = p.resid + rm.col;
-      const bool resid = p.epi == PQ8_EPI_RESIDUAL;
+      float* ycol = PQ8_TP(t, y) + rm.col;
+      const float* rcol = PQ8_TP(t, resid) + rm.col;
+      const bool resid = epi == PQ8_EPI_RESIDUAL;
+      bool dep_ok = true;
+      if constexpr (SEQ) {
+        // write-after-read, write-after-write and the residual's producer
+        const int nd = t.task->n_out_deps;
+        for (int d = 0; d < nd && dep_ok; ++d)
+          dep_ok = wait_dep(tasks, counters, t.task->out_dep[d], m_tile, BN, abort_flag, status);
+        if (!dep_ok) break;
+      }
       // Residual rows are loaded into out[] one chunk ahead: the tile's first
       // chunk before the accumulator is waited for, each next chunk as soon as
       // the previous one has been staged, so their latency is off the critical
@@ -419,23 +644,23 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       auto load_resid = [&](int m0) {
 #pragma unroll
         for (int j = 0; j < E; ++j)
-          out[j] = (store_lane && m0 + j < p.m) ? rcol[(size_t)(m0 + j) * p.out_cols] : 0.0f;
+          out[j] = (store_lane && m0 + j < m) ? rcol[(size_t)(m0 + j) * out_cols] : 0.0f;
       };
       if (resid) load_resid(m_tile * BN + half * kChunks * E);
-      if (!mbar_wait(&acc_full[acc], (local / ACC) & 1, abort_flag, p.status)) break;
+      if (!mbar_wait(&acc_full[acc], (local / ACC) & 1, abort_flag, status)) break;
       tc_fence_after();
 #pragma unroll 1
       for (int cc = 0; cc < kChunks; ++cc, ++chunk_seq) {
         const int c = half * kChunks + cc;
         const int m0 = m_tile * BN + c * E;
-        if (m0 >= p.m) break;
+        if (m0 >= m) break;
         uint32_t v[E];
         tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
         tmem_wait_ld();
-        const int cnt = min(E, p.m - m0);  // warp-uniform
+        const int cnt = min(E, m - m0);  // warp-uniform
         if (resid) {
 #pragma unroll
-          for (int j = 0; j < E; ++j) out[j] = fmaf(p.alpha, __uint_as_float(v[j]) + b, out[j]);
+          for (int j = 0; j < E; ++j) out[j] = fmaf(alpha, __uint_as_float(v[j]) + b, out[j]);
         } else if (glu) {
 #pragma unroll
           for (int j = 0; j < E; ++j) {
@@ -443,21 +668,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
             const float gate = __shfl_down_sync(0xffffffffu, z, 16);
             out[j] = __fdividef(z, 1.0f + __expf(-gate));
           }
-        } else if (p.epi == PQ8_EPI_SILU) {
+        } else if (epi == PQ8_EPI_SILU) {
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = silu_fast(__uint_as_float(v[j]) + b);
-        } else if (p.epi == PQ8_EPI_RELU) {
+        } else if (epi == PQ8_EPI_RELU) {
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = fmaxf(__uint_as_float(v[j]) + b, 0.0f);
         } else {
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = __uint_as_float(v[j]) + b;
         }
-        if (p.flags & PQ8_FLAG_OUT_TF32) {
+        if (flags & PQ8_FLAG_OUT_TF32) {
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = tf32_round(out[j]);
         }
-        if (p.tma_store) {
+        if (tma_store) {
           float* stage = out_stage + (half * 2 + (chunk_seq & 1)) * C::kOutChunkFloats;
           // the store issued from this buffer two chunks ago must have read it
           if (elected) bulk_wait_group_read<1>();
@@ -470,14 +695,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
           named_barrier_sync(1 + half, 128);
           // rows past M and columns past the output width are clipped by the TMA unit
           if (elected) {
-            tma_store_2d(&tmap_y, stage, n_tile * box_cols, m0);
+            tma_store_2d(ty, stage, n_tile * box_cols, m0);
             bulk_commit_group();
           }
         } else if (store_lane) {
-          float* yp = ycol + (size_t)m0 * p.out_cols;
+          float* yp = ycol + (size_t)m0 * out_cols;
 #pragma unroll
           for (int j = 0; j < E; ++j)
-            if (j < cnt) yp[(size_t)j * p.out_cols] = out[j];
+            if (j < cnt) yp[(size_t)j * out_cols] = out[j];
         }
         if (resid && cc + 1 < kChunks) load_resid(m0 + E);
       }
@@ -487,8 +712,22 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         if (PAIR && !leader) mbar_arrive_cluster(acc_empty_remote + acc * 8);
         else mbar_arrive(&acc_empty[acc]);
       }
+      if constexpr (SEQ) {
+        // This half's rows of the tile are written: signal them (once per half).
+        if (tma_store) {
+          if (elected) {
+            bulk_wait_group_all();
+            fence_proxy_async_global();
+            red_release_add(counters + t.task->counter + m_tile, 1);
+          }
+        } else {
+          __threadfence();
+          named_barrier_sync(1 + half, 128);
+          if (elected) red_release_add(counters + t.task->counter + m_tile, 1);
+        }
+      }
     }
-    if (p.tma_store && elected) bulk_wait_group_all();
+    if (elected) bulk_wait_group_all();
   } else if (warp == C::kTmaWarp) {
     // ----------------------------------------------------- activation producer
     if (lane == 0) {
@@ -496,12 +735,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       uint32_t issued = 0;
       Ring<STAGES> xr;
       for (int tile = unit0; tile < num_tiles; tile += unit_stride) {
-        const int m_tile = tile % p.m_tiles;
-        const int row0 = m_tile * BN + static_cast<int>(rank) * C::kRowsPerCta;
-        for (int kb = 0; kb < KB; ++kb, ++issued, xr.advance(1)) {
-          if (!mbar_wait(&xempty[xr.idx], xr.phase ^ 1u, abort_flag, p.status)) goto x_done;
+        const TileRef t = src.at(tile, rank, plan);
+        const int row0 = t.m_tile * BN + static_cast<int>(rank) * C::kRowsPerCta;
+        const void* tx = SEQ ? static_cast<const void*>(&t.task->tmap_x) : static_cast<const void*>(&tmap_x);
+        if constexpr (SEQ) {
+          const int nd = t.task->n_x_deps;
+          bool ok = true;
+          for (int d = 0; d < nd && ok; ++d)
+            ok = wait_dep(tasks, counters, t.task->x_dep[d], t.m_tile, BN, abort_flag, status);
+          if (!ok) goto x_done;
+          fence_proxy_async_global();  // the producers' rows, read by the tensor-copy unit
+        }
+        for (int kb = 0; kb < t.kb; ++kb, ++issued, xr.advance(1)) {
+          if (!mbar_wait(&xempty[xr.idx], xr.phase ^ 1u, abort_flag, status)) goto x_done;
           mbar_expect_tx(&xfull[xr.idx], C::kXStageBytes);
-          tma_load_2d(xs + xr.idx * C::kXStageBytes, &tmap_x, kb * 32, row0, &xfull[xr.idx]);
+          tma_load_2d(xs + xr.idx * C::kXStageBytes, tx, kb * 32, row0, &xfull[xr.idx]);
         }
       }
     x_done:
@@ -515,11 +763,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       uint32_t issued = 0;
       Ring<WSTAGES> wr;
       for (int tile = unit0; tile < num_tiles; tile += unit_stride) {
-        const int n_tile = (tile / p.m_tiles) * C::kCtas + static_cast<int>(rank);
-        const bool has_w = n_tile < p.n_tiles;
-        const uint8_t* wt = p.w + PQ8_HEADER_BYTES + (size_t)n_tile * KB * kRecordBytes;
-        for (int kb = 0; kb < KB; ++kb, ++issued, wr.advance(1)) {
-          if (!mbar_wait(&wempty[wr.idx], wr.phase ^ 1u, abort_flag, p.status)) goto w_done;
+        const TileRef t = src.at(tile, rank, plan);
+        const bool has_w = t.n_tile < PQ8_TP(t, n_tiles);
+        const uint8_t* wt = PQ8_TP(t, w) + PQ8_HEADER_BYTES + (size_t)t.n_tile * t.kb * kRecordBytes;
+        for (int kb = 0; kb < t.kb; ++kb, ++issued, wr.advance(1)) {
+          if (!mbar_wait(&wempty[wr.idx], wr.phase ^ 1u, abort_flag, status)) goto w_done;
           if (has_w) {
             mbar_expect_tx(&wfull[wr.idx], kRecordBytes);
             bulk_g2s(ws + wr.idx * kRecordBytes, wt + (size_t)kb * kRecordBytes, kRecordBytes, &wfull[wr.idx]);
@@ -535,29 +783,32 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   } else if (warp == C::kSchedWarp) {
     // ------------------------------------------------------------- scheduler
     // Does every barrier wait the MMA warp depends on (accumulator free,
-    // K blocks converted) and releases it through a two-warp rendezvous. The
-    // MMA warp itself never touches shared memory in its loop: on this part a
-    // shared-memory access (an mbarrier test included) by the warp that issues
-    // tcgen05.mma is held behind the MMAs that warp has queued, so each wait
-    // there costs a drain of the tensor pipe.
+    // K blocks converted) and releases it through a two-warp rendezvous
+    // every RK K blocks. The MMA warp itself never touches shared memory in
+    // its loop: on this part a shared-memory access (an mbarrier test
+    // included) by the warp that issues tcgen05.mma is held behind the MMAs
+    // that warp has queued, so each wait there costs a drain of the tensor
+    // pipe. The OR of the rendezvous carries an abort flag, so both warps
+    // always meet the same number of times.
     if (leader) {
       constexpr int RK = C::kRendezvousBlocks;
       // The leader's activation stages are vouched for here unless its
       // converters round them in place.
-      const bool sched_x = (p.flags & PQ8_FLAG_X_TF32) != 0;
+      const bool sched_x = (x_flags & PQ8_FLAG_X_TF32) != 0;
       Ring<ASLOTS> ar;
       Ring<STAGES> xr;
       bool bad = false;
       int local = 0;
       for (int tile = unit0; tile < num_tiles && !bad; tile += unit_stride, ++local) {
+        const int KB = src.at(tile, rank, plan).kb;
         const int acc = local % ACC;
-        if (lane == 0) bad = !mbar_wait(&acc_empty[acc], ((local / ACC) & 1) ^ 1, abort_flag, p.status);
+        if (lane == 0) bad = !mbar_wait(&acc_empty[acc], ((local / ACC) & 1) ^ 1, abort_flag, status);
         for (int kb0 = 0; kb0 < KB; kb0 += RK) {
           const int nb = KB - kb0 < RK ? KB - kb0 : RK;
           if (lane == 0)
             for (int b = 0; b < nb && !bad; ++b) {
-              bad = !mbar_wait(&conv[ar.idx], ar.phase, abort_flag, p.status);
-              if (sched_x) bad = bad || !mbar_wait(&xfull[xr.idx], xr.phase, abort_flag, p.status);
+              bad = !mbar_wait(&conv[ar.idx], ar.phase, abort_flag, status);
+              if (sched_x) bad = bad || !mbar_wait(&xfull[xr.idx], xr.phase, abort_flag, status);
               ar.advance(1);
               xr.advance(1);
             }
@@ -574,7 +825,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     // Whole warp: meets the scheduler once per RK K blocks; lane 0 issues.
     // The operands advance incrementally (descriptor start address, slot
     // column, barrier addresses) to keep the issuing lane's instruction
-    // stream short.
+    // stream short. A sequence's tiles differ in their K-block counts; the
+    // tile window reads those of the warp's next 32 tiles at once, since a
+    // memory access by this warp would wait behind the MMAs it has queued.
     if (leader) {
       constexpr uint32_t idesc = idesc_tf32(128 * C::kCtas, BN);
       constexpr int RK = C::kRendezvousBlocks;
@@ -586,7 +839,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       int stage = 0, slot = 0;
       bool stop = false;
       int local = 0;
+      TileWindow<C::kCtas, SEQ> win{};
+      if constexpr (!SEQ) win = TileWindow<C::kCtas, SEQ>{p.m_tiles, p.k_blocks};
       for (int tile = unit0; tile < num_tiles && !stop; tile += unit_stride, ++local) {
+        const int KB = win.get(local, rank, plan).kb;
         const int acc = local % ACC;
         const uint32_t d = tmem + acc * BN;
         for (int kb0 = 0; kb0 < KB; kb0 += RK) {
@@ -648,6 +904,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     if constexpr (PAIR) tmem_dealloc_pair(tmem, C::kTmemCols);
     else tmem_dealloc(tmem, C::kTmemCols);
   }
+  if constexpr (SEQ) {
+    // The last CTA to finish resets the counters for the next run of the plan.
+    int* finished = const_cast<int*>(&hdr->finished);
+    __shared__ int last_cta;
+    if (threadIdx.x == 0) {
+      __threadfence();
+      last_cta = atomicAdd(finished, 1) == static_cast<int>(gridDim.x) - 1;
+    }
+    __syncthreads();
+    if (last_cta) {
+      __threadfence();
+      for (int i = threadIdx.x; i < hdr->n_counters; i += blockDim.x) counters[i] = 0;
+      if (threadIdx.x == 0) *finished = 0;
+      __threadfence();
+    }
+  }
 }
+
+#undef PQ8_TP
 
 }  // namespace pq8

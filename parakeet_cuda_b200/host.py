@@ -30,7 +30,7 @@ import numpy as np
 
 from . import pq8
 from .cuda_driver import Driver, Event, PinnedArray
-from .layers import D_FF, D_MODEL, LAYER_PLAN, flops_per_row_per_layer
+from .layers import D_FF, D_MODEL, FRAMES_PER_WINDOW, LAYER_PLAN, flops_per_row_per_layer
 from .pq8 import EPI_GLU, EPI_RESIDUAL, FLAG_X_TF32, LAYOUT_GATES4, LAYOUT_GLU, LAYOUT_ROWS, LINEAR_GEMV_MAX_M
 
 MIB = 1 << 20
@@ -345,10 +345,59 @@ class EncoderStackHost:
             for entry in LAYER_PLAN:
                 self.launch(l, entry)
 
-    def capture(self):
-        """One ``step`` as a CUDA graph (``cuStreamBeginCapture``). Run ``step`` once
-        first so that per-device library state is set up outside the capture."""
-        return self.rt.stream.capture(self.step)
+    def sequence_tasks(self, dependencies: str = 'model', window: int = FRAMES_PER_WINDOW) -> list:
+        """Every linear of every layer as ``pq8_gemm_task``s, in launch order.
+
+        Dependencies the buffers show (the FFN hidden state, the GLU output, the
+        residual stream, and every rewrite of a buffer) are found by the library.
+        ``dependencies='model'`` adds the ones the stand-in buffers hide, as a
+        whole block would have them: each LayerNorm reads the residual stream as
+        the previous residual linear left it (FFN1 up, QKV, pointwise 1, FFN2 up
+        wait for those rows), and linear_out reads the attention of each window
+        of ``window`` frames (it waits for QKV on all rows of the windows its
+        rows belong to); the positional projection waits for nothing.
+        ``'buffers'`` keeps only the buffer dependencies."""
+        if dependencies not in ('model', 'buffers'):
+            raise ValueError(dependencies)
+        b = self.buffers
+        tasks, index = [], {}
+        last_residual = -1
+        for l in range(self.layers):
+            for name, _, n, k, epi, alpha, src, dst, flags in LAYER_PLAN:
+                after, after_window = -1, 0
+                if dependencies == 'model':
+                    if name in ('ffn1_up', 'qkv', 'pw1_glu', 'ffn2_up'):
+                        after = last_residual
+                    elif name == 'out':
+                        after, after_window = index[l, 'qkv'], window
+                w = self.weights[l][name]
+                resid = b['resid'].pointer if epi == EPI_RESIDUAL else None
+                tasks.append(pq8.GemmTask(w.pointer, b[src].pointer, b[dst].pointer, None, resid, self.rows, n, k,
+                                          epi, alpha, flags | FLAG_X_TF32, after, after_window))
+                index[l, name] = len(tasks) - 1
+                if epi == EPI_RESIDUAL:
+                    last_residual = len(tasks) - 1
+        return tasks
+
+    def make_sequence(self, dependencies: str = 'model') -> Buffer:
+        """Plan every linear of a step as one persistent launch (``pq8_sequence_plan``);
+        ``step_sequence`` runs it."""
+        tasks = self.sequence_tasks(dependencies)
+        nbytes = self.rt.lib.sequence_plan_size(tasks)
+        if getattr(self, '_plan', None) is None or self._plan.nbytes < nbytes:
+            self._plan = Buffer(self.rt.drv.alloc(nbytes), nbytes, (nbytes,), np.uint8)
+        self.rt.lib.sequence_plan(tasks, self._plan.pointer, self._plan.nbytes, self.rt.stream.handle)
+        return self._plan
+
+    def step_sequence(self) -> None:
+        """One step as a single persistent launch of the plan made by ``make_sequence``."""
+        self.rt.lib.call('pq8_sequence_run', self._plan.pointer, self.rt.stream.handle)
+
+    def capture(self, sequence: bool = False):
+        """One step as a CUDA graph (``cuStreamBeginCapture``): the per-linear launches of
+        ``step``, or the single launch of ``step_sequence``. Run the step once first so
+        that per-device library state is set up outside the capture."""
+        return self.rt.stream.capture(self.step_sequence if sequence else self.step)
 
     def _enqueue(self, graph) -> None:
         if graph is not None:
@@ -417,6 +466,9 @@ class EncoderStackHost:
             e.close()
 
     def close(self) -> None:
+        if getattr(self, '_plan', None) is not None:
+            self.rt.drv.free(self._plan.pointer)
+            self._plan = None
         if self._pipe is not None:
             for ptr in self._pipe['in'] + self._pipe['out']:
                 self.rt.drv.free(ptr)

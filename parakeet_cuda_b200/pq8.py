@@ -40,6 +40,13 @@ LINEAR_GEMV_MAX_M = 8    # pq8_linear's GEMV/GEMM dispatch threshold
 
 _P, _I, _F, _SZ, _LL = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_longlong
 
+
+class GemmTask(C.Structure):
+    """``pq8_gemm_task``: one GEMM of a sequence (``pq8_sequence_plan``)."""
+    _fields_ = [('w', _P), ('x', _P), ('y', _P), ('bias', _P), ('resid', _P), ('m', _I), ('n', _I), ('k', _I),
+                ('epilogue', _I), ('alpha', _F), ('flags', _I), ('after', _I), ('after_window', _I)]
+
+
 SIGNATURES = {
     'pq8_error_string': ([_I], C.c_char_p),
     'pq8_version': ([], _I),
@@ -68,6 +75,9 @@ SIGNATURES = {
     'pq8_tdt_control': ([_P, _P, _I, _P, _I, _I, _P, _P, _P, _P, _I, _P, _I, _P, _P], _I),
     'pq8_tdt_advance': ([_P, _P, _I, _P, _I, _I, _P, _P, _P, _P, _I, _P, _I, _P, _P, _P, _P, _P, _I, _I, _P], _I),
     'pq8_device_status': ([C.POINTER(_I), _P], _I),
+    'pq8_sequence_plan_size': ([C.POINTER(GemmTask), _I, C.POINTER(_SZ)], _I),
+    'pq8_sequence_plan': ([C.POINTER(GemmTask), _I, _P, _SZ, _P], _I),
+    'pq8_sequence_run': ([_P, _P], _I),
 }
 
 
@@ -123,6 +133,16 @@ class Library:
         out = _SZ()
         self.call('pq8_attention_workspace_size', windows, t, C.byref(out))
         return out.value
+
+    def sequence_plan_size(self, tasks) -> int:
+        arr = (GemmTask * len(tasks))(*tasks)
+        out = _SZ()
+        self.call('pq8_sequence_plan_size', arr, len(tasks), C.byref(out))
+        return out.value
+
+    def sequence_plan(self, tasks, plan: int, plan_bytes: int, stream=None) -> None:
+        arr = (GemmTask * len(tasks))(*tasks)
+        self.call('pq8_sequence_plan', arr, len(tasks), plan, plan_bytes, stream)
 
     def device_status(self, stream=None) -> int:
         out = _I()
