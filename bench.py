@@ -4,8 +4,8 @@
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N ...
 
-One step = every Q8_0 linear of the 24 FastConformer layers (9 fused GEMM
-launches per layer) over this GPU's windows: 8 windows x 375 frames = 3000
+One step = every Q8_0 linear of the 24 FastConformer layers (9 per layer, run
+as one persistent launch of pq8_sequence_run) over this GPU's windows: 8 windows x 375 frames = 3000
 activation rows per GPU, weights replicated, no collective on the data path
 (weak scaling: 8/16/32/64 windows on 1/2/4/8 GPUs). Rank 0 prints one JSON
 line. The metric is encoder frames per second for the whole job.
@@ -67,6 +67,8 @@ def config(args, n_gpus):
         'layers': args.layers,
         'parallelism': f'windows sharded over {n_gpus} GPU(s), weights replicated, no data-path collective',
         'l2': 'weights streamed per step (642 MB packed Q8_0 > 126 MB L2); no flush needed',
+        'execution': ('one persistent launch per step (pq8_sequence_run): the 216 linears as tiles with '
+                      'row-block dependencies that follow the block\'s data flow'),
         'weights': 'random Q8_0, int8 U[-127,127], fp16 scales U[1e-3,2e-2]; activations N(0,1)',
     }
 
@@ -337,32 +339,53 @@ def run_gpu(args):
     del model
     torch.cuda.synchronize()
 
-    # The timed step is one CUDA-graph replay of all 216 GEMM launches.
-    stack.step()
-    torch.cuda.synchronize()
-    graph = stack.capture()
+    # The timed step: every Q8_0 linear of the 24 layers as ONE persistent launch
+    # (pq8_sequence_run of a plan with the block's data-flow dependencies) on the
+    # torch-free host stack, replayed from a CUDA graph captured with
+    # cuStreamBeginCapture and timed with driver events on its stream.
+    from parakeet_cuda_b200.cuda_driver import Event as DrvEvent, PinnedArray
+    hstack.make_sequence('model')
+    hstack.step_sequence()
+    hrt.synchronize()
+    hgraph = hstack.capture(sequence=True)
     clocks = ClockSampler(n) if sched.rank == 0 else None
     for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
+        hgraph.launch(hrt.stream)
+    hrt.synchronize()
     if clocks:
         clocks.wait_ready()
     sched.barrier()
-
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
+    d0, d1 = DrvEvent(hrt.drv), DrvEvent(hrt.drv)
+    hrt.synchronize()
     sched.barrier()
     if clocks:
         clocks.mark()
+    d0.record(hrt.stream)
+    for _ in range(args.steps):
+        hgraph.launch(hrt.stream)
+    d1.record(hrt.stream)
+    d1.synchronize()
+    sched.barrier()
+    clock_info = clocks.stop() if clocks else None
+    ms = d0.elapsed_ms(d1) / args.steps
+    ms_max = sched.max_over_ranks(ms)
+
+    # The same linears as one launch each (216 launches, programmatic dependent
+    # launch between them, graph replay): the launch-per-linear step, beside it.
+    stack.step()
+    torch.cuda.synchronize()
+    graph = stack.capture()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    sched.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
         graph.replay()
     end.record()
     torch.cuda.synchronize()
-    sched.barrier()
-    clock_info = clocks.stop() if clocks else None
-    ms = start.elapsed_time(end) / args.steps
-    ms_max = sched.max_over_ranks(ms)
+    ms_launches = sched.max_over_ranks(start.elapsed_time(end) / args.steps)
 
     # Per-shape context: the same launches issued eagerly, each bracketed by
     # CUDA events on the launching stream (the events break the overlap of
@@ -393,14 +416,10 @@ def run_gpu(args):
     status = rt.device_status()
 
     # e2e: the public host API without PyTorch (EncoderStackHost: driver-API memory and
-    # streams, a cuStreamBeginCapture graph), page-locked H2D of each step's input and D2H of
+    # streams, the sequence graph), page-locked H2D of each step's input and D2H of
     # its result inside the timed region. The headline uses run_host_pipelined (copies of
     # neighbouring steps overlap the compute; two host buffers per direction in rotation);
     # one run_host per step, copies and compute back to back, is reported beside it.
-    from parakeet_cuda_b200.cuda_driver import Event as DrvEvent, PinnedArray
-    hstack.step()
-    hrt.synchronize()
-    hgraph = hstack.capture()
     hx = [PinnedArray(hrt.drv, (rows, 1024)) for _ in range(2)]
     hout = [PinnedArray(hrt.drv, (rows, 1024)) for _ in range(2)]
     for i, a in enumerate(hx):
@@ -412,7 +431,6 @@ def run_gpu(args):
     hstack.run_host_pipelined(h_in[:2], h_out[:2], hgraph)
     hrt.synchronize()
     sched.barrier()
-    d0, d1 = DrvEvent(hrt.drv), DrvEvent(hrt.drv)
     d0.record(hrt.stream)
     hstack.run_host_pipelined(h_in, h_out, hgraph)
     d1.record(hrt.stream)
@@ -425,7 +443,7 @@ def run_gpu(args):
     d1.record(hrt.stream)
     d1.synchronize()
     e2e_host_serial_ms = sched.max_over_ranks(d0.elapsed_ms(d1) / args.steps)
-    h_launches = hstack.launches_per_step
+    seq_status = hrt.device_status()
     hgraph.close()
     hstack.close()
     for a in hx + hout:
@@ -488,10 +506,9 @@ def run_gpu(args):
     if sched.rank == 0:
         peaks, peak_src = measured_peaks()
         flops_step = stack.flops_per_step()
-        # The timed step is the GEMM launches and nothing else, so its duration
-        # over the launch count is the kernel's average launch duration in the
-        # timed region (gaps between launches included).
-        launch_ms = ms / stack.launches_per_step
+        # The timed step is one launch of the sequence kernel and nothing else,
+        # so the step time is that kernel's average launch duration.
+        launch_ms = ms
         achieved = flops_step / (ms / 1e3) / 1e12
         # the timed region is args.steps graph replays (a fraction of a second):
         # the burst peak applies; the sustained one is reported beside it
@@ -522,34 +539,42 @@ def run_gpu(args):
                 'cublas_tf32_tflops': extras.get('tf32_cublas_tflops'),
                 'frac_of_cublas_tf32': (achieved / extras['tf32_cublas_tflops']
                                         if extras.get('tf32_cublas_tflops') else None),
-                'kernel': 'pq8::gemm_tc_kernel (all 9 encoder linears)',
-                'flops_per_step': flops_step, 'launches_per_step': stack.launches_per_step,
+                'kernel': ('pq8::gemm_tc_kernel, sequence form (every tile of the 216 linears of a step in one '
+                           'persistent launch)'),
+                'flops_per_step': flops_step, 'launches_per_step': 1,
                 'launch_ms_mean': launch_ms,
-                'achieved_basis': ('algorithmic FLOPs per step / timed graph step (CUDA events on the launching '
-                                   'stream; the step is only the GEMM launches)'),
+                'achieved_basis': ('algorithmic FLOPs per step / timed graph step (driver events on the launching '
+                                   'stream; the step is the one sequence launch)'),
+                'per_linear_launches': {'ms_per_step': ms_launches, 'launches_per_step': stack.launches_per_step,
+                                        'tflops': flops_step / (ms_launches / 1e3) / 1e12,
+                                        'frac': flops_step / (ms_launches / 1e3) / 1e12 / peak,
+                                        'frames_per_s': rows * n / (ms_launches / 1e3),
+                                        'what': 'the same linears as one pq8_gemm launch each (PDL, graph replay)'},
                 'eager_isolated_launches': {'kernel_ms_per_step': kernel_ms_step,
                                             'tflops': flops_step / (kernel_ms_step / 1e3) / 1e12,
                                             'per_shape': shapes},
                 'traffic_source': traffic.get('source') if traffic else None,
             },
             'e2e': {'value': frames / (e2e_host_ms / 1e3), 'unit': UNIT, 'h2d_bytes_per_step': rows * 1024 * 4,
-                    'd2h_bytes_per_step': rows * 1024 * 4, 'gpu_launches_per_step': h_launches + 1,
+                    'd2h_bytes_per_step': rows * 1024 * 4, 'gpu_launches_per_step': 2,
                     'api': ('parakeet_cuda_b200.host.EncoderStackHost.run_host_pipelined: no PyTorch (CUDA driver '
-                            'API through ctypes, page-locked host in/out, cuStreamBeginCapture graph); each step '
+                            'API through ctypes, page-locked host in/out, cuStreamBeginCapture graph of the '
+                            'sequence launch; one pq8_round_tf32 launch per step on the uploaded input); each step '
                             'copies its own input and result, overlapped with the neighbouring steps\' compute'),
                     'serial': {'value': frames / (e2e_host_serial_ms / 1e3),
                                'api': 'EncoderStackHost.run_host once per step (copies not overlapped)'},
                     'torch_hosted': {'value': frames / (e2e_ms / 1e3),
                                      'serial': frames / (e2e_serial_ms / 1e3),
                                      'api': 'parakeet_cuda_b200.encoder.EncoderStack.run_host_pipelined / run_host'}},
-            'gpu_launches': stack.launches_per_step * args.steps,
-            'device_status': status,
+            'gpu_launches': args.steps,
+            'device_status': status or seq_status,
             'x_rounding': ('GEMM inputs from outside the path (LayerNorm output, attention context, positional '
                            'table stand-ins) are produced TF32-rounded; SiLU/GLU outputs are rounded by the fused '
                            'epilogue; e2e rounds its uploaded input with one pq8_round_tf32 launch per step'),
             'in_kernel_rounding': {'ms_per_step': ms_kernel_rounding,
                                    'value': frames / (ms_kernel_rounding / 1e3),
-                                   'note': 'same step with every GEMM rounding its own X tile (no producer help)'},
+                                   'note': ('the launch-per-linear step with every GEMM rounding its own X tile '
+                                            '(no producer help)')},
         }
         if clock_info:
             line['clocks'] = clock_info
