@@ -531,7 +531,7 @@ def run_gpu(args):
                 'bound': 'tensor', 'achieved': achieved,
                 'peak': peak, 'unit': 'TFLOP/s', 'frac': achieved / peak,
                 'traffic': traffic.get('bytes_per_launch') if traffic else None,
-                'traffic_unit': 'DRAM bytes per launch (mean of the 9 linears; ncu capture)',
+                'traffic_unit': 'DRAM bytes per launch (one sequence launch = the whole step; ncu capture)',
                 'traffic_bytes_per_step': traffic.get('bytes_per_step_24_layers') if traffic else None,
                 'peak_source': (f'{peak_src}: MEASURED_PEAKS.json bf16_tflops / 2 (burst; dense TF32 is half '
                                 f'the BF16 rate; timed region {args.steps * ms / 1e3:.2f} s)'),
