@@ -357,11 +357,12 @@ PQ8_API int pq8_rel_attention(const float* qkv, const float* pos, const float* p
  * projected by the Q8_0 output linear: out float[windows * t][1024] with
  * t = ceil(ceil(ceil(frames / 2) / 2) / 2) rows per window. w0, w2, w5:
  * float[256][9] (the GGUF's fp16 kernels as float); w3, w6: float[256][256]
- * (output channel major); b*: float[256]; w_out: packed Q8_0 [1024, 4096]
- * (ROWS), b_out: float[1024]. The pointwise products go to cuBLAS (TF32, or
- * FP32 with PQ8_FLAG_FP32_PRODUCTS); everything else is pq8 kernels and
- * pq8_gemm. Replaces conv_first, conv_dw2, the stem SGEMMs, bias_act and
- * flatten_stem (runtime.cu:73-101). */
+ * (output channel major, 16-byte aligned); b*: float[256]; w_out: packed Q8_0
+ * [1024, 4096] (ROWS), b_out: float[1024]. The pointwise products run on the
+ * pq8 tensor-core kernel with the FP32 weights rounded to TF32 (with
+ * PQ8_FLAG_FP32_PRODUCTS: FP32 cuBLAS products, an exactness reference);
+ * everything else is pq8 kernels and pq8_gemm. Replaces conv_first, conv_dw2,
+ * the stem SGEMMs, bias_act and flatten_stem (runtime.cu:73-101). */
 PQ8_API int pq8_stem_workspace_size(int windows, int frames, size_t* bytes);
 PQ8_API int pq8_stem(const float* mel, int windows, int frames, const float* w0, const float* b0, const float* w2,
                      const float* b2, const float* w3, const float* b3, const float* w5, const float* b5,

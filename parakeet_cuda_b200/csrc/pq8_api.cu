@@ -147,6 +147,30 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   return to_code(cudaGetLastError());
 }
 
+// The tensor-core kernel on a dense row-major FP32 weight [n, k] (k a multiple
+// of 32, 16-byte aligned rows): the converters round the weights to TF32
+// (nearest-even) instead of expanding Q8_0 records. Used for the stem's
+// pointwise convolutions, whose weights are FP32 in the model.
+int gemm_dense_f32(DeviceState* ds, const float* w, const float* x, float* y, int m, int n, int k, int flags,
+                   cudaStream_t st) {
+  GemmParams p{};
+  p.w = reinterpret_cast<const uint8_t*>(w);
+  p.w_f32 = 1;
+  p.y = y;
+  p.status = ds->status;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.epi = PQ8_EPI_NONE;
+  p.alpha = 1.0f;
+  p.flags = flags;
+  p.layout = PQ8_LAYOUT_ROWS;
+  p.out_cols = n;
+  p.n_tiles = (n + kTileRows - 1) / kTileRows;
+  p.k_blocks = k / 32;
+  return launch_gemm<192, 5, 4, 2, false, 2, 8>(ds, 1, x, p, st);
+}
+
 // Launch with programmatic dependent launch allowed: the kernel may start
 // while the previous kernel in the stream finishes (it calls griddep_wait
 // before reading that kernel's results).
@@ -1344,7 +1368,8 @@ extern "C" int pq8_stem(const float* mel, int windows, int frames, const float* 
   if (flags & ~PQ8_FLAG_FP32_PRODUCTS) return PQ8_ERR_INVALID_ARGUMENT;
   const StemPlan sp = plan_stem(windows, frames);
   if (workspace == nullptr || workspace_bytes < sp.total) return PQ8_ERR_WORKSPACE;
-  if (!aligned(workspace, 256) || !aligned(out, 16)) return PQ8_ERR_MISALIGNED;
+  if (!aligned(workspace, 256) || !aligned(out, 16) || !aligned(w3, 16) || !aligned(w6, 16))
+    return PQ8_ERR_MISALIGNED;
   DeviceState* ds;
   int rc = device_state(&ds);
   if (rc) return rc;
@@ -1367,17 +1392,24 @@ extern "C" int pq8_stem(const float* mel, int windows, int frames, const float* 
     e = launch_pdl(stem_depthwise_kernel, dim3(frame_tiles(sp.t2) * 32, windows), dim3(kStemChannels), 0, st,
                    static_cast<const float*>(a), no_bias, w2, b2, b, sp.t1, 64, sp.t2, 32);
   if (e != cudaSuccess) return to_code(e);
-  {
+  if (!(flags & PQ8_FLAG_FP32_PRODUCTS)) {
+    // pointwise 256 x 256 on the tensor cores: out[p][n] = sum_k in[p][k] w[n][k] (TF32 operands, FP32
+    // accumulation; bias and ReLU applied by the reader)
+    if ((rc = gemm_dense_f32(ds, w3, b, c, static_cast<int>(p2), 256, 256, 0, st))) return rc;
+    e = launch_pdl(stem_depthwise_kernel, dim3(frame_tiles(sp.t3) * 16, windows), dim3(kStemChannels), 0, st,
+                   static_cast<const float*>(c), b3, w5, b5, d, sp.t2, 32, sp.t3, 16);
+    if (e != cudaSuccess) return to_code(e);
+    if ((rc = gemm_dense_f32(ds, w6, d, z, static_cast<int>(p3), 256, 256, 0, st))) return rc;
+  } else {
+    // exactness reference: FP32 products through cuBLAS
     std::lock_guard<std::mutex> lock(ds->blas_mutex);
     if (ds->blas == nullptr && cublasCreate(&ds->blas) != CUBLAS_STATUS_SUCCESS) return PQ8_ERR_LIBRARY;
     cublasHandle_t h = ds->blas;
     if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS ||
         cublasSetWorkspace(h, base + sp.blas, kBlasWorkspace) != CUBLAS_STATUS_SUCCESS)
       return PQ8_ERR_LIBRARY;
-    const cublasComputeType_t ct =
-        (flags & PQ8_FLAG_FP32_PRODUCTS) ? CUBLAS_COMPUTE_32F : CUBLAS_COMPUTE_32F_FAST_TF32;
+    const cublasComputeType_t ct = CUBLAS_COMPUTE_32F;
     const float one = 1.0f, zero = 0.0f;
-    // pointwise 256 x 256: out[p][n] = sum_k in[p][k] w[n][k] (row-major), bias and ReLU applied by the reader
     if (cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, 256, static_cast<int>(p2), 256, &one, w3, CUDA_R_32F, 256, b,
                      CUDA_R_32F, 256, &zero, c, CUDA_R_32F, 256, ct, CUBLAS_GEMM_DEFAULT) != CUBLAS_STATUS_SUCCESS)
       return PQ8_ERR_LIBRARY;

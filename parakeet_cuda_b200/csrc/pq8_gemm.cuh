@@ -66,6 +66,7 @@ struct GemmParams {
   int out_cols;
   int n_tiles, k_blocks, m_tiles;
   int tma_store;  // 1: epilogue stages chunks in shared memory and writes them with TMA stores
+  int w_f32;      // 1: w is a dense row-major FP32 [n, k] matrix (no header), rounded to TF32 by the converters
 };
 
 template <int BN_, int STAGES_, int ASLOTS_, int ACC_, bool PAIR_, int GROUPS_ = 2, int GROUP_WARPS_ = 4,
@@ -416,8 +417,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   if (threadIdx.x == 0) {
     bool ok = true;
     if constexpr (!SEQ) {  // a sequence's headers are checked when its plan is made
-      const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
-      ok = h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout && h->n_tiles == p.n_tiles;
+      if (!p.w_f32) {
+        const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
+        ok = h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout && h->n_tiles == p.n_tiles;
+      }
     }
     *bad_flag = ok ? 0 : 1;
     *abort_flag = 0;
@@ -499,10 +502,15 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     uint32_t tile_first = 0;  // index of the current tile's first K block
     bool has_w = false;
     uint32_t kb_tile = 0;
+    int n_tile = 0;
+    // dense FP32 weights (single GEMMs only): each converter thread reads its
+    // row's 32 values of the K block from global memory instead of a record
+    const bool w_f32 = !SEQ && p.w_f32 != 0;
     auto enter = [&]() {
       const TileRef t = src.at(tile, rank, plan);
       has_w = t.n_tile < PQ8_TP(t, n_tiles);
       kb_tile = static_cast<uint32_t>(t.kb);
+      n_tile = t.n_tile;
     };
     if (tile < num_tiles) enter();
     for (uint32_t it = grp;; it += G) {
@@ -526,7 +534,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         constexpr int H = C::kValuesPerThread / 16;
         uint4 q[H];
         uint32_t sbits = 0;
-        if (has_w) {
+        if (has_w && !w_f32) {
           const uint8_t* rec = ws + wst * kRecordBytes;
           sbits = *reinterpret_cast<const uint16_t*>(rec + kScaleOffset + row * 2);
 #pragma unroll
@@ -534,7 +542,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
             q[h] = *reinterpret_cast<const uint4*>(rec + (kpart * H + h) * 2048 + row * 16);
         }
         slot_ready = mbar_test_wait(smem_addr(&afree[slot]), ar.phase ^ 1u);
-        if (has_w) {
+        if (has_w && w_f32) {
+          const int wrow = n_tile * kTileRows + row;
+          const uint32_t kb = it - tile_first;
+          const float4* src4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.w) +
+                                                               (size_t)wrow * p.k + kb * 32 +
+                                                               kpart * C::kValuesPerThread);
+#pragma unroll
+          for (int i = 0; i < C::kValuesPerThread / 4; ++i) {
+            const float4 v = wrow < p.n ? src4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            a[4 * i] = tf32_rne_bits(__float_as_uint(v.x));
+            a[4 * i + 1] = tf32_rne_bits(__float_as_uint(v.y));
+            a[4 * i + 2] = tf32_rne_bits(__float_as_uint(v.z));
+            a[4 * i + 3] = tf32_rne_bits(__float_as_uint(v.w));
+          }
+        } else if (has_w) {
           const bool fast = scale_fp16_exact(sbits);
 #pragma unroll
           for (int h = 0; h < H; ++h) expand16_tf32(q[h], sbits, fast, a + h * 16);
@@ -764,7 +786,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       Ring<WSTAGES> wr;
       for (int tile = unit0; tile < num_tiles; tile += unit_stride) {
         const TileRef t = src.at(tile, rank, plan);
-        const bool has_w = t.n_tile < PQ8_TP(t, n_tiles);
+        // dense FP32 weights are read by the converters themselves
+        const bool has_w = t.n_tile < PQ8_TP(t, n_tiles) && !(!SEQ && p.w_f32);
         const uint8_t* wt = PQ8_TP(t, w) + PQ8_HEADER_BYTES + (size_t)t.n_tile * t.kb * kRecordBytes;
         for (int kb = 0; kb < t.kb; ++kb, ++issued, wr.advance(1)) {
           if (!mbar_wait(&wempty[wr.idx], wr.phase ^ 1u, abort_flag, status)) goto w_done;
