@@ -51,9 +51,9 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
     ap.add_argument('--tdt-batches', default='1,64', help='decode batch sizes of the tdt extra')
-    ap.add_argument('--extras', default='config0,gemv,cublas,tdt,sweep,load,block,refgpu,cpu',
-                    help=('comma list of side measurements to run (config0, gemv, cublas, tdt, sweep, load, block, '
-                          'refgpu, cpu)'))
+    ap.add_argument('--extras', default='config0,refkernels,gemv,cublas,tdt,sweep,load,block,refgpu,cpu',
+                    help=('comma list of side measurements to run (config0, refkernels, gemv, cublas, tdt, sweep, '
+                          'load, block, refgpu, cpu)'))
     return ap.parse_args()
 
 
@@ -486,6 +486,8 @@ def run_gpu(args):
             extras['tf32_cublas_tflops'] = cublas_tf32(torch)
         if 'config0' in wanted:
             extras['config0'] = config0_measure(torch, rt)
+        if 'refkernels' in wanted and sched.rank == 0:
+            extras['reference_gpu_kernels'] = reference_gpu_kernels()
         if 'tdt' in wanted:
             extras['tdt'] = tdt_measure(torch, rt, [int(b) for b in args.tdt_batches.split(',')])
         if 'sweep' in wanted:
@@ -670,6 +672,133 @@ def config0_measure(torch, rt):
         r['gtx750ti_us'] = {'q8_gemm_direct': direct_us, 'dequant_sgemm': sgemm_us}
         out['reference_benchmark_shapes'].append(r)
     del flush
+    return out
+
+
+REF_CUBINS = ROOT / 'baseline' / '_ref'
+# (label, m, k, n): the reference's benchmark shapes, config 0, and the decoder's M = 1 shapes
+REF_KERNEL_CASES = (('ref 1x32x3', 1, 32, 3), ('ref 17x640x65', 17, 640, 65), ('ref 33x1024x129', 33, 1024, 129),
+                    ('ref 441x1024x4096', 441, 1024, 4096), ('config0 128x1024x4096', 128, 1024, 4096),
+                    ('lstm gates 1x640x2560', 1, 640, 2560), ('joint.pred 1x640x640', 1, 640, 640),
+                    ('joint 1x640x8198', 1, 640, 8198))
+
+
+def reference_gpu_kernels():
+    """The reference's own GPU kernels on this B200, built from its sources for
+    sm_100a (baseline/Makefile), against pq8 on the same shapes and inputs.
+
+    Methods (analysis/benchmark_dense.py): (i) ``dequant_q8`` + ``cublasSgemm_v2``
+    (the production path, gpu.py:87-90,169-184: FP32 weights expanded, FP32
+    SGEMM), (ii) the direct ``q8_gemm`` kernel (kernels/q8_gemm.cu), (iii)
+    ``q8_gemv`` (runtime.cu:180-188) for M = 1; pq8 through ``pq8_linear``.
+    Each is captured as a CUDA graph of 10 calls; the graphs are replayed
+    alternately 10 times and the first 2 replays dropped; microseconds per call
+    (median). Outputs are checked against each other (max |diff| / RMS).
+    Driver API and cuBLAS through ctypes, no PyTorch."""
+    import ctypes as C
+    import numpy as np
+    from parakeet_cuda_b200 import pq8
+    from parakeet_cuda_b200.cuda_driver import Event
+    from parakeet_cuda_b200.host import HostRuntime
+    from parakeet_cuda_b200.synthetic import q8_0_blocks
+    rt_cubin, gemm_cubin = REF_CUBINS / 'runtime_sm100a.cubin', REF_CUBINS / 'q8_gemm_sm100a.cubin'
+    if not (rt_cubin.is_file() and gemm_cubin.is_file()):
+        return {'unavailable': 'baseline/_ref cubins not built (make -C baseline REFERENCE=<checkout>)'}
+    rt = HostRuntime(0, weight_bytes=256 << 20, work_bytes=256 << 20)
+    drv = rt.drv
+    blas = C.CDLL('libcublas.so.12')
+    for name, args in {'cublasCreate_v2': [C.POINTER(C.c_void_p)], 'cublasSetStream_v2': [C.c_void_p, C.c_void_p],
+                       'cublasDestroy_v2': [C.c_void_p],
+                       'cublasSgemm_v2': [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                          C.POINTER(C.c_float), C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                          C.POINTER(C.c_float), C.c_void_p, C.c_int]}.items():
+        fn = getattr(blas, name)
+        fn.argtypes, fn.restype = args, C.c_int
+    handle = C.c_void_p()
+    if blas.cublasCreate_v2(C.byref(handle)):
+        return {'unavailable': 'cublasCreate failed'}
+    blas.cublasSetStream_v2(handle, rt.stream.handle)
+    one, zero = C.c_float(1.0), C.c_float(0.0)
+    modules = {}
+    funcs = {}
+    for path, names in ((rt_cubin, (b'dequant_q8', b'q8_gemv')), (gemm_cubin, (b'q8_gemm',))):
+        mod = C.c_void_p()
+        drv.call('cuModuleLoad', C.byref(mod), str(path).encode())
+        modules[path] = mod
+        for nm in names:
+            f = C.c_void_p()
+            drv.call('cuModuleGetFunction', C.byref(f), mod, nm)
+            funcs[nm.decode()] = f
+
+    def launch(f, grid, params):
+        holders = [C.c_uint64(v) if isinstance(v, Ptr) else C.c_int(v) for v in params]
+        ptrs = (C.c_void_p * len(holders))(*(C.addressof(h) for h in holders))
+        launch.keep.append((holders, ptrs))
+        drv.call('cuLaunchKernel', f, grid, 1, 1, 256, 1, 1, 0, rt.stream.handle, ptrs, None)
+    launch.keep = []
+
+    class Ptr(int):
+        pass
+
+    out = {'method': 'graph of 10 calls, 10 alternating replays, first 2 dropped, median us per call',
+           'build': 'nvcc --cubin -O3 -std=c++17 -lineinfo -arch=sm_100a (baseline/Makefile)', 'cases': []}
+    rng = np.random.default_rng(17)
+    up = rt.uploader()
+    for label, m, k, n in REF_KERNEL_CASES:
+        rt.work.reset()
+        raw = q8_0_blocks(rng, n, k)
+        x = rng.standard_normal((m, k), np.float32)
+        d_raw = rt.upload(raw.reshape(-1))
+        d_x = rt.upload(x)
+        d_wf = rt.work.alloc((n, k))
+        ys = {name: rt.work.alloc((m, n)) for name in ('pq8', 'sgemm', 'direct', 'gemv')}
+        w = up.pack_rows([raw], n, k)
+        up.finish()
+        calls = {
+            'pq8': lambda: rt.linear(d_x, w, ys['pq8'], m),
+            'dequant_sgemm': lambda: (
+                launch(funcs['dequant_q8'], (n * k + 255) // 256, [Ptr(d_raw.pointer), Ptr(d_wf.pointer), n * k]),
+                blas.cublasSgemm_v2(handle, 1, 0, n, m, k, C.byref(one), d_wf.pointer, k, d_x.pointer, k,
+                                    C.byref(zero), ys['sgemm'].pointer, n)),
+            'q8_gemm_direct': lambda: launch(funcs['q8_gemm'], ((m + 31) // 32) * ((n + 63) // 64),
+                                             [Ptr(w_raw), Ptr(d_x.pointer), Ptr(ys['direct'].pointer), m, k, n]),
+        }
+        w_raw = d_raw.pointer
+        if m == 1:
+            calls['q8_gemv'] = lambda: launch(funcs['q8_gemv'], n, [Ptr(d_raw.pointer), Ptr(d_x.pointer),
+                                                                     Ptr(ys['gemv'].pointer), k, n])
+        for fn in calls.values():
+            fn()
+        rt.synchronize()
+        res = {n_: rt.download(b) for n_, b in ys.items()}
+        scale = float(np.sqrt(np.mean(res['sgemm'].astype(np.float64) ** 2))) or 1.0
+        check = {name: float(np.max(np.abs(res[key] - res['sgemm']))) / scale
+                 for name, key in (('pq8', 'pq8'), ('q8_gemm_direct', 'direct')) + ((('q8_gemv', 'gemv'),) if m == 1 else ())}
+        graphs = {name: rt.stream.capture(lambda fn=fn: [fn() for _ in range(10)]) for name, fn in calls.items()}
+        samples = {name: [] for name in calls}
+        a, b = Event(drv), Event(drv)
+        order = list(calls)
+        for rep in range(10):
+            for name in (order if rep % 2 == 0 else order[::-1]):
+                a.record(rt.stream)
+                graphs[name].launch(rt.stream)
+                b.record(rt.stream)
+                b.synchronize()
+                if rep >= 2:
+                    samples[name].append(a.elapsed_ms(b) * 1e3 / 10)
+        for g in graphs.values():
+            g.close()
+        us = {name: float(np.median(v)) for name, v in samples.items()}
+        flops = 2.0 * m * n * k
+        out['cases'].append({'case': label, 'm': m, 'k': k, 'n': n, 'us': us,
+                             'gflops': {name: flops / t / 1e3 for name, t in us.items()},
+                             'pq8_speedup': {name: t / us['pq8'] for name, t in us.items() if name != 'pq8'},
+                             'max_diff_over_rms_vs_sgemm': check})
+    launch.keep.clear()
+    for mod in modules.values():
+        drv.call('cuModuleUnload', mod)
+    blas.cublasDestroy_v2(handle)
+    rt.close()
     return out
 
 

@@ -82,7 +82,8 @@ extern "C" {
 #define PQ8_TILE_ROWS 128
 #define PQ8_RECORD_BYTES 4352 /* 128 rows x 32 int8 + 128 fp16 scales */
 #define PQ8_GEMV_MAX_M 64        /* the GEMV entry points (pq8_gemv, pq8_lstm_layer, pq8_joint_argmax) take m <= 64 */
-#define PQ8_LINEAR_GEMV_MAX_M 8  /* pq8_linear sends m <= 8 to pq8_gemv, larger m to pq8_gemm */
+#define PQ8_LINEAR_GEMV_MAX_M 8  /* pq8_linear sends m <= 8 to pq8_gemv; 9..64 to whichever kernel a
+                                    measured cost model finds faster for (m, n, k); larger m to pq8_gemm */
 
 /* Name of an error code (static string; never NULL). */
 PQ8_API const char* pq8_error_string(int code);
@@ -170,8 +171,11 @@ PQ8_API int pq8_gemv(const void* w, const float* x, float* y, const float* bias,
              int m, int n, int k, int epilogue, float alpha, void* workspace, size_t workspace_bytes,
              void* stream);
 
-/* Dispatch by m: pq8_gemv for m <= PQ8_LINEAR_GEMV_MAX_M (needs the workspace),
- * otherwise pq8_gemm. The drop-in for Blas.linear (gpu.py:87-90). */
+/* Dispatch by shape: pq8_gemv for m <= PQ8_LINEAR_GEMV_MAX_M, and for m up
+ * to PQ8_GEMV_MAX_M where its FP32 FMA work is small enough to beat the
+ * tensor-core GEMM's fixed cost (a measured cost model of both); pq8_gemm
+ * otherwise. The workspace must hold pq8_gemv_workspace_size(m, n, k) bytes
+ * for every m <= PQ8_GEMV_MAX_M. The drop-in for Blas.linear (gpu.py:87-90). */
 PQ8_API int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid,
                int m, int n, int k, int epilogue, float alpha, int flags, void* workspace,
                size_t workspace_bytes, void* stream);

@@ -147,30 +147,6 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   return to_code(cudaGetLastError());
 }
 
-// The tensor-core kernel on a dense row-major FP32 weight [n, k] (k a multiple
-// of 32, 16-byte aligned rows): the converters round the weights to TF32
-// (nearest-even) instead of expanding Q8_0 records. Used for the stem's
-// pointwise convolutions, whose weights are FP32 in the model.
-int gemm_dense_f32(DeviceState* ds, const float* w, const float* x, float* y, int m, int n, int k, int flags,
-                   cudaStream_t st) {
-  GemmParams p{};
-  p.w = reinterpret_cast<const uint8_t*>(w);
-  p.w_f32 = 1;
-  p.y = y;
-  p.status = ds->status;
-  p.m = m;
-  p.n = n;
-  p.k = k;
-  p.epi = PQ8_EPI_NONE;
-  p.alpha = 1.0f;
-  p.flags = flags;
-  p.layout = PQ8_LAYOUT_ROWS;
-  p.out_cols = n;
-  p.n_tiles = (n + kTileRows - 1) / kTileRows;
-  p.k_blocks = k / 32;
-  return launch_gemm<192, 5, 4, 2, false, 2, 8>(ds, 1, x, p, st);
-}
-
 // Launch with programmatic dependent launch allowed: the kernel may start
 // while the previous kernel in the stream finishes (it calls griddep_wait
 // before reading that kernel's results).
@@ -558,6 +534,49 @@ extern "C" int pq8_round_tf32(float* x, long long n, void* stream) {
   return to_code(cudaGetLastError());
 }
 
+namespace pq8 {
+namespace {
+
+// The tile configuration with the least modelled time for this shape.
+int launch_chosen(DeviceState* ds, const float* x, const GemmParams& p, cudaStream_t st) {
+  switch (choose_gemm(p.m, p.n_tiles, p.k_blocks, ds->sms)) {
+    case kG256: return launch_gemm<256, 4, 4, 1, false, 2, 7>(ds, kG256, x, p, st);
+    case kG192: return launch_gemm<192, 5, 4, 2, false, 2, 8>(ds, kG192, x, p, st);
+    case kG128: return launch_gemm<128, 7, 4, 2, false, 2, 8>(ds, kG128, x, p, st);
+    case kG64: return launch_gemm<64, 10, 4, 2, false, 2, 8>(ds, kG64, x, p, st);
+    case kP256: return launch_gemm<256, 7, 4, 1, true, 2, 8>(ds, kP256, x, p, st);
+    case kP192: return launch_gemm<192, 8, 4, 2, true, 2, 8>(ds, kP192, x, p, st);
+    default: return launch_gemm<128, 10, 4, 2, true, 2, 8>(ds, kP128, x, p, st);
+  }
+}
+
+// The tensor-core kernel on a dense row-major FP32 weight [n, k] (k a multiple
+// of 32, 16-byte aligned rows): the converters round the weights to TF32
+// (nearest-even) instead of expanding Q8_0 records. Used for the stem's
+// pointwise convolutions, whose weights are FP32 in the model.
+int gemm_dense_f32(DeviceState* ds, const float* w, const float* x, float* y, int m, int n, int k, int flags,
+                   cudaStream_t st) {
+  GemmParams p{};
+  p.w = reinterpret_cast<const uint8_t*>(w);
+  p.w_f32 = 1;
+  p.y = y;
+  p.status = ds->status;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.epi = PQ8_EPI_NONE;
+  p.alpha = 1.0f;
+  p.flags = flags;
+  p.layout = PQ8_LAYOUT_ROWS;
+  p.out_cols = n;
+  p.n_tiles = (n + kTileRows - 1) / kTileRows;
+  p.k_blocks = k / 32;
+  return launch_chosen(ds, x, p, st);
+}
+
+}  // namespace
+}  // namespace pq8
+
 extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bias, const float* resid, int m, int n,
                         int k, int epilogue, float alpha, int flags, void* stream) {
   int rc = check_linear_args(w, x, y, resid, m, n, k, epilogue);
@@ -582,16 +601,7 @@ extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bi
   p.out_cols = epilogue == PQ8_EPI_GLU ? n / 2 : n;
   p.n_tiles = (n + kTileRows - 1) / kTileRows;
   p.k_blocks = k / 32;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (choose_gemm(m, p.n_tiles, p.k_blocks, ds->sms)) {
-    case kG256: return launch_gemm<256, 4, 4, 1, false, 2, 7>(ds, kG256, x, p, st);
-    case kG192: return launch_gemm<192, 5, 4, 2, false, 2, 8>(ds, kG192, x, p, st);
-    case kG128: return launch_gemm<128, 7, 4, 2, false, 2, 8>(ds, kG128, x, p, st);
-    case kG64: return launch_gemm<64, 10, 4, 2, false, 2, 8>(ds, kG64, x, p, st);
-    case kP256: return launch_gemm<256, 7, 4, 1, true, 2, 8>(ds, kP256, x, p, st);
-    case kP192: return launch_gemm<192, 8, 4, 2, true, 2, 8>(ds, kP192, x, p, st);
-    default: return launch_gemm<128, 10, 4, 2, true, 2, 8>(ds, kP128, x, p, st);
-  }
+  return launch_chosen(ds, x, p, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------- GEMM sequences
@@ -889,10 +899,27 @@ extern "C" int pq8_gemv(const void* w, const float* x, float* y, const float* bi
   return launch_gemv(ds, p, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
+namespace pq8 {
+namespace {
+
+// pq8_linear's choice for PQ8_LINEAR_GEMV_MAX_M < m <= PQ8_GEMV_MAX_M, from
+// B200 measurements of both kernels at 9-64 rows (N 65-8198, K 640-4096, CUDA
+// graphs of back-to-back calls): the GEMV costs ~4 us plus ~0.1 ns per
+// multiply-add of its 8-row groups (FP32 FMA), the GEMM (one wave of tiles at
+// these sizes) ~3.3 us plus ~0.4 us per 32-wide K block. Within 6 % of the
+// faster kernel at every measured point.
+bool gemv_faster(int m, int n, int k) {
+  const double macs = static_cast<double>((m + 7) / 8 * 8) * n * k;
+  return 4.0 + 1.0e-7 * macs < 3.3 + 0.4 * (k / 32);
+}
+
+}  // namespace
+}  // namespace pq8
+
 extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid, int m,
                           int n, int k, int epilogue, float alpha, int flags, void* workspace, size_t workspace_bytes,
                           void* stream) {
-  if (m >= 1 && m <= PQ8_LINEAR_GEMV_MAX_M)
+  if (m >= 1 && (m <= PQ8_LINEAR_GEMV_MAX_M || (m <= PQ8_GEMV_MAX_M && gemv_faster(m, n, k))))
     return pq8_gemv(w, x, y, bias, resid, m, n, k, epilogue, alpha, workspace, workspace_bytes, stream);
   return pq8_gemm(w, x, y, bias, resid, m, n, k, epilogue, alpha, flags, stream);
 }

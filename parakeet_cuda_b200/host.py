@@ -31,7 +31,7 @@ import numpy as np
 from . import pq8
 from .cuda_driver import Driver, Event, PinnedArray
 from .layers import D_FF, D_MODEL, FRAMES_PER_WINDOW, LAYER_PLAN, flops_per_row_per_layer
-from .pq8 import EPI_GLU, EPI_RESIDUAL, FLAG_X_TF32, LAYOUT_GATES4, LAYOUT_GLU, LAYOUT_ROWS, LINEAR_GEMV_MAX_M
+from .pq8 import EPI_GLU, EPI_RESIDUAL, FLAG_X_TF32, LAYOUT_GATES4, LAYOUT_GLU, LAYOUT_ROWS, GEMV_MAX_M
 
 MIB = 1 << 20
 ALIGN = 256
@@ -171,7 +171,7 @@ class HostRuntime:
     def linear(self, x: Buffer, w: PackedQ8, out: Buffer, m: int, bias: Buffer | None = None,
                resid: Buffer | None = None, epilogue: int = pq8.EPI_NONE, alpha: float = 1.0, flags: int = 0) -> None:
         """As ``gemm``, with the library choosing the GEMV for a few rows."""
-        if 1 <= m <= LINEAR_GEMV_MAX_M and self.lib.gemv_workspace_size(m, w.n, w.k) > self.workspace.nbytes:
+        if 1 <= m <= GEMV_MAX_M and self.lib.gemv_workspace_size(m, w.n, w.k) > self.workspace.nbytes:
             raise MemoryError(f'GEMV workspace of {self.workspace.nbytes} bytes is too small for [{m}, {w.n}, {w.k}]')
         self.lib.call('pq8_linear', w.pointer, x.pointer, out.pointer, _ptr(bias), _ptr(resid), m, w.n, w.k, epilogue,
                       float(alpha), flags, self.workspace.pointer, self.workspace.nbytes, self.stream.handle)

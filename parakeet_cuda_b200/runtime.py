@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 from . import pq8
-from .pq8 import EPI_GLU, EPI_NONE, LINEAR_GEMV_MAX_M, LAYOUT_GATES4, LAYOUT_GLU, LAYOUT_ROWS
+from .pq8 import EPI_GLU, EPI_NONE, GEMV_MAX_M, LAYOUT_GATES4, LAYOUT_GLU, LAYOUT_ROWS
 
 MIB = 1 << 20
 
@@ -253,7 +253,7 @@ class Runtime:
         if out is None:
             out = torch.empty(rows, w.out_features if epilogue == EPI_GLU else w.n, dtype=torch.float32,
                               device=self.device)
-        if 1 <= rows <= LINEAR_GEMV_MAX_M:
+        if 1 <= rows <= GEMV_MAX_M:
             self.ensure_workspace(rows, w.n, k)
         self.lib.call('pq8_linear', w.pointer, x.data_ptr(), out.data_ptr(), _ptr(bias), _ptr(resid), rows, w.n, k,
                       epilogue, float(alpha), flags, self.workspace.data_ptr(), self.workspace.numel(),

@@ -216,6 +216,29 @@ def test_linear_dispatch_gemv_matches_gemm(rt):
         np.testing.assert_allclose(y, gold, atol=2e-4, rtol=2e-4)
 
 
+@pytest.mark.parametrize('m,n,k,kernel', [(16, 1024, 4096, 'gemv'), (24, 640, 640, 'gemv'), (48, 8198, 640, 'gemm'),
+                                          (64, 4096, 1024, 'gemm'), (9, 129, 1024, 'gemv')])
+def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
+    """pq8_linear sends 9..64 rows to whichever kernel its measured cost model
+    finds faster: the result is bit for bit that kernel's."""
+    rng = np.random.default_rng(m + n)
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k)
+    xd = dev(rng.normal(size=(m, k)).astype(np.float32))
+    got = rt.linear(xd, w).cpu().numpy()
+    if kernel == 'gemm':
+        want = rt.gemm(xd, w).cpu().numpy()
+    else:
+        rt.ensure_workspace(m, n, k)
+        y = torch.empty(m, n, device='cuda')
+        rt.lib.call('pq8_gemv', w.pointer, xd.data_ptr(), y.data_ptr(), None, None, m, n, k, EPI_NONE, 1.0,
+                    rt.workspace.data_ptr(), rt.workspace.numel(), rt.stream())
+        want = y.cpu().numpy()
+    np.testing.assert_array_equal(got, want)
+    gold = q8.gemm(np.asarray(xd.cpu().numpy()), raw, n, k)
+    assert q8.max_err_over_rms(got, gold) <= NORTH_STAR
+
+
 def test_gemv_epilogues(rt):
     rng = np.random.default_rng(6)
     m, n, k = 4, 1280, 640
