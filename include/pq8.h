@@ -173,12 +173,18 @@ PQ8_API int pq8_gemv(const void* w, const float* x, float* y, const float* bias,
 
 /* Dispatch by shape: pq8_gemv for m <= PQ8_LINEAR_GEMV_MAX_M, and for m up
  * to PQ8_GEMV_MAX_M where its FP32 FMA work is small enough to beat the
- * tensor-core GEMM's fixed cost (a measured cost model of both); pq8_gemm
- * otherwise. The workspace must hold pq8_gemv_workspace_size(m, n, k) bytes
- * for every m <= PQ8_GEMV_MAX_M. The drop-in for Blas.linear (gpu.py:87-90). */
+ * tensor-core GEMM's fixed cost (a measured cost model of both); the
+ * tensor-core GEMM otherwise, with split K when its tiles would fill at most
+ * half of the SMs (each tile's K blocks shared by up to 8 CTAs, partial sums
+ * added in a fixed order by the last of them, so results are deterministic).
+ * The workspace (zeroed once by pq8_workspace_init) must hold
+ * pq8_linear_workspace_size(m, n, k) bytes; with less, the GEMM runs
+ * unsplit. The drop-in for Blas.linear (gpu.py:87-90). */
 PQ8_API int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid,
                int m, int n, int k, int epilogue, float alpha, int flags, void* workspace,
                size_t workspace_bytes, void* stream);
+/* Workspace bytes pq8_linear needs for this shape (0 when it needs none). */
+PQ8_API int pq8_linear_workspace_size(int m, int n, int k, size_t* bytes);
 
 /* One LSTM layer of the TDT prediction network for m <= PQ8_GEMV_MAX_M streams:
  *   gates = W_ih x + W_hh h + bias, c' = s(f) c + s(i) tanh(g), h' = s(o) tanh(c')

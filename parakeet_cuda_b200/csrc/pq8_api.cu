@@ -86,6 +86,8 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS, int WSTAGES>
 int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaStream_t st) {
   using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES>;
+  if (p.k_splits < 1) p.k_splits = 1;
+  if (p.k_splits > 1 && (PAIR || p.partial == nullptr || p.tickets == nullptr)) return PQ8_ERR_INVALID_ARGUMENT;
   EncodeTiledFn enc;
   int rc = encode_fn(&enc);
   if (rc) return rc;
@@ -122,7 +124,7 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
     }
   }
   p.m_tiles = (p.m + BN - 1) / BN;
-  const int units = (PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles) * p.m_tiles;
+  const int units = (PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles) * p.m_tiles * p.k_splits;
   const int slots = PAIR ? ds->sms / 2 : ds->sms;
   const int grid = std::min(units, slots) * C::kCtas;
   cudaLaunchConfig_t cfg = {};
@@ -778,6 +780,7 @@ extern "C" int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* pl
     p.n_tiles = n_tiles;
     p.k_blocks = t.k / 32;
     p.m_tiles = (t.m + kSeqBN - 1) / kSeqBN;
+    p.k_splits = 1;
     p.tma_store = (p.out_cols % 4 == 0) && aligned(t.y, 16);
     q.tile0 = tile0;
     q.n_units = n_tiles;
@@ -913,6 +916,26 @@ bool gemv_faster(int m, int n, int k) {
   return 4.0 + 1.0e-7 * macs < 3.3 + 0.4 * (k / 32);
 }
 
+// Split K for pq8_linear's GEMM path: when BN = 128 tiles would fill at most
+// half of the SMs, each tile's K blocks are shared by up to 8 CTAs (at least
+// 8 K blocks each) and the partial sums go through the workspace: the counter
+// area's first words are the tiles' tickets, the partials follow it.
+struct SplitPlan {
+  int splits;
+  size_t bytes;
+};
+SplitPlan plan_split(int m, int n, int k, int sms) {
+  SplitPlan sp{1, 0};
+  const long long units = static_cast<long long>((m + 127) / 128) * ((n + kTileRows - 1) / kTileRows);
+  const int kb = k / 32;
+  if (units * 2 > sms || kb < 16) return sp;
+  const long long s = std::min<long long>({sms / units, kb / 8, 8});
+  if (s < 2) return sp;
+  sp.splits = static_cast<int>(s);
+  sp.bytes = kGemvCounterBytes + round256(sizeof(float) * static_cast<size_t>(units) * s * 128 * kTileRows);
+  return sp;
+}
+
 }  // namespace
 }  // namespace pq8
 
@@ -921,7 +944,55 @@ extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* 
                           void* stream) {
   if (m >= 1 && (m <= PQ8_LINEAR_GEMV_MAX_M || (m <= PQ8_GEMV_MAX_M && gemv_faster(m, n, k))))
     return pq8_gemv(w, x, y, bias, resid, m, n, k, epilogue, alpha, workspace, workspace_bytes, stream);
+  if (m >= 1 && k > 0 && k % 32 == 0 && n >= 1) {
+    DeviceState* ds;
+    int rc = device_state(&ds);
+    if (rc) return rc;
+    const SplitPlan sp = plan_split(m, n, k, ds->sms);
+    if (sp.splits > 1 && workspace != nullptr && workspace_bytes >= sp.bytes && aligned(workspace, 256)) {
+      if ((rc = check_linear_args(w, x, y, resid, m, n, k, epilogue))) return rc;
+      if (!aligned(x, 16)) return PQ8_ERR_MISALIGNED;
+      if (flags & ~(PQ8_FLAG_X_TF32 | PQ8_FLAG_OUT_TF32)) return PQ8_ERR_INVALID_ARGUMENT;
+      GemmParams p{};
+      p.w = static_cast<const uint8_t*>(w);
+      p.y = y;
+      p.bias = bias;
+      p.resid = resid;
+      p.status = ds->status;
+      p.m = m;
+      p.n = n;
+      p.k = k;
+      p.epi = epilogue;
+      p.alpha = alpha;
+      p.flags = flags;
+      p.layout = epilogue == PQ8_EPI_GLU ? PQ8_LAYOUT_GLU : PQ8_LAYOUT_ROWS;
+      p.out_cols = epilogue == PQ8_EPI_GLU ? n / 2 : n;
+      p.n_tiles = (n + kTileRows - 1) / kTileRows;
+      p.k_blocks = k / 32;
+      p.k_splits = sp.splits;
+      p.tickets = static_cast<int*>(workspace);
+      p.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kGemvCounterBytes);
+      return launch_gemm<128, 7, 4, 2, false, 2, 8>(ds, kG128, x, p, static_cast<cudaStream_t>(stream));
+    }
+  }
   return pq8_gemm(w, x, y, bias, resid, m, n, k, epilogue, alpha, flags, stream);
+}
+
+extern "C" int pq8_linear_workspace_size(int m, int n, int k, size_t* bytes) {
+  if (bytes == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (m < 0 || n < 1 || k <= 0 || k % 32) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  *bytes = 0;
+  if (m == 0) return PQ8_OK;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  if (m <= PQ8_GEMV_MAX_M) {
+    const GemvPlan g = plan_gemv(m, n, k, ds->sms);
+    if (g.ok) *bytes = g.total;
+  }
+  const SplitPlan sp = plan_split(m, n, k, ds->sms);
+  if (sp.splits > 1 && sp.bytes > *bytes) *bytes = sp.bytes;
+  return PQ8_OK;
 }
 
 extern "C" int pq8_lstm_layer(const void* w, const float* x, const uint16_t* embed_f16, const int* tokens,

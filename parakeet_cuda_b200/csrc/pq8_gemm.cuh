@@ -67,6 +67,14 @@ struct GemmParams {
   int n_tiles, k_blocks, m_tiles;
   int tma_store;  // 1: epilogue stages chunks in shared memory and writes them with TMA stores
   int w_f32;      // 1: w is a dense row-major FP32 [n, k] matrix (no header), rounded to TF32 by the converters
+  // Split K (single GEMMs, single-CTA tiles): each output tile's K blocks are
+  // shared by k_splits CTAs; each stores its raw accumulator to `partial`
+  // ([tile][split][BN activation rows][128 weight rows]), and the last of them
+  // (tickets[2 * tile + epilogue half], reset by that CTA) sums the partials in
+  // split order and runs the epilogue.
+  int k_splits;
+  float* partial;
+  int* tickets;
 };
 
 template <int BN_, int STAGES_, int ASLOTS_, int ACC_, bool PAIR_, int GROUPS_ = 2, int GROUP_WARPS_ = 4,
@@ -105,7 +113,7 @@ struct GemmCfg {
   static constexpr int kBarOff = kOutOff + 4 * kOutChunkFloats * 4;
   static constexpr int kNumBars = 2 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kUsedBytes = kMiscOff + 16;
+  static constexpr int kUsedBytes = kMiscOff + 24;
   static constexpr int kAColBase = ACC * BN;
   static constexpr int kColsNeeded = ACC * BN + ASLOTS * 32;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
@@ -285,7 +293,18 @@ __device__ __forceinline__ bool wait_dep(const SeqTask* tasks, int* counters, co
 struct TileRef {
   const SeqTask* task;  // sequences only
   int n_tile, m_tile, kb;
+  int kb0 = 0, split = 0;  // split K: first K block and split index of this tile
 };
+
+// Tile `tile` of a single GEMM: output tiles N-unit major, their K splits
+// fastest (the splits of a tile run side by side on consecutive CTAs).
+template <int kCtas>
+__device__ __forceinline__ TileRef single_tile(int tile, uint32_t rank, int m_tiles, int k_blocks, int splits) {
+  const int s = tile % splits, out_tile = tile / splits;
+  const int per = (k_blocks + splits - 1) / splits, kb0 = s * per;
+  const int kb = k_blocks - kb0 < per ? k_blocks - kb0 : per;
+  return {nullptr, (out_tile / m_tiles) * kCtas + static_cast<int>(rank), out_tile % m_tiles, kb, kb0, s};
+}
 
 // A role warp's view of its tiles (local index i = the CTA's i-th tile,
 // tile blockIdx + i * grid). For a sequence, the lanes look up 32 tiles at
@@ -300,10 +319,10 @@ struct TileWindow;
 
 template <int kCtas>
 struct TileWindow<kCtas, false> {
-  int m_tiles, k_blocks;
+  int m_tiles, k_blocks, splits;
   __device__ __forceinline__ TileRef get(int local, uint32_t rank, const uint8_t*) const {
     const int tile = static_cast<int>(blockIdx.x) / kCtas + local * static_cast<int>(gridDim.x / kCtas);
-    return {nullptr, (tile / m_tiles) * kCtas + static_cast<int>(rank), tile % m_tiles, k_blocks};
+    return single_tile<kCtas>(tile, rank, m_tiles, k_blocks, splits);
   }
 };
 
@@ -349,7 +368,7 @@ struct TileWindow<kCtas, true> {
 // producers, which reach a tile boundary well before its data is needed).
 template <int kCtas, bool SEQ>
 struct TileCursor {
-  int m_tiles, k_blocks;  // single GEMM
+  int m_tiles, k_blocks, splits;  // single GEMM
   int cur = 0;            // sequence: task of the latest lookup
   __device__ __forceinline__ TileRef at(int tile, uint32_t rank, const uint8_t* plan) {
     if constexpr (SEQ) {
@@ -361,7 +380,7 @@ struct TileCursor {
       const int u = tile - t->tile0, nu = t->n_units;
       return {t, u % nu, u / nu, t->p.k_blocks};
     } else {
-      return {nullptr, (tile / m_tiles) * kCtas + static_cast<int>(rank), tile % m_tiles, k_blocks};
+      return single_tile<kCtas>(tile, rank, m_tiles, k_blocks, splits);
     }
   }
 };
@@ -411,7 +430,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   int* counters = SEQ ? reinterpret_cast<int*>(const_cast<uint8_t*>(plan) + hdr->counters_offset) : nullptr;
   const int task_count = SEQ ? hdr->count : 1;
   const int n_units = PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles;
-  const int num_tiles = SEQ ? hdr->total_tiles : n_units * p.m_tiles;
+  const int num_tiles = SEQ ? hdr->total_tiles : n_units * p.m_tiles * p.k_splits;
   int* const status = p.status;
 
   if (threadIdx.x == 0) {
@@ -468,7 +487,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   // Arrivals that the leader's MMA waits for go to the leader's barriers.
   const uint32_t conv_remote = PAIR ? map_to_rank(conv, 0) : 0;
   const uint32_t acc_empty_remote = PAIR ? map_to_rank(acc_empty, 0) : 0;
-  TileCursor<C::kCtas, SEQ> src{p.m_tiles, p.k_blocks};
+  TileCursor<C::kCtas, SEQ> src{p.m_tiles, p.k_blocks, p.k_splits};
   const int x_flags = SEQ ? (task_count > 0 ? tasks[0].p.flags : 0) : p.flags;
   bool mma_issued = false;
 
@@ -502,7 +521,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     uint32_t tile_first = 0;  // index of the current tile's first K block
     bool has_w = false;
     uint32_t kb_tile = 0;
-    int n_tile = 0;
+    int n_tile = 0, kb0_tile = 0;
     // dense FP32 weights (single GEMMs only): each converter thread reads its
     // row's 32 values of the K block from global memory instead of a record
     const bool w_f32 = !SEQ && p.w_f32 != 0;
@@ -511,6 +530,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       has_w = t.n_tile < PQ8_TP(t, n_tiles);
       kb_tile = static_cast<uint32_t>(t.kb);
       n_tile = t.n_tile;
+      kb0_tile = t.kb0;
     };
     if (tile < num_tiles) enter();
     for (uint32_t it = grp;; it += G) {
@@ -544,7 +564,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         slot_ready = mbar_test_wait(smem_addr(&afree[slot]), ar.phase ^ 1u);
         if (has_w && w_f32) {
           const int wrow = n_tile * kTileRows + row;
-          const uint32_t kb = it - tile_first;
+          const uint32_t kb = it - tile_first + static_cast<uint32_t>(kb0_tile);
           const float4* src4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.w) +
                                                                (size_t)wrow * p.k + kb * 32 +
                                                                kpart * C::kValuesPerThread);
@@ -668,17 +688,64 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         for (int j = 0; j < E; ++j)
           out[j] = (store_lane && m0 + j < m) ? rcol[(size_t)(m0 + j) * out_cols] : 0.0f;
       };
-      if (resid) load_resid(m_tile * BN + half * kChunks * E);
+      const bool split = !SEQ && !PAIR && p.k_splits > 1;
+      if (resid && !split) load_resid(m_tile * BN + half * kChunks * E);
       if (!mbar_wait(&acc_full[acc], (local / ACC) & 1, abort_flag, status)) break;
       tc_fence_after();
+      // Split K: each half stores its rows of this split's raw accumulator
+      // (through L2), releases the accumulator and takes the half-tile's
+      // ticket; only the last split goes on, summing every split's partial in
+      // split order (the same order whichever CTA is last) before the epilogue.
+      const float* partials = nullptr;
+      if (split) {
+        const int out_tile = tile / p.k_splits;
+        float* mine = p.partial + ((size_t)out_tile * p.k_splits + t.split) * (BN * kTileRows);
+#pragma unroll 1
+        for (int cc = 0; cc < kChunks; ++cc) {
+          const int c = half * kChunks + cc;
+          uint32_t v[E];
+          tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < E; ++j) __stcg(mine + (size_t)(c * E + j) * kTileRows + r, __uint_as_float(v[j]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        __threadfence();
+        named_barrier_sync(1 + half, 128);
+        volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 12 + 4 * half);
+        if (elected) {
+          int* ticket = p.tickets + out_tile * 2 + half;
+          const bool last = atomicAdd(ticket, 1) == p.k_splits - 1;
+          if (last) atomicExch(ticket, 0);  // every split has taken its ticket
+          __threadfence();
+          *last_flag = last ? 1 : 0;
+        }
+        named_barrier_sync(1 + half, 128);
+        if (!*last_flag) continue;
+        __threadfence();
+        partials = p.partial + (size_t)out_tile * p.k_splits * (BN * kTileRows);
+        if (resid) load_resid(m_tile * BN + half * kChunks * E);
+      }
 #pragma unroll 1
       for (int cc = 0; cc < kChunks; ++cc, ++chunk_seq) {
         const int c = half * kChunks + cc;
         const int m0 = m_tile * BN + c * E;
         if (m0 >= m) break;
         uint32_t v[E];
-        tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
-        tmem_wait_ld();
+        if (split) {
+#pragma unroll
+          for (int j = 0; j < E; ++j) {
+            const float* col = partials + (size_t)(c * E + j) * kTileRows + r;
+            float sum = __ldcg(col);
+            for (int sp = 1; sp < p.k_splits; ++sp) sum += __ldcg(col + (size_t)sp * (BN * kTileRows));
+            v[j] = __float_as_uint(sum);
+          }
+        } else {
+          tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
+          tmem_wait_ld();
+        }
         const int cnt = min(E, m - m0);  // warp-uniform
         if (resid) {
 #pragma unroll
@@ -728,11 +795,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         }
         if (resid && cc + 1 < kChunks) load_resid(m0 + E);
       }
-      tc_fence_before();
-      __syncwarp();  // every lane's accumulator loads are complete: one arrival per warp
-      if (lane == 0) {
-        if (PAIR && !leader) mbar_arrive_cluster(acc_empty_remote + acc * 8);
-        else mbar_arrive(&acc_empty[acc]);
+      if (!split) {
+        tc_fence_before();
+        __syncwarp();  // every lane's accumulator loads are complete: one arrival per warp
+        if (lane == 0) {
+          if (PAIR && !leader) mbar_arrive_cluster(acc_empty_remote + acc * 8);
+          else mbar_arrive(&acc_empty[acc]);
+        }
       }
       if constexpr (SEQ) {
         // This half's rows of the tile are written: signal them (once per half).
@@ -771,7 +840,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         for (int kb = 0; kb < t.kb; ++kb, ++issued, xr.advance(1)) {
           if (!mbar_wait(&xempty[xr.idx], xr.phase ^ 1u, abort_flag, status)) goto x_done;
           mbar_expect_tx(&xfull[xr.idx], C::kXStageBytes);
-          tma_load_2d(xs + xr.idx * C::kXStageBytes, tx, kb * 32, row0, &xfull[xr.idx]);
+          tma_load_2d(xs + xr.idx * C::kXStageBytes, tx, (t.kb0 + kb) * 32, row0, &xfull[xr.idx]);
         }
       }
     x_done:
@@ -788,7 +857,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         const TileRef t = src.at(tile, rank, plan);
         // dense FP32 weights are read by the converters themselves
         const bool has_w = t.n_tile < PQ8_TP(t, n_tiles) && !(!SEQ && p.w_f32);
-        const uint8_t* wt = PQ8_TP(t, w) + PQ8_HEADER_BYTES + (size_t)t.n_tile * t.kb * kRecordBytes;
+        const uint8_t* wt = PQ8_TP(t, w) + PQ8_HEADER_BYTES +
+                            ((size_t)t.n_tile * PQ8_TP(t, k_blocks) + t.kb0) * kRecordBytes;
         for (int kb = 0; kb < t.kb; ++kb, ++issued, wr.advance(1)) {
           if (!mbar_wait(&wempty[wr.idx], wr.phase ^ 1u, abort_flag, status)) goto w_done;
           if (has_w) {
@@ -863,7 +933,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       bool stop = false;
       int local = 0;
       TileWindow<C::kCtas, SEQ> win{};
-      if constexpr (!SEQ) win = TileWindow<C::kCtas, SEQ>{p.m_tiles, p.k_blocks};
+      if constexpr (!SEQ) win = TileWindow<C::kCtas, SEQ>{p.m_tiles, p.k_blocks, p.k_splits};
       for (int tile = unit0; tile < num_tiles && !stop; tile += unit_stride, ++local) {
         const int KB = win.get(local, rank, plan).kb;
         const int acc = local % ACC;

@@ -101,7 +101,7 @@ class HostRuntime:
     """One device: driver context, compute stream, weight arena, GEMV workspace."""
 
     def __init__(self, index: int = 0, weight_bytes: int = 1024 * MIB, work_bytes: int = 256 * MIB,
-                 workspace_bytes: int = 8 * MIB, lib: pq8.Library | None = None):
+                 workspace_bytes: int = 16 * MIB, lib: pq8.Library | None = None):
         self.drv = Driver(index)
         info = self.drv.info()
         if info['sm'] != 100:
@@ -173,6 +173,7 @@ class HostRuntime:
         """As ``gemm``, with the library choosing the GEMV for a few rows."""
         if 1 <= m <= GEMV_MAX_M and self.lib.gemv_workspace_size(m, w.n, w.k) > self.workspace.nbytes:
             raise MemoryError(f'GEMV workspace of {self.workspace.nbytes} bytes is too small for [{m}, {w.n}, {w.k}]')
+        # (a workspace too small for split K only runs the GEMM unsplit)
         self.lib.call('pq8_linear', w.pointer, x.pointer, out.pointer, _ptr(bias), _ptr(resid), m, w.n, w.k, epilogue,
                       float(alpha), flags, self.workspace.pointer, self.workspace.nbytes, self.stream.handle)
 

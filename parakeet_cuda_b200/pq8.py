@@ -65,6 +65,7 @@ SIGNATURES = {
     'pq8_round_tf32': ([_P, _LL, _P], _I),
     'pq8_gemm': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P], _I),
     'pq8_gemv_workspace_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
+    'pq8_linear_workspace_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
     'pq8_workspace_init': ([_P, _SZ, _P], _I),
     'pq8_gemv': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _SZ, _P], _I),
     'pq8_gemv_static': ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P], _I),
@@ -122,6 +123,11 @@ class Library:
     def gemv_workspace_size(self, m: int, n: int, k: int) -> int:
         out = _SZ()
         self.call('pq8_gemv_workspace_size', m, n, k, C.byref(out))
+        return out.value
+
+    def linear_workspace_size(self, m: int, n: int, k: int) -> int:
+        out = _SZ()
+        self.call('pq8_linear_workspace_size', m, n, k, C.byref(out))
         return out.value
 
     def stem_workspace_size(self, windows: int, frames: int) -> int:

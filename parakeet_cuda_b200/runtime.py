@@ -236,7 +236,7 @@ class Runtime:
 
     # -- workspace ----------------------------------------------------------
     def ensure_workspace(self, m: int, n: int, k: int) -> None:
-        need = self.lib.gemv_workspace_size(m, n, k)
+        need = self.lib.linear_workspace_size(m, n, k)
         if need > self.workspace.numel():
             with torch.cuda.device(self.device):
                 self.workspace = torch.empty(max(need, 2 * self.workspace.numel()), dtype=torch.uint8,
@@ -253,7 +253,7 @@ class Runtime:
         if out is None:
             out = torch.empty(rows, w.out_features if epilogue == EPI_GLU else w.n, dtype=torch.float32,
                               device=self.device)
-        if 1 <= rows <= GEMV_MAX_M:
+        if rows >= 1:
             self.ensure_workspace(rows, w.n, k)
         self.lib.call('pq8_linear', w.pointer, x.data_ptr(), out.data_ptr(), _ptr(bias), _ptr(resid), rows, w.n, k,
                       epilogue, float(alpha), flags, self.workspace.data_ptr(), self.workspace.numel(),

@@ -220,7 +220,8 @@ def test_linear_dispatch_gemv_matches_gemm(rt):
                                           (64, 4096, 1024, 'gemm'), (9, 129, 1024, 'gemv')])
 def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
     """pq8_linear sends 9..64 rows to whichever kernel its measured cost model
-    finds faster: the result is bit for bit that kernel's."""
+    finds faster: the result is bit for bit that kernel's (for the tensor-core
+    GEMM, its unsplit form: the workspace is withheld, which turns split K off)."""
     rng = np.random.default_rng(m + n)
     raw = q8_0_blocks(rng, n, k)
     w = rt.pack(raw, n, k)
@@ -228,6 +229,12 @@ def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
     got = rt.linear(xd, w).cpu().numpy()
     if kernel == 'gemm':
         want = rt.gemm(xd, w).cpu().numpy()
+        y = torch.empty(m, n, device='cuda')
+        rt.lib.call('pq8_linear', w.pointer, xd.data_ptr(), y.data_ptr(), None, None, m, n, k, EPI_NONE, 1.0, 0,
+                    None, 0, rt.stream())
+        np.testing.assert_array_equal(y.cpu().numpy(), want)
+        check_gemm(torch.from_numpy(got), xd.cpu().numpy(), raw, n, k)
+        return
     else:
         rt.ensure_workspace(m, n, k)
         y = torch.empty(m, n, device='cuda')
@@ -237,6 +244,75 @@ def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
     np.testing.assert_array_equal(got, want)
     gold = q8.gemm(np.asarray(xd.cpu().numpy()), raw, n, k)
     assert q8.max_err_over_rms(got, gold) <= NORTH_STAR
+
+
+SPLIT_CASES = [  # m, n, k, epilogue, bias: K splits (units = M tiles x N tiles of 128)
+    (128, 4096, 1024, EPI_NONE, False),     # config 0: 32 units, 4 splits of 8 K blocks
+    (256, 1024, 4096, EPI_NONE, True),      # 16 units, 8 splits
+    (130, 1000, 1056, EPI_SILU, True),      # ragged M and N, 33 K blocks: splits of 9, 9, 9, 6
+    (100, 640, 2048, EPI_RESIDUAL, False),  # 5 units, 8 splits
+    (128, 2048, 1024, EPI_GLU, True),       # GLU pairs split like any row
+    (64, 4096, 1024, EPI_NONE, False),      # 64 rows: the GEMM side of the dispatch, split
+]
+
+
+@pytest.mark.parametrize('m,n,k,epi,with_bias', SPLIT_CASES)
+def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias):
+    """pq8_linear splits K when the GEMM's tiles would fill at most half of the
+    SMs: the result meets the north-star bar and the TF32-operand model bar,
+    and a repeat call is bit for bit the same (the last split of a tile adds
+    the partials in split order and resets the tile's tickets)."""
+    assert rt.lib.linear_workspace_size(m, n, k) > (rt.lib.gemv_workspace_size(m, n, k) if m <= 64 else 0)
+    rng = np.random.default_rng(1000 + m + n + k)
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32) if with_bias else None
+    n_out = n // 2 if epi == EPI_GLU else n
+    resid = rng.normal(size=(m, n_out)).astype(np.float32) if epi == EPI_RESIDUAL else None
+    alpha = 0.5 if epi == EPI_RESIDUAL else 1.0
+    xd = dev(x)
+    args = dict(bias=dev(bias) if with_bias else None, resid=dev(resid) if resid is not None else None,
+                epilogue=epi, alpha=alpha)
+    y1 = rt.linear(xd, w, **args)
+    y2 = rt.linear(xd, w, **args)
+    torch.cuda.synchronize()
+    assert rt.device_status() == 0
+    np.testing.assert_array_equal(y1.cpu().numpy(), y2.cpu().numpy())
+    check_gemm(y1, x, raw, n, k, epi=epi, bias=bias, resid=resid, alpha=alpha)
+    # the tickets are back at zero: the counter area's first 2 x units words
+    units = ((m + 127) // 128) * ((n + 127) // 128)
+    assert int(rt.workspace[:8 * units].view(torch.int32).abs().sum()) == 0
+
+
+def test_linear_split_k_in_graph_repeats(rt):
+    """Twenty split launches captured in one CUDA graph and replayed: the
+    tickets of one launch are reset before the next reads them."""
+    m, n, k = 128, 4096, 1024
+    rng = np.random.default_rng(5)
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k)
+    xs = [dev(rng.normal(size=(m, k)).astype(np.float32)) for _ in range(2)]
+    ys = [torch.empty(m, n, device='cuda') for _ in range(20)]
+    want = [rt.linear(xs[i % 2], w).clone() for i in range(2)]
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        g.capture_begin()
+        for i, y in enumerate(ys):
+            rt.lib.call('pq8_linear', w.pointer, xs[i % 2].data_ptr(), y.data_ptr(), None, None, m, n, k, EPI_NONE,
+                        1.0, 0, rt.workspace.data_ptr(), rt.workspace.numel(), side.cuda_stream)
+        g.capture_end()
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert rt.device_status() == 0
+    for i, y in enumerate(ys):
+        assert torch.equal(y, want[i % 2])
+    del g
 
 
 def test_gemv_epilogues(rt):
