@@ -51,10 +51,17 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-extras', action='store_true', help='skip the GEMV and cuBLAS-TF32 side measurements')
     ap.add_argument('--tdt-batches', default='1,64', help='decode batch sizes of the tdt extra')
-    ap.add_argument('--extras', default='config0,refkernels,gemv,cublas,tdt,sweep,load,block,refgpu,cpu',
+    ap.add_argument('--extras', default=None,
                     help=('comma list of side measurements to run (config0, refkernels, gemv, cublas, tdt, sweep, '
-                          'load, block, refgpu, cpu)'))
-    return ap.parse_args()
+                          'load, block, refgpu, cpu); default all of them on one GPU, and on several GPUs only '
+                          'the ones that measure the job (sweep, block): the others repeat the one-GPU figures '
+                          'on every rank while all N GPUs are held'))
+    args = ap.parse_args()
+    if args.extras is None:
+        world = int(os.environ.get('WORLD_SIZE', 1))
+        args.extras = ('config0,refkernels,gemv,cublas,tdt,sweep,load,block,refgpu,cpu' if world == 1
+                       else 'sweep,block')
+    return args
 
 
 def config(args, n_gpus):

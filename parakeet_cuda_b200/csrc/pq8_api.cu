@@ -87,7 +87,8 @@ template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS, int WS
 int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaStream_t st) {
   using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES>;
   if (p.k_splits < 1) p.k_splits = 1;
-  if (p.k_splits > 1 && (PAIR || p.partial == nullptr || p.tickets == nullptr)) return PQ8_ERR_INVALID_ARGUMENT;
+  if (p.k_splits > 1 && (PAIR || C::kRedSlots < 1 || p.partial == nullptr || p.tickets == nullptr))
+    return PQ8_ERR_INVALID_ARGUMENT;
   EncodeTiledFn enc;
   int rc = encode_fn(&enc);
   if (rc) return rc;
@@ -126,6 +127,8 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   p.m_tiles = (p.m + BN - 1) / BN;
   const int units = (PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles) * p.m_tiles * p.k_splits;
   const int slots = PAIR ? ds->sms / 2 : ds->sms;
+  // a split CTA runs exactly one tile (its last split reuses the activation ring)
+  if (p.k_splits > 1 && units > slots) return PQ8_ERR_INVALID_ARGUMENT;
   const int grid = std::min(units, slots) * C::kCtas;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -917,9 +920,14 @@ bool gemv_faster(int m, int n, int k) {
 }
 
 // Split K for pq8_linear's GEMM path: when BN = 128 tiles would fill at most
-// half of the SMs, each tile's K blocks are shared by up to 8 CTAs (at least
-// 8 K blocks each) and the partial sums go through the workspace: the counter
-// area's first words are the tiles' tickets, the partials follow it.
+// half of the SMs and K is long (>= 64 blocks), each tile's K blocks are shared
+// by up to 8 CTAs (at least 16 K blocks each) and the partial sums go through
+// the workspace: the counter area's first words are the tiles' tickets, the
+// partials follow it. Measured on B200: a tile's single-CTA pipeline runs
+// about 0.48 us per K block, and the last split pulls the others' partials
+// back at about 1.3 us per split, so shorter K ranges gain nothing
+// (M = 128 x N = 1024 x K = 4096: 54 us unsplit, 24 us in 8 splits; K = 1024
+// shapes within 0.5 us either way).
 struct SplitPlan {
   int splits;
   size_t bytes;
@@ -928,8 +936,14 @@ SplitPlan plan_split(int m, int n, int k, int sms) {
   SplitPlan sp{1, 0};
   const long long units = static_cast<long long>((m + 127) / 128) * ((n + kTileRows - 1) / kTileRows);
   const int kb = k / 32;
-  if (units * 2 > sms || kb < 16) return sp;
-  const long long s = std::min<long long>({sms / units, kb / 8, 8});
+  long long s = std::min<long long>({sms / units, kb / 16, 8});
+  if (units * 2 > sms || kb < 64) s = 1;
+  // PQ8_LINEAR_SPLITS=<s> in the environment forces the split count (within
+  // the same limits: one tile per CTA, at least 2 K blocks per split)
+  if (const char* force = std::getenv("PQ8_LINEAR_SPLITS"))
+    s = std::min<long long>({std::max(1, std::atoi(force)), sms / units, kb / 2, 8});
+  // every split gets K blocks: splits of ceil(kb / s) blocks, the last one shorter
+  while (s > 1 && (s - 1) * ((kb + s - 1) / s) >= kb) --s;
   if (s < 2) return sp;
   sp.splits = static_cast<int>(s);
   sp.bytes = kGemvCounterBytes + round256(sizeof(float) * static_cast<size_t>(units) * s * 128 * kTileRows);

@@ -111,7 +111,14 @@ struct GemmCfg {
   static constexpr int kOutChunkFloats = 32 * 128;
   static constexpr int kOutOff = kWOff + WSTAGES * kRecordBytes;
   static constexpr int kBarOff = kOutOff + 4 * kOutChunkFloats * 4;
-  static constexpr int kNumBars = 2 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1;
+  // Split K: the last split of a tile pulls the partial sums back with bulk
+  // copies, one [kEpiCols activation rows][128] piece per (chunk, split),
+  // into the activation ring (idle by then: a split CTA runs one tile),
+  // kRedSlots pieces in flight per epilogue half.
+  static constexpr int kRedPieceBytes = kEpiCols * 128 * 4;
+  static constexpr int kRedSlotsFit = STAGES * kXStageBytes / (2 * kRedPieceBytes);
+  static constexpr int kRedSlots = kRedSlotsFit < 4 ? kRedSlotsFit : 4;
+  static constexpr int kNumBars = 2 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1 + 8;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kUsedBytes = kMiscOff + 24;
   static constexpr int kAColBase = ACC * BN;
@@ -410,6 +417,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   uint64_t* acc_full = afree + ASLOTS;
   uint64_t* acc_empty = acc_full + ACC;
   uint64_t* drain = acc_empty + ACC;
+  uint64_t* red_full = drain + 1;  // [2 halves][4]: split-K partial pieces landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   int* bad_flag = reinterpret_cast<int*>(smem + C::kMiscOff + 8);
@@ -461,6 +469,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       mbar_init(&acc_empty[a], C::kEpiWarps * C::kCtas);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
+    for (int b = 0; b < 8; ++b) mbar_init(&red_full[b], 1);
     fence_mbar_init();
   }
   if (warp == C::kTmaWarp && lane == 0 && !SEQ) {
@@ -648,6 +657,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     constexpr int E = C::kEpiCols;
     constexpr int kChunks = BN / E / 2;            // E-column chunks per half
     int chunk_seq = 0;                             // chunks issued by this half (selects the buffer)
+    // split K: this half's piece slots, and the pieces its elected thread has
+    // issued and seen land
+    float* const red_buf = reinterpret_cast<float*>(xs) + half * C::kRedSlots * (C::kRedPieceBytes / 4);
+    int red_issued = 0, red_landed = 0;
     int local = 0;
     griddep_wait();  // the residual and the output may be in use by the previous kernel
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
@@ -697,6 +710,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       // ticket; only the last split goes on, summing every split's partial in
       // split order (the same order whichever CTA is last) before the epilogue.
       const float* partials = nullptr;
+      auto issue_piece = [&](int i) {  // piece i = (chunk i / splits, split i % splits)
+        const int slot = i % C::kRedSlots;
+        const float* piece = partials + (size_t)(i % p.k_splits) * (BN * kTileRows) +
+                             (size_t)((half * kChunks + i / p.k_splits) * E) * kTileRows;
+        mbar_expect_tx(&red_full[half * 4 + slot], C::kRedPieceBytes);
+        bulk_g2s(red_buf + slot * (C::kRedPieceBytes / 4), piece, C::kRedPieceBytes, &red_full[half * 4 + slot]);
+      };
       if (split) {
         const int out_tile = tile / p.k_splits;
         float* mine = p.partial + ((size_t)out_tile * p.k_splits + t.split) * (BN * kTileRows);
@@ -715,17 +735,22 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         __threadfence();
         named_barrier_sync(1 + half, 128);
         volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 12 + 4 * half);
+        partials = p.partial + (size_t)out_tile * p.k_splits * (BN * kTileRows);
         if (elected) {
           int* ticket = p.tickets + out_tile * 2 + half;
           const bool last = atomicAdd(ticket, 1) == p.k_splits - 1;
-          if (last) atomicExch(ticket, 0);  // every split has taken its ticket
-          __threadfence();
+          if (last) {
+            atomicExch(ticket, 0);  // every split has taken its ticket
+            __threadfence();
+            fence_proxy_async_global();  // the other splits' partials, read by the bulk-copy unit
+            const int first = min(C::kRedSlots, kChunks * p.k_splits);
+            for (int i = 0; i < first; ++i) issue_piece(i);
+            red_issued = first;
+          }
           *last_flag = last ? 1 : 0;
         }
         named_barrier_sync(1 + half, 128);
         if (!*last_flag) continue;
-        __threadfence();
-        partials = p.partial + (size_t)out_tile * p.k_splits * (BN * kTileRows);
         if (resid) load_resid(m_tile * BN + half * kChunks * E);
       }
 #pragma unroll 1
@@ -735,13 +760,26 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         if (m0 >= m) break;
         uint32_t v[E];
         if (split) {
+          // the chunk's pieces, split by split, added in split order (onto
+          // +0, which leaves the first piece's values as they are)
+          bool ok = true;
 #pragma unroll
-          for (int j = 0; j < E; ++j) {
-            const float* col = partials + (size_t)(c * E + j) * kTileRows + r;
-            float sum = __ldcg(col);
-            for (int sp = 1; sp < p.k_splits; ++sp) sum += __ldcg(col + (size_t)sp * (BN * kTileRows));
-            v[j] = __float_as_uint(sum);
+          for (int j = 0; j < E; ++j) v[j] = 0u;
+#pragma unroll 1
+          for (int sp = 0; sp < p.k_splits; ++sp) {
+            const int i = cc * p.k_splits + sp, slot = i % C::kRedSlots;
+            if (!mbar_wait(&red_full[half * 4 + slot], (i / C::kRedSlots) & 1, abort_flag, status)) {
+              ok = false;
+              break;
+            }
+            ++red_landed;
+            const float* piece = red_buf + slot * (C::kRedPieceBytes / 4) + r;
+#pragma unroll
+            for (int j = 0; j < E; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + piece[j * kTileRows]);
+            named_barrier_sync(1 + half, 128);  // every thread of the half is done with the slot
+            if (elected && red_issued < kChunks * p.k_splits) issue_piece(red_issued++);
           }
+          if (!ok) break;
         } else {
           tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
           tmem_wait_ld();
@@ -818,7 +856,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         }
       }
     }
-    if (elected) bulk_wait_group_all();
+    if (elected) {
+      bulk_wait_group_all();
+      // after an abort: never leave pieces still landing in shared memory
+      for (int i = red_landed; i < red_issued; ++i)
+        mbar_drain(&red_full[half * 4 + i % C::kRedSlots], (i / C::kRedSlots) & 1);
+    }
   } else if (warp == C::kTmaWarp) {
     // ----------------------------------------------------- activation producer
     if (lane == 0) {

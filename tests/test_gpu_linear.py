@@ -246,26 +246,31 @@ def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
     assert q8.max_err_over_rms(got, gold) <= NORTH_STAR
 
 
-SPLIT_CASES = [  # m, n, k, epilogue, bias: K splits (units = M tiles x N tiles of 128)
-    (128, 4096, 1024, EPI_NONE, False),     # config 0: 32 units, 4 splits of 8 K blocks
-    (256, 1024, 4096, EPI_NONE, True),      # 16 units, 8 splits
-    (130, 1000, 1056, EPI_SILU, True),      # ragged M and N, 33 K blocks: splits of 9, 9, 9, 6
-    (100, 640, 2048, EPI_RESIDUAL, False),  # 5 units, 8 splits
-    (128, 2048, 1024, EPI_GLU, True),       # GLU pairs split like any row
-    (64, 4096, 1024, EPI_NONE, False),      # 64 rows: the GEMM side of the dispatch, split
+SPLIT_CASES = [  # m, n, k, epilogue, bias, forced splits: units = M tiles x N tiles of 128
+    (128, 1024, 4096, EPI_NONE, False, None),     # 8 units, 8 splits of 16 K blocks
+    (441, 1024, 4096, EPI_NONE, True, None),      # reference contract shape: 32 units, 4 splits
+    (130, 1000, 2080, EPI_SILU, True, None),      # ragged M and N, 65 K blocks: splits of 17, 17, 17, 14
+    (100, 640, 2048, EPI_RESIDUAL, False, None),  # 5 units, 4 splits
+    (128, 2048, 2048, EPI_GLU, True, None),       # GLU pairs split like any row
+    (64, 4096, 2048, EPI_NONE, False, None),      # 64 rows on the GEMM side of the dispatch
+    (128, 4096, 1024, EPI_NONE, False, 4),        # config 0, forced: 4 splits of 8
+    (128, 1024, 1056, EPI_RESIDUAL, True, 8),     # forced 8 -> 7 splits: six of 5 K blocks and one of 3
 ]
 
 
-@pytest.mark.parametrize('m,n,k,epi,with_bias', SPLIT_CASES)
-def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias):
+@pytest.mark.parametrize('m,n,k,epi,with_bias,forced', SPLIT_CASES)
+def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias, forced, monkeypatch):
     """pq8_linear splits K when the GEMM's tiles would fill at most half of the
-    SMs: the result meets the north-star bar and the TF32-operand model bar,
-    and a repeat call is bit for bit the same (the last split of a tile adds
-    the partials in split order and resets the tile's tickets)."""
+    SMs and K is long (PQ8_LINEAR_SPLITS forces a count): the result meets the
+    north-star bar and the TF32-operand model bar, and a repeat call is bit for
+    bit the same (the last split of a tile adds the partials in split order
+    and resets the tile's tickets)."""
+    if forced:
+        monkeypatch.setenv('PQ8_LINEAR_SPLITS', str(forced))
     assert rt.lib.linear_workspace_size(m, n, k) > (rt.lib.gemv_workspace_size(m, n, k) if m <= 64 else 0)
     rng = np.random.default_rng(1000 + m + n + k)
     raw = q8_0_blocks(rng, n, k)
-    w = rt.pack(raw, n, k)
+    w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
     x = rng.normal(size=(m, k)).astype(np.float32)
     bias = rng.normal(size=n).astype(np.float32) if with_bias else None
     n_out = n // 2 if epi == EPI_GLU else n
@@ -288,7 +293,7 @@ def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias):
 def test_linear_split_k_in_graph_repeats(rt):
     """Twenty split launches captured in one CUDA graph and replayed: the
     tickets of one launch are reset before the next reads them."""
-    m, n, k = 128, 4096, 1024
+    m, n, k = 128, 1024, 4096
     rng = np.random.default_rng(5)
     raw = q8_0_blocks(rng, n, k)
     w = rt.pack(raw, n, k)
