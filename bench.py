@@ -876,7 +876,7 @@ def tdt_measure(torch, rt, batches=(1, 64)):
     from parakeet_cuda_b200.decoder import PQ8Decoder
     from parakeet_cuda_b200.pq8 import EPI_NONE
     from parakeet_cuda_b200.synthetic import SyntheticParakeet
-    from parakeet_cuda_b200.tdt import greedy_decode_batch, greedy_decode_device
+    from parakeet_cuda_b200.tdt import greedy_decode_batch, greedy_decode_device, greedy_decode_persistent
     model = SyntheticParakeet(seed=11, encoder_layers=0)
     rt.load_weights(model, ['joint.enc.weight', 'joint.enc.bias'])
     w_enc, b_enc = rt.weight('joint.enc.weight'), rt.weight('joint.enc.bias').reshape(-1)
@@ -919,6 +919,22 @@ def tdt_measure(torch, rt, batches=(1, 64)):
             'loop': 'device (pq8_tdt_advance; CUDA graph of 16 steps, host polls the remaining count); '
                     'steps_per_s over the replay loop, call_* over the whole call (frame table, graph capture, '
                     'results to host lists)'}
+        # the whole loop in one persistent launch (pq8_tdt_decode: weights resident in shared memory)
+        dper = PQ8Decoder(model, rt, batch=1)
+        greedy_decode_persistent([s[:20] for s in streams_dev], dper, model.metadata['asr.tdt.durations'])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res_per = greedy_decode_persistent(streams_dev, dper, model.metadata['asr.tdt.durations'])
+        t_per = time.perf_counter() - t0
+        calls_per = sum(r['joint_calls'] for r in res_per)
+        out[f'batch{batch}_persistent'] = {
+            'lockstep_steps': dper.steps, 'joint_calls': calls_per, 'kernel_seconds': dper.loop_seconds,
+            'us_per_step': dper.loop_seconds / max(dper.steps, 1) * 1e6,
+            'steps_per_s': dper.steps / dper.loop_seconds, 'joint_calls_per_s': calls_per / dper.loop_seconds,
+            'call_seconds': t_per, 'call_joint_calls_per_s': calls_per / t_per,
+            'same_result_as_host_loop': res_per == res,
+            'loop': 'device (pq8_tdt_decode: one cooperative launch for the whole decode); steps_per_s over the '
+                    'launch (CUDA events), call_* over the whole call'}
     return out
 
 

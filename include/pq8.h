@@ -253,6 +253,50 @@ PQ8_API int pq8_tdt_advance(const int* ids, const int* durations, int n_duration
                             int emitted_capacity, int* trace, int trace_capacity, int* remaining, float* h,
                             float* c, const float* h_new, const float* c_new, int layers, int hidden, void* stream);
 
+/* Weights of the TDT prediction and joint networks for pq8_tdt_decode, all
+ * resident on the device (H = hidden, J = joint width, E = embedding width):
+ *   lstm[l]       GATES4-packed [4H, in_l + H] = [W_ih | W_hh], in_0 = E, in_1 = H
+ *   lstm_bias[l]  b_ih + b_hh, float[4H] (gate order i, f, g, o)
+ *   pred          ROWS-packed joint.pred [J, H]; pred_bias float[J]
+ *   joint         ROWS-packed joint.joint_net.2 [n_joint, J]; joint_bias float[n_joint]
+ *   embed         fp16 [vocab][E] (decoder.prediction.embed; row 8192 is the blank's)
+ * vocab = number of token logits (the rest, n_joint - vocab, are durations). */
+typedef struct pq8_tdt_weights {
+  const void* lstm[2];
+  const float* lstm_bias[2];
+  const void* pred;
+  const float* pred_bias;
+  const void* joint;
+  const float* joint_bias;
+  const uint16_t* embed;
+  int hidden, embed_k, joint_k, n_joint, vocab;
+} pq8_tdt_weights;
+
+/* Workspace bytes pq8_tdt_decode needs for m streams. */
+PQ8_API int pq8_tdt_decode_workspace_size(int m, int hidden, int joint_k, size_t* bytes);
+
+/* The whole greedy TDT decode of m <= 64 streams in one persistent launch:
+ * the loop of decoder.py:78-97 (predict after an emitted token, joint, the
+ * control rules of pq8_tdt_control, commit) with no host round trip per step.
+ * One CTA per SM keeps its share of all four weights in shared memory for the
+ * whole decode; grid barriers (bounded waits: PQ8_ERR_TIMEOUT in the device
+ * status word) separate the joint from the prediction-network phases, and the
+ * prediction network runs only for streams that emitted.
+ * enc: stream i's projected frame t is row i * enc_stride + t of a float[.][J]
+ * table. state, emitted, trace: as pq8_tdt_control's (state word 7 holds the
+ * stream's committed LSTM slot); set state to {frames_i, 0, 0, 8192, 0, 0,
+ * frames_i == 0, 0} for a fresh decode (resume = 0: LSTM state and pred start
+ * from zero and the first prediction runs on the blank token). The launch
+ * stops when every stream is done or after max_steps joint steps; resume = 1
+ * continues such a decode from the workspace (same workspace, state and
+ * streams). *steps_out (device int) = joint steps run, *remaining (device
+ * int) = streams not done. Results equal the host loop's over pq8_lstm_layer,
+ * pq8_gemv and pq8_joint_argmax up to the order of FP32 additions. */
+PQ8_API int pq8_tdt_decode(const pq8_tdt_weights* weights, const float* enc, int enc_stride, const int* durations,
+                           int n_durations, int* state, int m, int* emitted, int emitted_capacity, int* trace,
+                           int trace_capacity, int max_steps, int resume, int* steps_out, int* remaining,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* pq8_gemv without a workspace argument, for callers that cannot allocate
  * device memory: a host that keeps all device memory in its own pre-reserved
  * pool, or a latency-critical loop where cudaMalloc would synchronize the

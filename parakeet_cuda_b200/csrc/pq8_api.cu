@@ -16,6 +16,7 @@
 #include "pq8_gemv.cuh"
 #include "pq8_block.cuh"
 #include "pq8_tdt.cuh"
+#include "pq8_decode.cuh"
 
 namespace pq8 {
 
@@ -1140,6 +1141,136 @@ extern "C" int pq8_tdt_advance(const int* ids, const int* durations, int n_durat
                              durations, n_durations, state, m, enc_stride, tokens, enc_rows, commit_mask, emitted,
                              emitted_capacity, trace, trace_capacity, remaining, h, c, h_new, c_new, layers, hidden,
                              ds->status);
+  if (e != cudaSuccess) return to_code(e);
+  return to_code(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- persistent TDT decode
+namespace {
+
+struct DecodeWorkspace {
+  size_t keys, h, c, pred, total;
+};
+
+DecodeWorkspace decode_workspace(int m, int hidden, int joint_k) {
+  DecodeWorkspace d{};
+  size_t off = 256;  // barrier counter at 0, abort flag at 4
+  d.keys = off;
+  off += round256(3 * sizeof(unsigned long long) * 2 * m);
+  d.h = off;
+  off += round256(sizeof(float) * 4 * (size_t)m * hidden);
+  d.c = off;
+  off += round256(sizeof(float) * 4 * (size_t)m * hidden);
+  d.pred = off;
+  off += round256(sizeof(float) * (size_t)m * joint_k);
+  d.total = off;
+  return d;
+}
+
+}  // namespace
+
+extern "C" int pq8_tdt_decode_workspace_size(int m, int hidden, int joint_k, size_t* bytes) {
+  if (bytes == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (m < 1 || m > kDecodeMaxStreams || hidden < 32 || hidden % 32 || joint_k < 32 || joint_k % 32)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  *bytes = decode_workspace(m, hidden, joint_k).total;
+  return PQ8_OK;
+}
+
+extern "C" int pq8_tdt_decode(const pq8_tdt_weights* w, const float* enc, int enc_stride, const int* durations,
+                              int n_durations, int* state, int m, int* emitted, int emitted_capacity, int* trace,
+                              int trace_capacity, int max_steps, int resume, int* steps_out, int* remaining,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (w == nullptr || enc == nullptr || durations == nullptr || state == nullptr || steps_out == nullptr ||
+      remaining == nullptr || workspace == nullptr || (emitted_capacity > 0 && emitted == nullptr) ||
+      (trace_capacity > 0 && trace == nullptr))
+    return PQ8_ERR_INVALID_ARGUMENT;
+  for (int l = 0; l < 2; ++l)
+    if (w->lstm[l] == nullptr || w->lstm_bias[l] == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (w->pred == nullptr || w->pred_bias == nullptr || w->joint == nullptr || w->joint_bias == nullptr ||
+      w->embed == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  const int H = w->hidden, E = w->embed_k, J = w->joint_k;
+  if (m < 1 || m > kDecodeMaxStreams || H < 32 || H % 32 || E < 32 || E % 32 || J < 32 || J % 32 ||
+      w->vocab < 1 || w->n_joint <= w->vocab || n_durations < 1 || enc_stride < 0 || max_steps < 0 ||
+      emitted_capacity < 0 || trace_capacity < 0)
+    return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned(enc, 16) || !aligned(workspace, 256)) return PQ8_ERR_MISALIGNED;
+  for (int l = 0; l < 2; ++l)
+    if (!aligned(w->lstm[l], 16)) return PQ8_ERR_MISALIGNED;
+  if (!aligned(w->pred, 16) || !aligned(w->joint, 16) || !aligned(w->embed, 8)) return PQ8_ERR_MISALIGNED;
+  const DecodeWorkspace d = decode_workspace(m, H, J);
+  if (workspace_bytes < d.total) return PQ8_ERR_WORKSPACE;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  // one CTA per SM, and every CTA gets at least one row of every matrix
+  const int grid = std::min({ds->sms, H, J, w->n_joint});
+  auto ceil_div = [](int a, int b) { return (a + b - 1) / b; };
+  const int kmax = std::max(E + H, std::max(2 * H, J));
+  const DecodeLayout L = decode_layout(ceil_div(w->n_joint, grid), ceil_div(H, grid), ceil_div(J, grid), J / 32,
+                                       (E + H) / 32, 2 * H / 32, H / 32, kmax, m);
+  if (L.total > 227u * 1024u) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  cudaError_t e = cudaFuncSetAttribute(tdt_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+  if (e != cudaSuccess) return to_code(e);
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tdt_decode_kernel, kDecodeThreads, L.total);
+  if (e != cudaSuccess) return to_code(e);
+  if (per_sm < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* base = static_cast<unsigned char*>(workspace);
+  // fresh: zero LSTM state, pred, keys and the barrier; resumed: keys and barrier only
+  e = cudaMemsetAsync(base, 0, resume ? d.h : d.total, st);
+  if (e != cudaSuccess) return to_code(e);
+  DecodeParams p{};
+  for (int l = 0; l < 2; ++l) {
+    p.w_lstm[l] = static_cast<const uint8_t*>(w->lstm[l]);
+    p.b_lstm[l] = w->lstm_bias[l];
+  }
+  p.w_pred = static_cast<const uint8_t*>(w->pred);
+  p.b_pred = w->pred_bias;
+  p.w_joint = static_cast<const uint8_t*>(w->joint);
+  p.b_joint = w->joint_bias;
+  p.embed = w->embed;
+  p.enc = enc;
+  p.durations = durations;
+  p.state = state;
+  p.emitted = emitted;
+  p.trace = trace;
+  p.steps_out = steps_out;
+  p.remaining = remaining;
+  p.barrier = reinterpret_cast<unsigned*>(base);
+  p.abort = reinterpret_cast<int*>(base + 4);
+  p.keys = reinterpret_cast<unsigned long long*>(base + d.keys);
+  p.h = reinterpret_cast<float*>(base + d.h);
+  p.c = reinterpret_cast<float*>(base + d.c);
+  p.pred = reinterpret_cast<float*>(base + d.pred);
+  p.status = ds->status;
+  p.m = m;
+  p.hidden = H;
+  p.embed_k = E;
+  p.joint_k = J;
+  p.n_joint = w->n_joint;
+  p.vocab = w->vocab;
+  p.n_durations = n_durations;
+  p.enc_stride = enc_stride;
+  p.emitted_capacity = emitted_capacity;
+  p.trace_capacity = trace_capacity;
+  p.max_steps = max_steps;
+  p.resume = resume ? 1 : 0;
+  // all CTAs must be resident at once: a cooperative launch fails instead of
+  // running with some of them waiting for an SM
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, tdt_decode_kernel, p);
   if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }

@@ -47,6 +47,13 @@ class GemmTask(C.Structure):
                 ('epilogue', _I), ('alpha', _F), ('flags', _I), ('after', _I), ('after_window', _I)]
 
 
+class TdtWeights(C.Structure):
+    """``pq8_tdt_weights``: the prediction and joint networks for ``pq8_tdt_decode``."""
+    _fields_ = [('lstm', _P * 2), ('lstm_bias', _P * 2), ('pred', _P), ('pred_bias', _P), ('joint', _P),
+                ('joint_bias', _P), ('embed', _P), ('hidden', _I), ('embed_k', _I), ('joint_k', _I),
+                ('n_joint', _I), ('vocab', _I)]
+
+
 SIGNATURES = {
     'pq8_error_string': ([_I], C.c_char_p),
     'pq8_version': ([], _I),
@@ -79,6 +86,9 @@ SIGNATURES = {
     'pq8_sequence_plan_size': ([C.POINTER(GemmTask), _I, C.POINTER(_SZ)], _I),
     'pq8_sequence_plan': ([C.POINTER(GemmTask), _I, _P, _SZ, _P], _I),
     'pq8_sequence_run': ([_P, _P], _I),
+    'pq8_tdt_decode_workspace_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
+    'pq8_tdt_decode': ([C.POINTER(TdtWeights), _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _I, _P, _P, _P, _SZ,
+                        _P], _I),
 }
 
 
@@ -123,6 +133,11 @@ class Library:
     def gemv_workspace_size(self, m: int, n: int, k: int) -> int:
         out = _SZ()
         self.call('pq8_gemv_workspace_size', m, n, k, C.byref(out))
+        return out.value
+
+    def tdt_decode_workspace_size(self, m: int, hidden: int, joint_k: int) -> int:
+        out = _SZ()
+        self.call('pq8_tdt_decode_workspace_size', m, hidden, joint_k, C.byref(out))
         return out.value
 
     def linear_workspace_size(self, m: int, n: int, k: int) -> int:

@@ -20,6 +20,7 @@ bit-identical candidates, so the results equal ``greedy_decode_batch``'s.
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass, field
 import time
 
@@ -211,6 +212,11 @@ def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 1
     status = rt.device_status()
     if status:
         raise RuntimeError(f'device status {status} after the device TDT loop')
+    return _device_results(state, emitted, trace, b)
+
+
+def _device_results(state, emitted, trace, b: int) -> list:
+    """Per-stream results from the device records of pq8_tdt_control's layout."""
     st = state.cpu().numpy()
     # only the filled prefix of the per-stream records crosses to the host
     em = emitted[:, :max(1, int(st[:, 4].max()))].cpu().numpy()
@@ -227,3 +233,75 @@ def greedy_decode_device(projected, decoder, durations, steps_per_graph: int = 1
             'joint_calls': nc,
         })
     return out
+
+
+def greedy_decode_persistent(projected, decoder, durations, max_steps: int | None = None,
+                             steps_per_launch: int | None = None) -> list:
+    """B <= 64 streams (``projected[b]`` = frames of stream b, [T_b, 640], a host
+    array or a device tensor) through ``pq8_tdt_decode``: the whole greedy loop
+    in one persistent launch on ``decoder``'s resident weights (or one launch
+    per ``steps_per_launch`` lock-step steps, each resuming the last). Same
+    results as ``greedy_decode_batch`` up to the order of FP32 additions in the
+    products. ``decoder.loop_seconds`` = device time of the launches (CUDA
+    events), ``decoder.steps`` = lock-step steps."""
+    from .decoder import VOCAB
+    from .pq8 import TdtWeights
+    b = len(projected)
+    if not 1 <= b <= 64:
+        raise ValueError(f'pq8_tdt_decode takes 1..64 streams, got {b}')
+    rt, dev = decoder.rt, decoder.rt.device
+    frames = [int(p.shape[0]) for p in projected]
+    t_max = max(max(frames), 1)
+    enc = torch.zeros(b * t_max, int(projected[0].shape[1]), dtype=torch.float32, device=dev)
+    for i, p in enumerate(projected):
+        if frames[i]:
+            src = p if isinstance(p, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(p, np.float32))
+            enc[i * t_max:i * t_max + frames[i]].copy_(src)
+    cap = t_max * MAX_SYMBOLS
+    i32 = dict(dtype=torch.int32, device=dev)
+    state = torch.zeros(b, 8, dtype=torch.int32)
+    state[:, 0] = torch.tensor(frames, dtype=torch.int32)
+    state[:, 3] = BLANK
+    state[:, 6] = (state[:, 0] == 0).to(torch.int32)
+    state = state.to(dev)
+    dur = torch.tensor(list(durations), **i32)
+    emitted = torch.zeros(b, cap, 3, **i32)
+    trace = torch.zeros(b, cap, 3, **i32)
+    counters = torch.zeros(2, **i32)  # steps run, streams remaining
+    w = TdtWeights()
+    for l in range(LAYERS):
+        w.lstm[l] = decoder.lstm[l][0].pointer
+        w.lstm_bias[l] = decoder.lstm[l][1].data_ptr()
+    w.pred, w.pred_bias = decoder.w_pred.pointer, decoder.b_pred.data_ptr()
+    w.joint, w.joint_bias = decoder.w_joint.pointer, decoder.b_joint.data_ptr()
+    w.embed = decoder.embed.data_ptr()
+    w.hidden, w.embed_k, w.joint_k = HIDDEN, decoder.lstm[0][2], decoder.w_joint.k
+    w.n_joint, w.vocab = decoder.n_out, VOCAB
+    lib = rt.lib
+    ws = torch.empty(lib.tdt_decode_workspace_size(b, HIDDEN, w.joint_k), dtype=torch.uint8, device=dev)
+    # a stream of T frames takes at most T * MAX_SYMBOLS joint calls
+    limit = cap if max_steps is None else max_steps
+    per = steps_per_launch or max(limit, 1)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = rt.stream()
+    steps, resume, seconds = 0, 0, 0.0
+    while steps < limit or (steps == 0 and limit == 0):
+        n = min(per, limit - steps)
+        e0.record()
+        lib.call('pq8_tdt_decode', C.byref(w), enc.data_ptr(), t_max, dur.data_ptr(), dur.numel(), state.data_ptr(),
+                 b, emitted.data_ptr(), cap, trace.data_ptr(), cap, n, resume, counters[0:1].data_ptr(),
+                 counters[1:2].data_ptr(), ws.data_ptr(), ws.numel(), st)
+        e1.record()
+        e1.synchronize()
+        seconds += e0.elapsed_time(e1) / 1e3
+        ran, remaining = (int(v) for v in counters.cpu().tolist())
+        steps += ran
+        resume = 1
+        if remaining == 0 or ran < n or n == 0:
+            break
+    decoder.loop_seconds, decoder.steps = seconds, steps
+    status = rt.device_status()
+    if status:
+        raise RuntimeError(f'device status {status} after pq8_tdt_decode')
+    return _device_results(state, emitted, trace, b)

@@ -11,7 +11,7 @@ from parakeet_cuda_b200 import pq8
 from parakeet_cuda_b200.decoder import PQ8Decoder
 from parakeet_cuda_b200.runtime import Runtime, pack_concat_host
 from parakeet_cuda_b200.synthetic import SyntheticParakeet, q8_0_blocks
-from parakeet_cuda_b200.tdt import greedy_decode, greedy_decode_batch, greedy_decode_device
+from parakeet_cuda_b200.tdt import greedy_decode, greedy_decode_batch, greedy_decode_device, greedy_decode_persistent
 
 pytestmark = pytest.mark.gpu
 
@@ -227,6 +227,88 @@ def test_tdt_device_loop_step_limit(rt):
     assert d.steps == 37 and r['joint_calls'] == 37
     ref = otdt.greedy_decode(projected[0], otdt.Decoder64(model), DURATIONS)
     assert r['decode_trace'] == ref['decode_trace'][:37]
+
+
+def check_streams_vs_oracle(projected, got, model, max_ties):
+    """Every call's (frame, token, skip) equals the float64 oracle's, or is a
+    near-tie (within TIE_EPS) that the oracle adopts; returns the tie count."""
+    ref = otdt.greedy_decode_streams(projected, model, DURATIONS, follow=[g['decode_trace'] for g in got],
+                                     tie_eps=TIE_EPS)
+    ties = 0
+    for i, (g, r) in enumerate(zip(got, ref)):
+        assert r['mismatch'] is None, (i, r['mismatch'])
+        assert g['decode_trace'] == r['decode_trace'], i
+        assert g['tokens'] == r['tokens'], i
+        assert g['joint_calls'] == r['joint_calls'], i
+        ties += r['ties']
+    assert ties <= max_ties
+    return ties
+
+
+def test_tdt_persistent_matches_reference_golden(rt, golden_dir):
+    """pq8_tdt_decode (the whole loop in one launch) on the reference's own
+    decodes: blanks, zero durations and the 10-symbol cap."""
+    meta = json.loads((golden_dir / 'golden_meta.json').read_text())
+    data = np.load(golden_dir / 'tdt_decode.npz')
+    for case in meta['tdt_random']:
+        seed = case['seed']
+        model = SyntheticParakeet(seed=seed, encoder_layers=0, blank_bias=case['blank_bias'],
+                                  duration0_bias=case['duration0_bias'])
+        [r] = greedy_decode_persistent([data[f'seed{seed}_projected']], PQ8Decoder(model, rt, batch=1), DURATIONS)
+        np.testing.assert_array_equal(np.asarray(r['tokens'], np.int32), data[f'seed{seed}_tokens'])
+        np.testing.assert_array_equal(np.asarray(r['decode_trace'], np.int32).reshape(-1, 3),
+                                      data[f'seed{seed}_trace'])
+        assert r['joint_calls'] == case['joint_calls']
+    assert rt.device_status() == 0
+
+
+@pytest.mark.parametrize('batch', [1, 4, 13, 64])
+def test_tdt_persistent_matches_oracle(rt, batch):
+    """Streams of different lengths (one empty) with blanks in the mix: the
+    persistent decode against the float64 oracle, call by call."""
+    model = SyntheticParakeet(seed=12, encoder_layers=0, blank_bias=1.0)
+    rng = np.random.default_rng(90 + batch)
+    lengths = [int(rng.integers(5, 60)) for _ in range(batch)]
+    if batch > 1:
+        lengths[1] = 0
+    projected = [rng.normal(size=(n, 640)).astype(np.float32) for n in lengths]
+    got = greedy_decode_persistent(projected, PQ8Decoder(model, rt, batch=1), DURATIONS)
+    check_streams_vs_oracle(projected, got, model, max_ties=2)
+    assert rt.device_status() == 0
+
+
+def test_tdt_persistent_batch64_1000_steps_matches_oracle(rt):
+    """BASELINE config 3 at batch 64 through pq8_tdt_decode: 64 streams of
+    1400 frames, at least 1000 joint calls each, against the float64 oracle."""
+    model = SyntheticParakeet(seed=11, encoder_layers=0)
+    rng = np.random.default_rng(2027)
+    projected = [rng.normal(size=(1400, 640)).astype(np.float32) for _ in range(64)]
+    d = PQ8Decoder(model, rt, batch=1)
+    got = greedy_decode_persistent(projected, d, DURATIONS)
+    assert min(g['joint_calls'] for g in got) >= 1000
+    ties = check_streams_vs_oracle(projected, got, model, max_ties=8)
+    print(f'batch 64: {d.steps} steps in {d.loop_seconds * 1e3:.2f} ms, {ties} near-ties')
+    assert rt.device_status() == 0
+
+
+def test_tdt_persistent_resume_and_step_limit(rt):
+    """A decode split over launches of 37 steps (each resuming the last from
+    the workspace) equals the one-launch decode bit for bit; max_steps stops
+    after exactly that many steps."""
+    model = SyntheticParakeet(seed=12, encoder_layers=0, blank_bias=1.0)
+    rng = np.random.default_rng(123)
+    projected = [rng.normal(size=(int(n), 640)).astype(np.float32) for n in (80, 3, 51, 120)]
+    d = PQ8Decoder(model, rt, batch=1)
+    whole = greedy_decode_persistent(projected, d, DURATIONS)
+    steps = d.steps
+    pieces = greedy_decode_persistent(projected, d, DURATIONS, steps_per_launch=37)
+    assert d.steps == steps
+    assert pieces == whole
+    cut = greedy_decode_persistent(projected, d, DURATIONS, max_steps=37)
+    assert d.steps == 37
+    for c, w in zip(cut, whole):
+        assert c['decode_trace'] == w['decode_trace'][:37]
+    assert rt.device_status() == 0
 
 
 @pytest.mark.parametrize('m', [1, 7, 300])
