@@ -1094,8 +1094,14 @@ def merge_sweep(parts, peaks):
 
 
 def sweep_measure(torch, rt, rank=0, world=1):
-    """This rank's config-4 points through pq8_linear (CUDA events, 10 launches
-    per point after one untimed); ``merge_sweep`` combines the ranks."""
+    """This rank's config-4 points through pq8_linear, each timed as a CUDA graph
+    of back-to-back launches (the reference's own graph method,
+    analysis/benchmark_dense.py:47-63: launch overhead out of the figure), best
+    of 3 replays. Where the Q8_0 matrix would stay in the 126 MB L2 between
+    launches, the launches rotate over copies of it totalling >= 256 MB, so
+    every launch streams its weights from HBM. ``merge_sweep`` combines the
+    ranks."""
+    import dataclasses
     import numpy as np
     from parakeet_cuda_b200.synthetic import q8_0_blocks
     weights = {}
@@ -1103,20 +1109,39 @@ def sweep_measure(torch, rt, rank=0, world=1):
     def time_point(n, k, rows):
         if (n, k) not in weights:
             weights.clear()
-            weights[(n, k)] = rt.pack(q8_0_blocks(np.random.default_rng(n + k), n, k), n, k)
-        w = weights[(n, k)]
+            torch.cuda.empty_cache()
+            w0 = rt.pack(q8_0_blocks(np.random.default_rng(n + k), n, k), n, k)
+            nbytes = w0.data.numel()
+            copies = [w0] + [dataclasses.replace(w0, data=w0.data.clone())
+                             for _ in range(min(255, -(-(256 << 20) // nbytes) - 1))]
+            weights[(n, k)] = copies
+        ws = weights[(n, k)]
         x = torch.randn(rows, k, device=rt.device)
         y = torch.empty(rows, n, device=rt.device)
-        rt.linear(x, w, out=y)
+        rt.linear(x, ws[0], out=y)  # workspace sized outside the capture
         torch.cuda.synchronize()
-        reps = 10
+        reps = max(10, len(ws)) if rows <= 1024 else 4
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(rt.device)
+        side.wait_stream(torch.cuda.current_stream(rt.device))
+        with torch.cuda.stream(side):
+            g.capture_begin()
+            for i in range(reps):
+                rt.linear(x, ws[i % len(ws)], out=y)
+            g.capture_end()
+        torch.cuda.current_stream(rt.device).wait_stream(side)
+        g.replay()
+        torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(reps):
-            rt.linear(x, w, out=y)
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) / reps / 1e3
+        best = float('inf')
+        for _ in range(3):
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            best = min(best, a.elapsed_time(b) / reps / 1e3)
+        del g
+        return best
 
     return sweep_local(rank, world, time_point)
 
