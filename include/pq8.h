@@ -393,8 +393,9 @@ PQ8_API int pq8_conv_depthwise_bn_silu(const float* x, const uint16_t* w9_f16, c
  * pos_bias_u / _v: float[1024] (head-major); ctx: float[windows * t][1024],
  * heads merged. Scores ((q + u) k + (q + v) p_{t-1+j-i}) / sqrt(128), softmax
  * over keys, context = probabilities x V. By default one fused kernel does
- * everything on chip (tensor-core products with FP16 operands, which keep
- * TF32's 11-bit significand, FP32 accumulation, online softmax); with
+ * everything on chip (tcgen05 products with FP16 operands, which keep TF32's
+ * 11-bit significand, FP32 accumulation in tensor memory, online softmax;
+ * a CTA per window, head and 128 queries); with
  * PQ8_FLAG_FP32_PRODUCTS the three products are FP32 cuBLAS GEMMs around pq8
  * bias / shift / softmax kernels (an exactness reference, slower).
  * PQ8_FLAG_OUT_TF32 rounds ctx for linear_out. Replaces query_bias, rel_scores, softmax and the attention

@@ -1474,7 +1474,7 @@ extern "C" int pq8_rel_attention(const float* qkv, const float* pos, const float
   int rc = device_state(&ds);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (!(flags & PQ8_FLAG_FP32_PRODUCTS) && std::getenv("PQ8_ATTN_TC") != nullptr) {
+  if (!(flags & PQ8_FLAG_FP32_PRODUCTS)) {
     // Fused tensor-core kernel (tcgen05, accumulators in tensor memory).
     {
       std::lock_guard<std::mutex> lock(g_mutex);
@@ -1485,26 +1485,9 @@ extern "C" int pq8_rel_attention(const float* qkv, const float* pos, const float
         ds->attr_set[13] = true;
       }
     }
-    const dim3 grid((t + kTcQ - 1) / kTcQ, 8, windows);
+    const dim3 grid((t + kTcQ - 1) / kTcQ, 8, windows);  // kTcThreads threads: softmax and producer warps
     cudaError_t e = launch_pdl(rel_attention_tc_kernel, grid, dim3(kTcThreads), kTcSmemBytes, st, qkv, pos,
                                pos_bias_u, pos_bias_v, ctx, t, (flags & PQ8_FLAG_OUT_TF32) ? 1 : 0, ds->status);
-    if (e != cudaSuccess) return to_code(e);
-    return to_code(cudaGetLastError());
-  }
-  if (!(flags & PQ8_FLAG_FP32_PRODUCTS)) {
-    // Fused kernel on mma.sync: scores and probabilities stay on chip.
-    {
-      std::lock_guard<std::mutex> lock(g_mutex);
-      if (!ds->attr_set[12]) {
-        cudaError_t e = cudaFuncSetAttribute(rel_attention_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kAttSmemBytes));
-        if (e != cudaSuccess) return to_code(e);
-        ds->attr_set[12] = true;
-      }
-    }
-    const dim3 grid((t + kAttQ - 1) / kAttQ, 8, windows);
-    cudaError_t e = launch_pdl(rel_attention_fused_kernel, grid, dim3(128), kAttSmemBytes, st, qkv, pos, pos_bias_u,
-                               pos_bias_v, ctx, t, (flags & PQ8_FLAG_OUT_TF32) ? 1 : 0);
     if (e != cudaSuccess) return to_code(e);
     return to_code(cudaGetLastError());
   }

@@ -1,8 +1,9 @@
 // The FastConformer block around the Q8_0 linears (parakeet_cuda/reference.py:33-66):
 // LayerNorm, the conv module's depthwise convolution with BatchNorm and SiLU,
-// the relative-position attention (fused; with FP32 products the three
-// batched products go to cuBLAS around the bias / shift-softmax kernels), and
-// the subsampling stem. The linears are pq8_gemm.
+// the relative-position attention with FP32 products (the three batched
+// products on cuBLAS around the bias / shift-softmax kernels; the fused
+// tensor-core attention is pq8_attention.cuh), and the subsampling stem. The
+// linears are pq8_gemm.
 //
 // LayerNorm, the depthwise convolution and the stem's stages are HBM-bound:
 // each reads its input once and writes its output once, coalesced across
@@ -210,228 +211,6 @@ __global__ void rel_shift_softmax_kernel(float* __restrict__ ac, const float* __
     for (int j = lane; j < t; j += 32) sum += expf((s[j] + p[j]) * scale - m);
     const float inv = 1.0f / warp_sum(sum);
     for (int j = lane; j < t; j += 32) s[j] = expf((s[j] + p[j]) * scale - m) * inv;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Fused relative-position attention, flash style: one CTA per (window, head,
-// 64 queries), 4 warps of 16 queries. Per tile of 64 keys a warp computes
-//   positional scores  Qv . P_band^T  (16 x 80 positions: the diagonals its
-//                       queries need, P_band = positional rows t-1+j-i),
-//   content scores     Qu . K^T       (16 x 64),
-// adds the positional scores along the shift through a per-warp scratch,
-// scales by 1/sqrt(128), updates an online softmax and accumulates
-//   context          P . V            (16 x 128)
-// on the tensor cores with mma.sync m16n8k16 (FP16 operands, the 11-bit
-// significand TF32 keeps; FP32 accumulation). Q, K, V and the positional
-// projection are read from their FP32 buffers and converted when staged, so
-// no score or probability touches HBM.
-constexpr int kAttQ = 64, kAttK = 64, kAttD = 128;
-constexpr int kAttBand = 128;             // positional rows of one (query tile, key tile): 2 * 64 - 1, padded
-constexpr int kAttLd = kAttD + 8;         // fp16 row stride of K, V and the band (16-byte pad)
-constexpr int kAttWarpBand = 80;          // band columns one warp needs (16 queries x 64 keys)
-constexpr int kAttScratchLd = kAttWarpBand + 4;
-constexpr size_t kAttSmemBytes = sizeof(__half) * (2 * kAttK * kAttLd + kAttBand * kAttLd) +
-                                 sizeof(float) * 4 * 16 * kAttScratchLd;
-
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  const __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// B fragment (16 x 8, k = rows of a row-major [k][n] shared-memory tile) via
-// ldmatrix with transpose: lanes 0-15 give the addresses of rows k0 .. k0+15
-// at column n0 (16-byte aligned); lane l receives M[k0+2(l%4)+{0,1}][n0+l/4]
-// and M[k0+8+2(l%4)+{0,1}][n0+l/4].
-__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& b0, uint32_t& b1, const __half* row_addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
-               : "=r"(b0), "=r"(b1)
-               : "r"(smem_addr(row_addr)));
-}
-
-__global__ void __launch_bounds__(128)
-    rel_attention_fused_kernel(const float* __restrict__ qkv, const float* __restrict__ pos,
-                               const float* __restrict__ pos_bias_u, const float* __restrict__ pos_bias_v,
-                               float* __restrict__ ctx, int t, int round_out) {
-  griddep_launch();
-  extern __shared__ __align__(16) unsigned char att_smem[];
-  __half* k_s = reinterpret_cast<__half*>(att_smem);               // [64 keys][136]
-  __half* v_s = k_s + kAttK * kAttLd;                               // [64 keys][136]
-  __half* band_s = v_s + kAttK * kAttLd;                            // [128 band rows][136]
-  float* scratch = reinterpret_cast<float*>(band_s + kAttBand * kAttLd);  // [4 warps][16][84]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
-  const int i0 = blockIdx.x * kAttQ, h = blockIdx.y, win = blockIdx.z;
-  const size_t row_base = static_cast<size_t>(win) * t;
-  float* my_scratch = scratch + warp * 16 * kAttScratchLd;
-  const int q0w = 48 - 16 * warp;  // first band column this warp needs
-  griddep_wait();  // qkv and pos come from the previous kernels
-
-  // Query fragments (rows 16 warp + g, + 8) with each positional bias, 8 k-steps of 16.
-  uint32_t qu[8][4], qv[8][4];
-  {
-    const int ra = min(i0 + 16 * warp + g, t - 1), rb = min(i0 + 16 * warp + g + 8, t - 1);
-    const float* qa = qkv + (row_base + ra) * 3072 + h * kAttD;
-    const float* qb = qkv + (row_base + rb) * 3072 + h * kAttD;
-    const float* u = pos_bias_u + h * kAttD;
-    const float* v = pos_bias_v + h * kAttD;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int d = ks * 16 + 2 * q + 8 * half;
-        const float2 xa = *reinterpret_cast<const float2*>(qa + d), xb = *reinterpret_cast<const float2*>(qb + d);
-        const float2 bu = *reinterpret_cast<const float2*>(u + d), bv = *reinterpret_cast<const float2*>(v + d);
-        qu[ks][2 * half] = pack_half2(xa.x + bu.x, xa.y + bu.y);
-        qu[ks][2 * half + 1] = pack_half2(xb.x + bu.x, xb.y + bu.y);
-        qv[ks][2 * half] = pack_half2(xa.x + bv.x, xa.y + bv.y);
-        qv[ks][2 * half + 1] = pack_half2(xb.x + bv.x, xb.y + bv.y);
-      }
-    }
-  }
-  float o[16][4];
-#pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-  float m_row[2] = {-INFINITY, -INFINITY}, l_row[2] = {0.0f, 0.0f};
-  const float kScaleLog2 = 1.4426950408889634f * rsqrtf(128.0f);  // 1/sqrt(128) in base 2
-
-  for (int j0 = 0; j0 < t; j0 += kAttK) {
-    // The positional band is a ring of 128 rows: band row b of this tile is in
-    // slot (ring + b) % 128, and the first 64 rows of a tile are the last 64 of
-    // the tile before, so after the first tile only 64 rows are loaded.
-    const int ring = j0 & (kAttBand - 1);
-    __syncthreads();  // the previous tile's operands are no longer read
-    // Stage K, V [key][d] and the positional band [row][d] as FP16.
-    for (int idx = tid; idx < kAttK * (kAttD / 4); idx += 128) {
-      const int key = idx >> 5, d = (idx & 31) * 4, j = j0 + key;
-      float4 kv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vv = kv;
-      if (j < t) {
-        const float* r = qkv + (row_base + j) * 3072 + h * kAttD + d;
-        kv = *reinterpret_cast<const float4*>(r + 1024);
-        vv = *reinterpret_cast<const float4*>(r + 2048);
-      }
-      *reinterpret_cast<uint2*>(k_s + key * kAttLd + d) = make_uint2(pack_half2(kv.x, kv.y), pack_half2(kv.z, kv.w));
-      *reinterpret_cast<uint2*>(v_s + key * kAttLd + d) = make_uint2(pack_half2(vv.x, vv.y), pack_half2(vv.z, vv.w));
-    }
-    const int pb = t - 64 + j0 - i0;  // position of band row 0 (query i0 + 63, key j0)
-    const int first_row = j0 == 0 ? 0 : kAttBand - kAttK;  // rows not already in the ring
-    for (int idx = tid + first_row * (kAttD / 4); idx < kAttBand * (kAttD / 4); idx += 128) {
-      const int r = idx >> 5, d = (idx & 31) * 4, p = pb + r;
-      float4 pv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (p >= 0 && p < 2 * t - 1) pv = *reinterpret_cast<const float4*>(pos + static_cast<size_t>(p) * 1024 + h * kAttD + d);
-      *reinterpret_cast<uint2*>(band_s + ((ring + r) & (kAttBand - 1)) * kAttLd + d) =
-          make_uint2(pack_half2(pv.x, pv.y), pack_half2(pv.z, pv.w));
-    }
-    __syncthreads();
-
-    // Positional scores of this warp's 16 queries over its 80 band columns, to the scratch.
-    {
-      float bd[10][4];
-#pragma unroll
-      for (int n = 0; n < 10; ++n) bd[n][0] = bd[n][1] = bd[n][2] = bd[n][3] = 0.0f;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-#pragma unroll
-        for (int n = 0; n < 10; ++n) {
-          const __half* br = band_s + ((ring + q0w + 8 * n + g) & (kAttBand - 1)) * kAttLd + ks * 16 + 2 * q;
-          mma_16816(bd[n], qv[ks], *reinterpret_cast<const uint32_t*>(br), *reinterpret_cast<const uint32_t*>(br + 8));
-        }
-#pragma unroll
-      for (int n = 0; n < 10; ++n) {
-        *reinterpret_cast<float2*>(my_scratch + g * kAttScratchLd + 8 * n + 2 * q) = make_float2(bd[n][0], bd[n][1]);
-        *reinterpret_cast<float2*>(my_scratch + (g + 8) * kAttScratchLd + 8 * n + 2 * q) =
-            make_float2(bd[n][2], bd[n][3]);
-      }
-      __syncwarp();
-    }
-    // Content scores, plus the positional score on the shifted diagonal: for
-    // query row r (0..15 in the warp) and key column c, band column c - r + 15.
-    float sc[8][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks)
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        const __half* kr = k_s + (8 * n + g) * kAttLd + ks * 16 + 2 * q;
-        mma_16816(sc[n], qu[ks], *reinterpret_cast<const uint32_t*>(kr), *reinterpret_cast<const uint32_t*>(kr + 8));
-      }
-    float tile_max[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = g + 8 * (e >> 1), c = 8 * n + 2 * q + (e & 1);
-        const float z = (sc[n][e] + my_scratch[r * kAttScratchLd + c - r + 15]) * kScaleLog2;
-        sc[n][e] = (j0 + c < t) ? z : -INFINITY;
-        tile_max[e >> 1] = fmaxf(tile_max[e >> 1], sc[n][e]);
-      }
-    float alpha[2];
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      tile_max[rr] = fmaxf(tile_max[rr], __shfl_xor_sync(0xffffffffu, tile_max[rr], 1));
-      tile_max[rr] = fmaxf(tile_max[rr], __shfl_xor_sync(0xffffffffu, tile_max[rr], 2));
-      const float m_new = fmaxf(m_row[rr], tile_max[rr]);
-      alpha[rr] = exp2f(m_row[rr] - m_new);  // 0 on the first tile (m_row = -inf)
-      m_row[rr] = m_new;
-      l_row[rr] *= alpha[rr];
-    }
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] *= alpha[0];
-      o[n][1] *= alpha[0];
-      o[n][2] *= alpha[1];
-      o[n][3] *= alpha[1];
-    }
-    // Probabilities (unnormalised) as the A operand of the context product.
-    uint32_t pa[4][4];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const float p0 = exp2f(sc[n][0] - m_row[0]), p1 = exp2f(sc[n][1] - m_row[0]);
-      const float p2 = exp2f(sc[n][2] - m_row[1]), p3 = exp2f(sc[n][3] - m_row[1]);
-      l_row[0] += p0 + p1;
-      l_row[1] += p2 + p3;
-      pa[n >> 1][(n & 1) * 2] = pack_half2(p0, p1);
-      pa[n >> 1][(n & 1) * 2 + 1] = pack_half2(p2, p3);
-    }
-    const int lrow = lane & 15;  // ldmatrix row address of this lane (lanes 16-31: ignored, kept valid)
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        uint32_t b0, b1;
-        ldmatrix_x2_trans(b0, b1, v_s + (kk * 16 + lrow) * kAttLd + 8 * n);
-        mma_16816(o[n], pa[kk], b0, b1);
-      }
-    __syncwarp();  // the scratch is rewritten by the next tile
-  }
-  // Row sums across the 4 lanes of a row, normalise, write heads merged.
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    l_row[rr] += __shfl_xor_sync(0xffffffffu, l_row[rr], 1);
-    l_row[rr] += __shfl_xor_sync(0xffffffffu, l_row[rr], 2);
-  }
-  const float inv[2] = {1.0f / l_row[0], 1.0f / l_row[1]};
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const int i = i0 + 16 * warp + g + 8 * rr;
-    if (i >= t) continue;
-    float* out = ctx + (row_base + i) * 1024 + h * kAttD;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      float a = o[n][2 * rr] * inv[rr], b = o[n][2 * rr + 1] * inv[rr];
-      if (round_out) {
-        a = tf32_round(a);
-        b = tf32_round(b);
-      }
-      *reinterpret_cast<float2*>(out + 8 * n + 2 * q) = make_float2(a, b);
-    }
   }
 }
 
