@@ -995,7 +995,7 @@ def block_measure(torch, rt, args, linear_ms):
             'encoder_with_stem_frames_per_s': frames / (ms + stem_ms) * 1e3,
             'tflops_algorithmic': blocks.flops_per_step() / ms / 1e9,
             'linear_stack_ms_per_step': linear_ms,
-            'attention': 'fused pq8 kernel (mma.sync FP16 operands, FP32 accumulation, online softmax)',
+            'attention': 'fused pq8 kernel on tcgen05 (FP16 operands, FP32 accumulation in tensor memory, online softmax)',
             'note': 'linear_pos once per layer on the 2T-1 positional rows, shared by all windows'}
 
 
