@@ -1384,8 +1384,9 @@ extern "C" int pq8_layer_norm(const float* x, const float* w, const float* b, fl
   if (rc) return rc;
   const int round_out = (flags & PQ8_FLAG_OUT_TF32) ? 1 : 0;
   constexpr int kRowsPerCta = 8;  // warps per CTA, one row at a time each
-  // enough warps for two rows each at most (the weight and bias are loaded once per warp)
-  const dim3 grid(static_cast<unsigned>(std::min<long long>((rows + 2 * kRowsPerCta - 1) / (2 * kRowsPerCta),
+  // a warp per row up to 64 warps per SM (all of them resident at once), so
+  // a LayerNorm of up to ~9,000 rows costs one memory round trip per row
+  const dim3 grid(static_cast<unsigned>(std::min<long long>((rows + kRowsPerCta - 1) / kRowsPerCta,
                                                             8LL * ds->sms)));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void (*const kernels[8])(const float*, const float*, const float*, float*, int, int) = {
