@@ -865,6 +865,35 @@ def gemv_measure(torch, rt, stack):
     out['stack']['launches'] = stack.launches_per_step
     out['single']['shape'] = [big_n, big_k]
     del g, big
+    # the same 216 products as one pq8_gemv_batch launch
+    from parakeet_cuda_b200.pq8 import GemvBatchTask
+    ys = []
+    tasks = []
+    for layer in stack.weights:
+        for name, w in layer.items():
+            glu = name == 'pw1_glu'
+            yt = torch.empty(1, w.n // 2 if glu else w.n, device=rt.device)
+            ys.append(yt)
+            tasks.append(GemvBatchTask(w.pointer, x[w.k].data_ptr(), yt.data_ptr(), None, None, w.n, w.k,
+                                       3 if glu else 0, 1.0))
+    plan_bytes, ws_bytes = rt.lib.gemv_batch_sizes(tasks)
+    plan = torch.empty(plan_bytes, dtype=torch.uint8, device=rt.device)
+    bws = torch.empty(ws_bytes, dtype=torch.uint8, device=rt.device)
+    ctas = rt.lib.gemv_batch_plan(tasks, plan.data_ptr(), plan_bytes, bws.data_ptr(), ws_bytes, rt.stream())
+    run = lambda: rt.lib.call('pq8_gemv_batch_run', plan.data_ptr(), ctas, rt.stream())
+    run()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        run()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    gbs = stack.weight_bytes / (ms / 1e3) / 1e9
+    out['stack_batch'] = {'bytes': stack.weight_bytes, 'ms': ms, 'achieved_gbs': gbs, 'frac': gbs / peaks['hbm_gbs'],
+                          'launches': 1, 'ctas': ctas,
+                          'api': 'pq8_gemv_batch_plan / pq8_gemv_batch_run: the 216 products in one launch'}
     return out
 
 

@@ -253,6 +253,39 @@ PQ8_API int pq8_tdt_advance(const int* ids, const int* durations, int n_duration
                             int emitted_capacity, int* trace, int trace_capacity, int* remaining, float* h,
                             float* c, const float* h_new, const float* c_new, int layers, int hidden, void* stream);
 
+/* One M = 1 product of a GEMV batch: y[0:n'] = epilogue(W x + bias) with W
+ * packed [n, k] (GLU-packed for PQ8_EPI_GLU, n' = n / 2; else ROWS, n' = n),
+ * x float[k] (16-byte aligned), y float[n'], bias float[n] or NULL, resid
+ * float[n'] for PQ8_EPI_RESIDUAL (y = resid + alpha z). */
+typedef struct pq8_gemv_task {
+  const void* w;
+  const float* x;
+  float* y;
+  const float* bias;
+  const float* resid;
+  int n, k, epilogue;
+  float alpha;
+} pq8_gemv_task;
+
+/* Bytes of the plan and of the workspace pq8_gemv_batch_plan needs for these tasks. */
+PQ8_API int pq8_gemv_batch_sizes(const pq8_gemv_task* tasks, int count, size_t* plan_bytes,
+                                 size_t* workspace_bytes);
+/* Many independent M = 1 GEMVs as one launch: the reference runs its M = 1
+ * products one q8_gemv launch at a time (runtime.cu:180-188); for matrices of
+ * a few MB each, one launch per matrix is bound by launch and ramp-up latency,
+ * while here every task's 128-row tiles stream side by side in one grid
+ * (each CTA streams up to 32 K blocks of one tile; longer K ranges are split
+ * and reduced in split order through the workspace, deterministically).
+ * Writes the task table into `plan` (device memory, 16-byte aligned) and
+ * zeroes the workspace (device memory, 256-byte aligned; tied to the plan);
+ * *ctas receives the grid size for pq8_gemv_batch_run. Synchronises the
+ * stream. The tasks' buffers must stay valid while the plan is used. */
+PQ8_API int pq8_gemv_batch_plan(const pq8_gemv_task* tasks, int count, void* plan, size_t plan_bytes,
+                                void* workspace, size_t workspace_bytes, int* ctas, void* stream);
+/* Runs a planned batch (capturable in a CUDA graph; the workspace counters
+ * reset themselves, so replays need no re-initialisation). */
+PQ8_API int pq8_gemv_batch_run(const void* plan, int ctas, void* stream);
+
 /* Weights of the TDT prediction and joint networks for pq8_tdt_decode, all
  * resident on the device (H = hidden, J = joint width, E = embedding width):
  *   lstm[l]       GATES4-packed [4H, in_l + H] = [W_ih | W_hh], in_0 = E, in_1 = H

@@ -31,7 +31,11 @@ struct DeviceState {
   bool ready = false;
   int sms = 0;
   int* status = nullptr;
-  bool attr_set[16] = {};
+  // cudaFuncSetAttribute done, per kernel: slots 0-6 the GEMM tile
+  // configurations (GemmConfig), 8-11 the GEMV (MT = 1, 2, 4, 8), 13 the
+  // attention, 14-15 the streaming GEMV (MT = 1, 2), 16 the GEMM sequence
+  // kernel, 17 the GEMV batch kernel
+  bool attr_set[24] = {};
   cublasHandle_t blas = nullptr;  // attention GEMMs; created on first use, guarded by blas_mutex
   std::mutex blas_mutex;
 };
@@ -619,7 +623,7 @@ namespace {
 
 constexpr int kSeqBN = 192, kSeqStages = 5, kSeqSlots = 4, kSeqAcc = 2, kSeqWStages = 8;
 using SeqCfg = GemmCfg<kSeqBN, kSeqStages, kSeqSlots, kSeqAcc, false, 2, 4, 32, kSeqWStages>;
-constexpr int kSeqCfgId = 15;  // DeviceState::attr_set slot of the sequence kernel
+constexpr int kSeqCfgId = 16;  // DeviceState::attr_set slot of the sequence kernel
 constexpr size_t kSeqHeaderBytes = sizeof(SeqPlanHeader);
 
 struct SeqLayout {
@@ -1142,6 +1146,143 @@ extern "C" int pq8_tdt_advance(const int* ids, const int* durations, int n_durat
                              durations, n_durations, state, m, enc_stride, tokens, enc_rows, commit_mask, emitted,
                              emitted_capacity, trace, trace_capacity, remaining, h, c, h_new, c_new, layers, hidden,
                              ds->status);
+  if (e != cudaSuccess) return to_code(e);
+  return to_code(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- GEMV batch
+namespace {
+
+constexpr int kBatchKbPerCta = 32;             // K blocks one CTA streams (~139 KB of records)
+constexpr uint32_t kBatchMagic = 0x42385150u;  // "PQ8B"
+static_assert(sizeof(BatchPlanHeader) == 16, "plan header");
+static_assert(sizeof(GemvTask) % 16 == 0, "task table entries stay 16-byte aligned");
+
+struct BatchTaskShape {
+  int n_tiles, kb, splits, kbps;
+  size_t ws_bytes;
+};
+BatchTaskShape batch_task_shape(int n, int k) {
+  BatchTaskShape b{};
+  b.n_tiles = (n + kTileRows - 1) / kTileRows;
+  b.kb = k / 32;
+  b.splits = (b.kb + kBatchKbPerCta - 1) / kBatchKbPerCta;
+  b.kbps = (b.kb + b.splits - 1) / b.splits;
+  b.ws_bytes = round256(sizeof(int) * b.n_tiles) +
+               (b.splits > 1 ? round256(sizeof(float) * (size_t)b.n_tiles * b.splits * kGemvThreads) : 0);
+  return b;
+}
+
+int check_batch_task(const pq8_gemv_task& t) {
+  if (t.w == nullptr || t.x == nullptr || t.y == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (t.n < 1 || t.k <= 0 || t.k % 32) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (t.epilogue < PQ8_EPI_NONE || t.epilogue > PQ8_EPI_RESIDUAL) return PQ8_ERR_INVALID_ARGUMENT;
+  if (t.epilogue == PQ8_EPI_GLU && t.n % 2) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  if (t.epilogue == PQ8_EPI_RESIDUAL && t.resid == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(t.w, 16) || !aligned(t.x, 16)) return PQ8_ERR_MISALIGNED;
+  return PQ8_OK;
+}
+
+}  // namespace
+
+extern "C" int pq8_gemv_batch_sizes(const pq8_gemv_task* tasks, int count, size_t* plan_bytes,
+                                    size_t* workspace_bytes) {
+  if (tasks == nullptr || count < 1 || plan_bytes == nullptr || workspace_bytes == nullptr)
+    return PQ8_ERR_INVALID_ARGUMENT;
+  size_t ws = 0;
+  for (int i = 0; i < count; ++i) {
+    const int rc = check_batch_task(tasks[i]);
+    if (rc) return rc;
+    ws += batch_task_shape(tasks[i].n, tasks[i].k).ws_bytes;
+  }
+  *plan_bytes = sizeof(BatchPlanHeader) + sizeof(GemvTask) * static_cast<size_t>(count);
+  *workspace_bytes = ws;
+  return PQ8_OK;
+}
+
+extern "C" int pq8_gemv_batch_plan(const pq8_gemv_task* tasks, int count, void* plan, size_t plan_bytes,
+                                   void* workspace, size_t workspace_bytes, int* ctas, void* stream) {
+  size_t need_plan = 0, need_ws = 0;
+  int rc = pq8_gemv_batch_sizes(tasks, count, &need_plan, &need_ws);
+  if (rc) return rc;
+  if (plan == nullptr || ctas == nullptr || workspace == nullptr) return PQ8_ERR_INVALID_ARGUMENT;
+  if (plan_bytes < need_plan || workspace_bytes < need_ws) return PQ8_ERR_WORKSPACE;
+  if (!aligned(plan, 16) || !aligned(workspace, 256)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  if ((rc = device_state(&ds))) return rc;
+  std::vector<unsigned char> blob(need_plan, 0);
+  BatchPlanHeader* hdr = reinterpret_cast<BatchPlanHeader*>(blob.data());
+  GemvTask* table = reinterpret_cast<GemvTask*>(blob.data() + sizeof(BatchPlanHeader));
+  auto* base = static_cast<unsigned char*>(workspace);
+  size_t off = 0;
+  long long total = 0;
+  for (int i = 0; i < count; ++i) {
+    const pq8_gemv_task& t = tasks[i];
+    const BatchTaskShape b = batch_task_shape(t.n, t.k);
+    GemvParams& p = table[i].p;
+    p.w = static_cast<const uint8_t*>(t.w);
+    p.x0 = t.x;
+    p.x_mode = kXPlain;
+    p.x_vec4 = 1;
+    p.y = t.y;
+    p.bias = t.bias;
+    p.resid = t.resid;
+    p.alpha = t.alpha;
+    p.epi = t.epilogue;
+    p.m = 1;
+    p.n = t.n;
+    p.k = t.k;
+    p.layout = t.epilogue == PQ8_EPI_GLU ? PQ8_LAYOUT_GLU : PQ8_LAYOUT_ROWS;
+    p.out_cols = t.epilogue == PQ8_EPI_GLU ? t.n / 2 : t.n;
+    p.n_tiles = b.n_tiles;
+    p.k_blocks = b.kb;
+    p.splits = b.splits;
+    p.kb_per_split = b.kbps;
+    p.cluster_reduce = 0;
+    p.tickets = reinterpret_cast<int*>(base + off);
+    p.partial = reinterpret_cast<float*>(base + off + round256(sizeof(int) * b.n_tiles));
+    p.mode = kGemvLinear;
+    p.status = ds->status;
+    off += b.ws_bytes;
+    table[i].cta0 = static_cast<int>(total);
+    total += static_cast<long long>(b.n_tiles) * b.splits;
+  }
+  if (total > (1ll << 30)) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  hdr->magic = kBatchMagic;
+  hdr->count = count;
+  hdr->ctas = static_cast<int>(total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, need_ws, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(plan, blob.data(), need_plan, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return to_code(e);
+  *ctas = static_cast<int>(total);
+  return PQ8_OK;
+}
+
+extern "C" int pq8_gemv_batch_run(const void* plan, int ctas, void* stream) {
+  if (plan == nullptr || ctas < 1) return PQ8_ERR_INVALID_ARGUMENT;
+  if (!aligned(plan, 16)) return PQ8_ERR_MISALIGNED;
+  DeviceState* ds;
+  int rc = device_state(&ds);
+  if (rc) return rc;
+  // the task count is read by the kernel from the plan's header, not by the
+  // host (so the launch stays capturable)
+  const size_t smem = ((sizeof(float) * kBatchKbPerCta * 32 + 127) & ~size_t(127)) + kStreamRingBytes;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!ds->attr_set[17]) {
+      cudaError_t e = cudaFuncSetAttribute(gemv_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return to_code(e);
+      ds->attr_set[17] = true;
+    }
+  }
+  const unsigned char* p = static_cast<const unsigned char*>(plan);
+  cudaError_t e = launch_pdl(gemv_batch_kernel, dim3(static_cast<unsigned>(ctas)), dim3(kStreamThreads), smem,
+                             static_cast<cudaStream_t>(stream),
+                             reinterpret_cast<const GemvTask*>(p + sizeof(BatchPlanHeader)),
+                             reinterpret_cast<const BatchPlanHeader*>(p));
   if (e != cudaSuccess) return to_code(e);
   return to_code(cudaGetLastError());
 }

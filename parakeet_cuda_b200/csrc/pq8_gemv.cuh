@@ -239,8 +239,7 @@ __device__ __forceinline__ void compute_sync() {
 // row's bytes itself, U K blocks ahead (small launches where latency matters
 // more than bytes in flight).
 template <int MT, bool STREAM>
-__global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM ? 2 : kGemvCtasPerSm)
-    gemv_kernel(const GemvParams p) {
+__device__ __forceinline__ void gemv_cta(const GemvParams& p, const int bx, const int by) {
   static_assert(MT * 2 * 8 <= kGemvThreads, "the joint tail gives 8 threads to each (row, part) pair");
   extern __shared__ __align__(128) float xs[];
   __shared__ float gate_s[MT][4][32];
@@ -251,12 +250,12 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
   __shared__ int abort_s;
   __shared__ float comb[STREAM ? MT : 1][kGemvThreads];  // second group's sums
 
-  const int t = blockIdx.x / p.splits, split = blockIdx.x % p.splits;
+  const int t = bx / p.splits, split = bx % p.splits;
   const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
   // Row group: activation rows [row0, row0 + mg) of the launch's p.m rows.
-  const int row0 = blockIdx.y * MT;
+  const int row0 = by * MT;
   const int mg = min(MT, p.m - row0);
-  const size_t grp_sel = blockIdx.y;
+  const size_t grp_sel = by;
   float* const partial = p.partial + grp_sel * ((size_t)p.n_tiles * p.splits * kGemvThreads * MT);
   int* const tickets = p.tickets + grp_sel * p.n_tiles;
   int* const done_count = p.done_count + grp_sel;
@@ -277,7 +276,7 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
   // Cluster split-K stores into the leader's shared memory only once every
   // CTA of the cluster is known to have started (first barrier phase).
   if (!STREAM && p.cluster_reduce) cluster_arrive_relaxed();
-  if (r == 0 && blockIdx.x == 0 && blockIdx.y == 0) {
+  if (r == 0 && bx == 0 && by == 0) {
     const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
     if (!(h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout && h->n_tiles == p.n_tiles))
       atomicCAS(p.status, 0, PQ8_ERR_LAYOUT);
@@ -618,6 +617,48 @@ __global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM
     }
   }
   if (r == 0) *done_count = 0;
+}
+
+template <int MT, bool STREAM>
+__global__ void __launch_bounds__(STREAM ? kStreamThreads : kGemvThreads, STREAM ? 2 : kGemvCtasPerSm)
+    gemv_kernel(const GemvParams p) {
+  gemv_cta<MT, STREAM>(p, static_cast<int>(blockIdx.x), static_cast<int>(blockIdx.y));
+}
+
+// Many independent M = 1 products in one launch (pq8_gemv_batch_run): task i
+// owns CTAs [cta0, cta0 + ctas) of the grid, and each CTA runs the streaming
+// GEMV of its task as if it were CTA blockIdx.x - cta0 of that task's own
+// launch. One launch keeps HBM streaming across matrices of a few MB each,
+// which as separate launches are bound by launch and ramp-up latency.
+struct GemvTask {
+  GemvParams p;
+  int cta0;
+  int pad[3];
+};
+
+// Header of a batch plan (the task table follows it).
+struct BatchPlanHeader {
+  uint32_t magic;
+  int count, ctas, pad;
+};
+
+__global__ void __launch_bounds__(kStreamThreads, 2)
+    gemv_batch_kernel(const GemvTask* tasks, const BatchPlanHeader* hdr) {
+  __shared__ GemvParams ps;
+  __shared__ int bx_s;
+  if (threadIdx.x == 0) {
+    const int count = hdr->count;
+    int lo = 0, hi = count - 1;  // last task with cta0 <= blockIdx.x
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tasks[mid].cta0 <= static_cast<int>(blockIdx.x)) lo = mid;
+      else hi = mid - 1;
+    }
+    ps = tasks[lo].p;
+    bx_s = static_cast<int>(blockIdx.x) - tasks[lo].cta0;
+  }
+  __syncthreads();
+  gemv_cta<1, true>(ps, bx_s, 0);
 }
 
 // TDT commit: rows whose mask is set take the candidate LSTM state

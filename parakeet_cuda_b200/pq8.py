@@ -47,6 +47,12 @@ class GemmTask(C.Structure):
                 ('epilogue', _I), ('alpha', _F), ('flags', _I), ('after', _I), ('after_window', _I)]
 
 
+class GemvBatchTask(C.Structure):
+    """``pq8_gemv_task``: one M = 1 product of a GEMV batch (``pq8_gemv_batch_plan``)."""
+    _fields_ = [('w', _P), ('x', _P), ('y', _P), ('bias', _P), ('resid', _P), ('n', _I), ('k', _I),
+                ('epilogue', _I), ('alpha', _F)]
+
+
 class TdtWeights(C.Structure):
     """``pq8_tdt_weights``: the prediction and joint networks for ``pq8_tdt_decode``."""
     _fields_ = [('lstm', _P * 2), ('lstm_bias', _P * 2), ('pred', _P), ('pred_bias', _P), ('joint', _P),
@@ -86,6 +92,9 @@ SIGNATURES = {
     'pq8_sequence_plan_size': ([C.POINTER(GemmTask), _I, C.POINTER(_SZ)], _I),
     'pq8_sequence_plan': ([C.POINTER(GemmTask), _I, _P, _SZ, _P], _I),
     'pq8_sequence_run': ([_P, _P], _I),
+    'pq8_gemv_batch_sizes': ([C.POINTER(GemvBatchTask), _I, C.POINTER(_SZ), C.POINTER(_SZ)], _I),
+    'pq8_gemv_batch_plan': ([C.POINTER(GemvBatchTask), _I, _P, _SZ, _P, _SZ, C.POINTER(_I), _P], _I),
+    'pq8_gemv_batch_run': ([_P, _I, _P], _I),
     'pq8_tdt_decode_workspace_size': ([_I, _I, _I, C.POINTER(_SZ)], _I),
     'pq8_tdt_decode': ([C.POINTER(TdtWeights), _P, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _I, _P, _P, _P, _SZ,
                         _P], _I),
@@ -134,6 +143,21 @@ class Library:
         out = _SZ()
         self.call('pq8_gemv_workspace_size', m, n, k, C.byref(out))
         return out.value
+
+    def gemv_batch_sizes(self, tasks) -> tuple[int, int]:
+        """(plan bytes, workspace bytes) for a list of ``GemvBatchTask``."""
+        arr = (GemvBatchTask * len(tasks))(*tasks)
+        plan, ws = _SZ(), _SZ()
+        self.call('pq8_gemv_batch_sizes', arr, len(tasks), C.byref(plan), C.byref(ws))
+        return plan.value, ws.value
+
+    def gemv_batch_plan(self, tasks, plan, plan_bytes, workspace, workspace_bytes, stream) -> int:
+        """Writes the plan; returns the grid size for ``pq8_gemv_batch_run``."""
+        arr = (GemvBatchTask * len(tasks))(*tasks)
+        ctas = _I()
+        self.call('pq8_gemv_batch_plan', arr, len(tasks), plan, plan_bytes, workspace, workspace_bytes,
+                  C.byref(ctas), stream)
+        return ctas.value
 
     def tdt_decode_workspace_size(self, m: int, hidden: int, joint_k: int) -> int:
         out = _SZ()

@@ -1,5 +1,6 @@
 """GPU parity of the decoder regime: fused LSTM layer, fused joint + arg-max,
 and the greedy TDT loop against the reference's golden token ids."""
+import ctypes as C
 import json
 
 import numpy as np
@@ -308,6 +309,41 @@ def test_tdt_persistent_resume_and_step_limit(rt):
     assert d.steps == 37
     for c, w in zip(cut, whole):
         assert c['decode_trace'] == w['decode_trace'][:37]
+    assert rt.device_status() == 0
+
+
+def test_tdt_persistent_rejects_bad_arguments(rt):
+    """pq8_tdt_decode validates before launching: more than 64 streams, a
+    misaligned frame table, a short workspace."""
+    from parakeet_cuda_b200.pq8 import PQ8Error, TdtWeights
+    model = SyntheticParakeet(seed=12, encoder_layers=0)
+    d = PQ8Decoder(model, rt, batch=1)
+    w = TdtWeights()
+    for l in range(2):
+        w.lstm[l] = d.lstm[l][0].pointer
+        w.lstm_bias[l] = d.lstm[l][1].data_ptr()
+    w.pred, w.pred_bias = d.w_pred.pointer, d.b_pred.data_ptr()
+    w.joint, w.joint_bias = d.w_joint.pointer, d.b_joint.data_ptr()
+    w.embed = d.embed.data_ptr()
+    w.hidden, w.embed_k, w.joint_k, w.n_joint, w.vocab = 640, 640, 640, d.n_out, 8193
+    enc = torch.zeros(65 * 4 + 1, 640, device='cuda')
+    i32 = dict(dtype=torch.int32, device='cuda')
+    state, rec, cnt = torch.zeros(65, 8, **i32), torch.zeros(65, 40, 3, **i32), torch.zeros(2, **i32)
+    dur = torch.tensor(DURATIONS, **i32)
+    ws = torch.empty(rt.lib.tdt_decode_workspace_size(64, 640, 640), dtype=torch.uint8, device='cuda')
+
+    def call(m, enc_ptr, ws_bytes):
+        rt.lib.call('pq8_tdt_decode', C.byref(w), enc_ptr, 4, dur.data_ptr(), 5, state.data_ptr(), m,
+                    rec.data_ptr(), 40, rec.data_ptr(), 40, 10, 0, cnt[0:1].data_ptr(), cnt[1:2].data_ptr(),
+                    ws.data_ptr(), ws_bytes, rt.stream())
+
+    with pytest.raises(PQ8Error, match='UNSUPPORTED_SHAPE'):
+        call(65, enc.data_ptr(), ws.numel())
+    with pytest.raises(PQ8Error, match='MISALIGNED'):
+        call(1, enc.data_ptr() + 4, ws.numel())
+    with pytest.raises(PQ8Error, match='PQ8_ERR_WORKSPACE'):
+        call(64, enc.data_ptr(), ws.numel() - 256)
+    torch.cuda.synchronize()
     assert rt.device_status() == 0
 
 

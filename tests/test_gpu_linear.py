@@ -484,3 +484,48 @@ def test_workspace_shared_across_shapes(rt):
 def test_status_clean_at_end(rt):
     torch.cuda.synchronize()
     assert rt.device_status() == 0
+
+
+def test_gemv_batch_matches_oracle(rt):
+    """pq8_gemv_batch: a mix of M = 1 products (short and long K, GLU, residual,
+    bias, ragged N) in one launch, each against the float64 product; replays
+    of the planned launch give the same bits (the split tickets reset
+    themselves)."""
+    rng = np.random.default_rng(321)
+    shapes = [(1024, 1024, EPI_NONE), (4096, 1024, EPI_SILU), (1024, 4096, EPI_RESIDUAL), (2048, 1024, EPI_GLU),
+              (8198, 640, EPI_NONE), (200, 2080, EPI_RELU), (129, 32, EPI_NONE), (640, 8192, EPI_NONE)]
+    tasks, keep, golds = [], [], []
+    for n, k, epi in shapes:
+        raw = q8_0_blocks(rng, n, k)
+        w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
+        x = rng.normal(size=(1, k)).astype(np.float32)
+        bias = rng.normal(size=n).astype(np.float32)
+        n_out = n // 2 if epi == EPI_GLU else n
+        resid = rng.normal(size=(1, n_out)).astype(np.float32) if epi == EPI_RESIDUAL else None
+        xd, bd = dev(x), dev(bias)
+        rd = dev(resid) if resid is not None else None
+        y = torch.full((1, n_out), float('nan'), device='cuda')
+        tasks.append(pq8.GemvBatchTask(w.pointer, xd.data_ptr(), y.data_ptr(), bd.data_ptr(),
+                                       rd.data_ptr() if rd is not None else None, n, k, epi, 0.5))
+        keep += [w, xd, bd, rd, y]
+        z = q8.gemm(x, raw, n, k) + bias
+        golds.append((y, q8.epilogue(z, epi, None, resid, 0.5), z, epi))
+    plan_bytes, ws_bytes = rt.lib.gemv_batch_sizes(tasks)
+    plan = torch.empty(plan_bytes, dtype=torch.uint8, device='cuda')
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda')
+    ctas = rt.lib.gemv_batch_plan(tasks, plan.data_ptr(), plan_bytes, ws.data_ptr(), ws_bytes, rt.stream())
+    rt.lib.call('pq8_gemv_batch_run', plan.data_ptr(), ctas, rt.stream())
+    torch.cuda.synchronize()
+    assert rt.device_status() == 0
+    first = [g[0].clone() for g in golds]
+    for y, gold, z, epi in golds:
+        got = y.cpu().numpy().astype(np.float64)
+        assert np.isfinite(got).all()
+        scale = max(1.0, float(np.sqrt((z ** 2).mean())))
+        np.testing.assert_allclose(got, gold, atol=2e-4 * scale, rtol=2e-4)
+    for _ in range(3):
+        rt.lib.call('pq8_gemv_batch_run', plan.data_ptr(), ctas, rt.stream())
+    torch.cuda.synchronize()
+    for (y, *_), f in zip(golds, first):
+        assert torch.equal(y, f)
+    assert rt.device_status() == 0
