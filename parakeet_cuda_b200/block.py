@@ -8,10 +8,13 @@ residual stream, entirely on the GPU:
 step                   kernel
 =====================  ===========================================================
 LayerNorm (x5)         ``pq8_layer_norm`` (output TF32-rounded when a GEMM reads it)
-FFN1 / FFN2            ``pq8_gemm`` + SiLU, ``pq8_gemm`` with ``x += 0.5 y``
+FFN1 / FFN2            ``pq8_gemm`` + SiLU, ``pq8_gemm`` with ``x += 0.5 y``: the pair
+                       as one ``pq8_sequence_run`` (down-projection tiles start as
+                       soon as their rows of the hidden state are written)
 Q, K, V                one ``pq8_gemm`` on the packed ``[3072, 1024]`` weight
 linear_pos             one ``pq8_gemm`` on the ``2t - 1`` positional rows, once per
-                       layer for all windows (their positions are identical)
+                       layer for all windows (their positions are identical);
+                       QKV and linear_pos run as one sequence launch
 attention              ``pq8_rel_attention`` (one fused kernel: products, shift, softmax)
 linear_out             ``pq8_gemm`` with ``x += y``
 conv module            ``pq8_gemm`` + GLU, ``pq8_conv_depthwise_bn_silu``,
@@ -29,7 +32,7 @@ import numpy as np
 import torch
 
 from .encoder import D_FF, D_MODEL, EncoderStack, LAYER_PLAN
-from .pq8 import ATTN_FP32, EPI_RESIDUAL, FLAG_OUT_TF32, FLAG_X_TF32
+from .pq8 import ATTN_FP32, EPI_RESIDUAL, FLAG_OUT_TF32, FLAG_X_TF32, GemmTask
 from .runtime import Runtime
 
 LN_NAMES = ('norm_feed_forward1', 'norm_self_att', 'norm_conv', 'norm_feed_forward2', 'norm_out')
@@ -39,7 +42,7 @@ class EncoderBlocks:
     """``layers`` encoder blocks over ``windows`` windows of ``t`` frames on one device."""
 
     def __init__(self, model, runtime: Runtime, windows: int, t: int, layers: int = 24,
-                 attention_fp32: bool = False):
+                 attention_fp32: bool = False, sequences: bool = True):
         self.rt, self.windows, self.t, self.layers = runtime, windows, t, layers
         self.rows = windows * t
         self.attn_flags = FLAG_OUT_TF32 | (ATTN_FP32 if attention_fp32 else 0)
@@ -81,6 +84,24 @@ class EncoderBlocks:
         need = runtime.lib.attention_workspace_size(windows, t)
         self.attn_ws = torch.empty(need, dtype=torch.uint8, device=dev)
         self._plan = {e[0]: e for e in LAYER_PLAN}
+        # linears that follow one another with nothing in between, as sequence
+        # launches (plans bound to the buffers above)
+        self.seq_plans = None
+        if sequences:
+            self.seq_plans = []
+            for l in range(layers):
+                groups = {
+                    'ffn1': [self._task(l, 'ffn1_up', 'norm', 'hidden'), self._task(l, 'ffn1_down', 'hidden', 'x')],
+                    'att_in': [self._task(l, 'qkv', 'norm', 'qkv'), self._task(l, 'pos', self.pe, 'pos')],
+                    'ffn2': [self._task(l, 'ffn2_up', 'norm', 'hidden'), self._task(l, 'ffn2_down', 'hidden', 'x')],
+                }
+                plans = {}
+                for key, tasks in groups.items():
+                    nbytes = runtime.lib.sequence_plan_size(tasks)
+                    plan = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+                    runtime.lib.sequence_plan(tasks, plan.data_ptr(), nbytes, runtime.stream())
+                    plans[key] = plan
+                self.seq_plans.append(plans)
 
     # -- pieces ----------------------------------------------------------------
     def _ln(self, l: int, name: str, src: str, dst: str, tf32: bool = True) -> None:
@@ -88,6 +109,19 @@ class EncoderBlocks:
         x, y = self.buf[src], self.buf[dst]
         self.rt.lib.call('pq8_layer_norm', x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), x.shape[0],
                          x.shape[1], FLAG_OUT_TF32 if tf32 else 0, self.rt.stream())
+
+    def _task(self, l: int, name: str, src, dst: str) -> GemmTask:
+        """The linear as a ``pq8_gemm_task`` on the block's buffers (as ``_gemm`` launches it)."""
+        _, _, n, k, epi, alpha, _, _, flags = self._plan[name]
+        x = self.buf[src] if isinstance(src, str) else src
+        out = self.buf[dst]
+        w = self.linears[l][name]
+        resid = out.data_ptr() if epi == EPI_RESIDUAL else None
+        return GemmTask(w.pointer, x.data_ptr(), out.data_ptr(), None, resid, x.shape[0], w.n, w.k, epi, alpha,
+                        flags | FLAG_X_TF32, -1, 0)
+
+    def _sequence(self, l: int, key: str) -> None:
+        self.rt.lib.call('pq8_sequence_run', self.seq_plans[l][key].data_ptr(), self.rt.stream())
 
     def _gemm(self, l: int, name: str, src, dst: str, out_tf32: bool | None = None) -> None:
         _, _, n, k, epi, alpha, _, _, flags = self._plan[name]
@@ -104,12 +138,19 @@ class EncoderBlocks:
         ``final_norm=False`` leaves out the block's last LayerNorm (``norm_out``)
         and keeps the residual stream as it stands before it."""
         b, p, lib, st = self.buf, self.params[l], self.rt.lib, self.rt.stream()
+        seq = self.seq_plans is not None
         self._ln(l, 'norm_feed_forward1', 'x', 'norm')
-        self._gemm(l, 'ffn1_up', 'norm', 'hidden')
-        self._gemm(l, 'ffn1_down', 'hidden', 'x')
+        if seq:
+            self._sequence(l, 'ffn1')
+        else:
+            self._gemm(l, 'ffn1_up', 'norm', 'hidden')
+            self._gemm(l, 'ffn1_down', 'hidden', 'x')
         self._ln(l, 'norm_self_att', 'x', 'norm')
-        self._gemm(l, 'qkv', 'norm', 'qkv')
-        self._gemm(l, 'pos', self.pe, 'pos')
+        if seq:
+            self._sequence(l, 'att_in')
+        else:
+            self._gemm(l, 'qkv', 'norm', 'qkv')
+            self._gemm(l, 'pos', self.pe, 'pos')
         lib.call('pq8_rel_attention', b['qkv'].data_ptr(), b['pos'].data_ptr(), p['u'].data_ptr(), p['v'].data_ptr(),
                  b['ctx'].data_ptr(), self.windows, self.t, self.attn_flags, self.attn_ws.data_ptr(),
                  self.attn_ws.numel(), st)
@@ -122,8 +163,11 @@ class EncoderBlocks:
                  FLAG_OUT_TF32, st)
         self._gemm(l, 'pw2', 'dw', 'x')
         self._ln(l, 'norm_feed_forward2', 'x', 'norm')
-        self._gemm(l, 'ffn2_up', 'norm', 'hidden')
-        self._gemm(l, 'ffn2_down', 'hidden', 'x')
+        if seq:
+            self._sequence(l, 'ffn2')
+        else:
+            self._gemm(l, 'ffn2_up', 'norm', 'hidden')
+            self._gemm(l, 'ffn2_down', 'hidden', 'x')
         if final_norm:
             self._ln(l, 'norm_out', 'x', 'x', tf32=False)  # the block's output, next block's input
 
