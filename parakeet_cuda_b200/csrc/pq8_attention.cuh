@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int n_tiles = (t + kTcKeys - 1) / kTcKeys;
 
   if (tid == 0) {
-    mbar_init(bar_s, 1);
+    mbar_init(bar_s, 2);  // the S and the positional-band issuers' commits
     mbar_init(bar_pv, 1);
     mbar_init(s_free, 4);
     mbar_init(p_full, 4);
@@ -180,25 +180,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       *reinterpret_cast<uint4*>(plane + sw128(slot * 64 + r, c16 & 7)) = val;
       if (slot < 2) *reinterpret_cast<uint4*>(plane + sw128((3 + slot) * 64 + r, c16 & 7)) = val;
     };
-    auto stage_slab = [&](int sl) {
-      float4 ba[8], bb[8];
+    // slabs 0 and 1 (the first tile's other two come with it): all 32 loads
+    // of a thread in flight at once
+    {
+      float4 ba[2][8], bb[2][8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int item = q * kTcRoleThreads + pt, r = item >> 4, c16 = item & 15;
-        const int pp = p0 + 64 * sl + r;
-        if (pp >= 0 && pp < n_pos) {
-          const float* src = pos + static_cast<size_t>(pp) * 1024 + h * kTcD + c16 * 8;
-          ba[q] = *reinterpret_cast<const float4*>(src);
-          bb[q] = *reinterpret_cast<const float4*>(src + 4);
-        } else {
-          ba[q] = bb[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int sl = 0; sl < 2; ++sl)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int item = q * kTcRoleThreads + pt, r = item >> 4, c16 = item & 15;
+          const int pp = p0 + 64 * sl + r;
+          if (pp >= 0 && pp < n_pos) {
+            const float* src = pos + static_cast<size_t>(pp) * 1024 + h * kTcD + c16 * 8;
+            ba[sl][q] = *reinterpret_cast<const float4*>(src);
+            bb[sl][q] = *reinterpret_cast<const float4*>(src + 4);
+          } else {
+            ba[sl][q] = bb[sl][q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          }
         }
-      }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) store_slab(sl, q * kTcRoleThreads + pt, pack_h8(ba[q], bb[q]));
-    };
-    stage_slab(0);
-    stage_slab(1);
+      for (int sl = 0; sl < 2; ++sl)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) store_slab(sl, q * kTcRoleThreads + pt, pack_h8(ba[sl][q], bb[sl][q]));
+    }
     // MMA issue (thread pt = 0). A wait that runs out stops the issue; the
     // thread keeps meeting the other producers at their named barrier, and
     // all of them leave at the next tile's (bounded) wait, which then fails.
@@ -285,6 +289,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       fence_proxy_async_smem();  // generic-proxy stores, read by the tensor cores
       named_barrier_sync(1, kTcRoleThreads);
+      // Two issuing threads in different warps: pt 0 issues S (and the
+      // context products), pt 32 the positional band, each committing to
+      // bar_s (two arrivals), so the two chains of MMA issues overlap.
+      if (pt == 32 && !failed) {
+        if (k > 0 && !mbar_wait(s_free, (k - 1) & 1, abort_flag, status)) failed = true;
+        if (!failed) {
+          tc_fence_after();
+          constexpr uint32_t id_bd = idesc_f16(128, 192);
+          const uint32_t band = sbase + kTcBandOff + (k % 3) * (64 * 128);  // slots k % 3 .. + 2
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t koff = (kk & 3) * 32;
+            const uint64_t a = smem_desc_sw128(sbase + kTcQvOff + (kk >> 2) * (kTcQ * 128) + koff);
+            const uint64_t b = smem_desc_sw128(band + (kk >> 2) * kTcPlaneBytes + koff);
+            mma_f16_ss(tmem + kTcColBd, a, b, id_bd, kk > 0);
+          }
+          mma_commit(bar_s);
+          ++s_issued;
+        }
+      }
       if (pt == 0 && !failed) {
         if (k > 0 && !mbar_wait(s_free, (k - 1) & 1, abort_flag, status)) failed = true;
         if (!failed) {
@@ -297,15 +321,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint64_t a = smem_desc_sw128(sbase + kTcQuOff + (kk >> 2) * (kTcQ * 128) + koff);
             const uint64_t b = smem_desc_sw128(kb + (kk >> 2) * (64 * 128) + koff);
             mma_f16_ss(tmem + kTcColS, a, b, id_s, kk > 0);
-          }
-          constexpr uint32_t id_bd = idesc_f16(128, 192);
-          const uint32_t band = sbase + kTcBandOff + (k % 3) * (64 * 128);  // slots k % 3 .. + 2
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t koff = (kk & 3) * 32;
-            const uint64_t a = smem_desc_sw128(sbase + kTcQvOff + (kk >> 2) * (kTcQ * 128) + koff);
-            const uint64_t b = smem_desc_sw128(band + (kk >> 2) * kTcPlaneBytes + koff);
-            mma_f16_ss(tmem + kTcColBd, a, b, id_bd, kk > 0);
           }
           mma_commit(bar_s);
           ++s_issued;
@@ -320,6 +335,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     }
+    if (pt == 32 && (failed || k < n_tiles) && s_issued > 0) mbar_drain(bar_s, (s_issued - 1) & 1);
     if (pt == 0) {
       if (!failed && k == n_tiles) {
         if (!mbar_wait(p_full, (n_tiles - 1) & 1, abort_flag, status)) {
