@@ -56,6 +56,34 @@ def test_argument_validation_without_device(lib):
         lib.packed_size(3, 64, pq8.LAYOUT_GLU)
 
 
+def test_batch_and_decode_sizing_without_device(lib):
+    """The GEMV batch and persistent-decode sizing entry points validate and
+    size on the host: per task its tile tickets (and split partials when K is
+    longer than 32 blocks per CTA); the decode workspace scales with streams."""
+    t = lambda n, k, epi=0, resid=None: pq8.GemvBatchTask(16, 16, 16, None, resid, n, k, epi, 1.0)
+    plan, ws = lib.gemv_batch_sizes([t(1024, 1024)])
+    assert ws == 256  # 8 tiles x 4-byte tickets, rounded to 256; one split: no partials
+    _, ws2 = lib.gemv_batch_sizes([t(1024, 4096)])  # 4 splits of 32 K blocks
+    assert ws2 == 256 + 8 * 4 * 128 * 4  # tickets + [8 tiles][4 splits][128 rows] partial sums
+    plan3, ws3 = lib.gemv_batch_sizes([t(1024, 1024), t(1024, 4096)])
+    assert ws3 == ws + ws2
+    assert plan3 - plan == plan - 16  # a 16-byte header and one fixed-size entry per task
+    for bad, code in ((t(1024, 1000), pq8.ERR_UNSUPPORTED_SHAPE), (t(1023, 64, 3), pq8.ERR_UNSUPPORTED_SHAPE),
+                      (t(64, 64, 4), pq8.ERR_INVALID_ARGUMENT), (t(64, 64, 9), pq8.ERR_INVALID_ARGUMENT)):
+        with pytest.raises(pq8.PQ8Error) as e:
+            lib.gemv_batch_sizes([bad])
+        assert e.value.code == code
+    bad_align = pq8.GemvBatchTask(16, 20, 16, None, None, 64, 64, 0, 1.0)
+    with pytest.raises(pq8.PQ8Error) as e:
+        lib.gemv_batch_sizes([bad_align])
+    assert e.value.code == pq8.ERR_MISALIGNED
+    one, many = lib.tdt_decode_workspace_size(1, 640, 640), lib.tdt_decode_workspace_size(64, 640, 640)
+    assert 0 < one < many
+    with pytest.raises(pq8.PQ8Error) as e:
+        lib.tdt_decode_workspace_size(65, 640, 640)
+    assert e.value.code == pq8.ERR_UNSUPPORTED_SHAPE
+
+
 def reference_pack(raw, n, k, layout):
     """Restatement of the packed layout documented in include/pq8.h / pq8_pack.cpp."""
     blocks = np.asarray(raw, np.uint8).reshape(n, k // 32, 34)
