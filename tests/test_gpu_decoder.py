@@ -12,7 +12,8 @@ from parakeet_cuda_b200 import pq8
 from parakeet_cuda_b200.decoder import PQ8Decoder
 from parakeet_cuda_b200.runtime import Runtime, pack_concat_host
 from parakeet_cuda_b200.synthetic import SyntheticParakeet, q8_0_blocks
-from parakeet_cuda_b200.tdt import greedy_decode, greedy_decode_batch, greedy_decode_device, greedy_decode_persistent
+from parakeet_cuda_b200.tdt import (greedy_decode, greedy_decode_batch, greedy_decode_device, greedy_decode_gpu,
+                                     greedy_decode_persistent)
 
 pytestmark = pytest.mark.gpu
 
@@ -309,6 +310,18 @@ def test_tdt_persistent_resume_and_step_limit(rt):
     assert d.steps == 37
     for c, w in zip(cut, whole):
         assert c['decode_trace'] == w['decode_trace'][:37]
+    assert rt.device_status() == 0
+
+
+@pytest.mark.parametrize('batch', [5, 20])
+def test_tdt_gpu_dispatch_matches_oracle(rt, batch):
+    """greedy_decode_gpu takes the persistent launch for few streams and the
+    graph loop for many; both match the oracle call by call."""
+    model = SyntheticParakeet(seed=12, encoder_layers=0, blank_bias=1.0)
+    rng = np.random.default_rng(500 + batch)
+    projected = [rng.normal(size=(int(rng.integers(10, 50)), 640)).astype(np.float32) for _ in range(batch)]
+    got = greedy_decode_gpu(projected, PQ8Decoder(model, rt, batch=batch), DURATIONS)
+    check_streams_vs_oracle(projected, got, model, max_ties=2)
     assert rt.device_status() == 0
 
 
