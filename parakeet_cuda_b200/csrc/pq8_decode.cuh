@@ -35,7 +35,7 @@ namespace pq8 {
 
 constexpr int kDecodeThreads = 256;
 constexpr int kDecodeMaxStreams = 64;
-constexpr int kDecodeGroup = 8;  // streams per matrix-vector pass (activation rows staged at once)
+constexpr int kDecodeGroup = 16;  // streams per matrix-vector pass (activation rows staged at once)
 
 // One Q8_0 matrix slice resident in shared memory: rows [0, rows) of the
 // CTA's share, K blocks [0, kb). Values in two planes ([kb][row][16 B] for K
@@ -146,14 +146,16 @@ __device__ void load_slice(uint8_t* smem, const SmemQ8& s, const uint8_t* w, int
 }
 
 // Activation rows staged for a pass over a slice: the row count rounded up
-// to 1, 2, 4 or 8 (the matrix-vector product's template width).
-__device__ __forceinline__ int group_rows(int mc) { return mc <= 1 ? 1 : mc <= 2 ? 2 : mc <= 4 ? 4 : 8; }
+// to 1, 2, 4, 8 or 16 (the matrix-vector product's template width).
+__device__ __forceinline__ int group_rows(int mc) {
+  return mc <= 1 ? 1 : mc <= 2 ? 2 : mc <= 4 ? 4 : mc <= 8 ? 8 : 16;
+}
 
 // xs[j][k] = load(j, k) (a float4 at k, k % 4 == 0) for rows j < mc and 0
 // for rows mc .. group_rows(mc) - 1. A thread issues all its loads of a
 // chunk (up to kStageUnroll float4s) before it stores any of them, so one
 // staging costs about one memory round trip, not one per element.
-constexpr int kStageUnroll = 10;
+constexpr int kStageUnroll = 10;  // (16 rows x 1280 floats: two chunks of loads)
 template <typename LoadFn>
 __device__ __forceinline__ void stage_rows(float* xs, int K, int mc, LoadFn load) {
   const int k4 = K / 4, n4 = group_rows(mc) * k4;
@@ -215,7 +217,8 @@ __device__ __forceinline__ void slice_matvec_rows(uint8_t* smem, const SmemQ8& s
     case 1: slice_matvec<1>(smem, s, xs, part, zs); break;
     case 2: slice_matvec<2>(smem, s, xs, part, zs); break;
     case 4: slice_matvec<4>(smem, s, xs, part, zs); break;
-    default: slice_matvec<8>(smem, s, xs, part, zs); break;
+    case 8: slice_matvec<8>(smem, s, xs, part, zs); break;
+    default: slice_matvec<16>(smem, s, xs, part, zs); break;
   }
 }
 
@@ -488,12 +491,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) tdt_decode_kernel(const Dec
       __syncthreads();
       slice_matvec_rows(smem, sj, xs, part, zs, mc);
       const int warp = t >> 5, lane = t & 31;
-      if (warp < mc) {  // warp w: stream list[g0 + w]
+      for (int jw = warp; jw < mc; jw += kDecodeThreads / 32) {  // warp w: streams list[g0 + w], + 8, ...
         float v0 = -INFINITY, v1 = -INFINITY;
         int i0 = INT_MAX, i1 = INT_MAX;
         for (int r = lane; r < sj.rows; r += 32) {
           const int row = j0 + r;
-          const float z = zs[r * kDecodeGroup + warp] + p.b_joint[row];
+          const float z = zs[r * kDecodeGroup + jw] + p.b_joint[row];
           if (row < p.vocab) argmax_merge(v0, i0, z, row);
           else argmax_merge(v1, i1, z, row);
         }
@@ -503,7 +506,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) tdt_decode_kernel(const Dec
           argmax_merge(v1, i1, __shfl_down_sync(0xffffffffu, v1, off), __shfl_down_sync(0xffffffffu, i1, off));
         }
         if (lane == 0) {
-          const int b = list[g0 + warp];
+          const int b = list[g0 + jw];
           if (i0 != INT_MAX) atomicMax(keys + b * 2 + 0, argmax_key(v0, i0));
           if (i1 != INT_MAX) atomicMax(keys + b * 2 + 1, argmax_key(v1, i1));
         }

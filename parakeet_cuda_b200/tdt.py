@@ -308,8 +308,8 @@ def greedy_decode_persistent(projected, decoder, durations, max_steps: int | Non
 
 
 # Streams up to which the persistent launch beats the graph-replayed loop
-# (measured per lock-step step on the config-3 decode: 16.8 vs 20.4 us at one
-# stream, 47.9 vs 51.7 at 16, 67.6 vs 59.2 at 24, 124 vs 85 at 48).
+# (measured per lock-step step on the config-3 decode: 16.8-17.4 vs 20.4 us
+# at one stream, 45.1 vs 52.0 at 16, 64.9 vs 58.6 at 24, 150 vs 96 at 64).
 PERSISTENT_MAX_STREAMS = 16
 
 
