@@ -175,11 +175,13 @@ PQ8_API int pq8_gemv(const void* w, const float* x, float* y, const float* bias,
  * to PQ8_GEMV_MAX_M where its FP32 FMA work is small enough to beat the
  * tensor-core GEMM's fixed cost (a measured cost model of both); the
  * tensor-core GEMM otherwise, with split K when its tiles would fill at most
- * half of the SMs (each tile's K blocks shared by up to 8 CTAs, partial sums
- * added in a fixed order by the last of them, so results are deterministic).
- * The workspace (zeroed once by pq8_workspace_init) must hold
+ * half of the SMs (each tile's K blocks shared by 2, 4 or 8 CTAs of one
+ * cluster; their partial sums go through the workspace, and after a cluster
+ * barrier each CTA adds 1/S of the tile's rows in split order, so results are
+ * deterministic). The workspace (zeroed once by pq8_workspace_init) must hold
  * pq8_linear_workspace_size(m, n, k) bytes; with less, the GEMM runs
- * unsplit. The drop-in for Blas.linear (gpu.py:87-90). */
+ * unsplit. PQ8_LINEAR_SPLITS=<s> in the environment forces the split count
+ * (1 turns split K off). The drop-in for Blas.linear (gpu.py:87-90). */
 PQ8_API int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid,
                int m, int n, int k, int epilogue, float alpha, int flags, void* workspace,
                size_t workspace_bytes, void* stream);

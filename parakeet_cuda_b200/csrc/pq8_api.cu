@@ -93,7 +93,8 @@ template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS, int WS
 int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaStream_t st) {
   using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES>;
   if (p.k_splits < 1) p.k_splits = 1;
-  if (p.k_splits > 1 && (PAIR || C::kRedSlots < 1 || p.partial == nullptr || p.tickets == nullptr))
+  if (p.k_splits > 1 &&
+      (!C::kSplitK || p.partial == nullptr || (p.k_splits != 2 && p.k_splits != 4 && p.k_splits != 8)))
     return PQ8_ERR_INVALID_ARGUMENT;
   EncodeTiledFn enc;
   int rc = encode_fn(&enc);
@@ -133,7 +134,8 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   p.m_tiles = (p.m + BN - 1) / BN;
   const int units = (PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles) * p.m_tiles * p.k_splits;
   const int slots = PAIR ? ds->sms / 2 : ds->sms;
-  // a split CTA runs exactly one tile (its last split reuses the activation ring)
+  // a split CTA runs exactly one tile (it stages partials in the activation
+  // ring); the splits of a tile are consecutive CTAs and form one cluster
   if (p.k_splits > 1 && units > slots) return PQ8_ERR_INVALID_ARGUMENT;
   const int grid = std::min(units, slots) * C::kCtas;
   cudaLaunchConfig_t cfg = {};
@@ -143,7 +145,7 @@ int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaS
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = C::kCtas;
+  attr[0].val.clusterDim.x = p.k_splits > 1 ? p.k_splits : C::kCtas;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   // Programmatic dependent launch: set-up, weight fetch and conversion overlap
@@ -926,34 +928,33 @@ bool gemv_faster(int m, int n, int k) {
 }
 
 // Split K for pq8_linear's GEMM path: when BN = 128 tiles would fill at most
-// half of the SMs and K is long (>= 64 blocks), each tile's K blocks are shared
-// by up to 8 CTAs (at least 16 K blocks each) and the partial sums go through
-// the workspace: the counter area's first words are the tiles' tickets, the
-// partials follow it. Measured on B200: a tile's single-CTA pipeline runs
-// about 0.48 us per K block, and the last split pulls the others' partials
-// back at about 1.3 us per split, so shorter K ranges gain nothing
-// (M = 128 x N = 1024 x K = 4096: 54 us unsplit, 24 us in 8 splits; K = 1024
-// shapes within 0.5 us either way).
+// half of the SMs, each tile's K blocks are shared by S = 2, 4 or 8 CTAs (S x
+// tiles within the SM count, at least 4 K blocks each) launched as clusters
+// of S. Each split stores its partial sums to the workspace, after its 64 KB
+// counter area ([tile][split][128][128] fp32); after a cluster barrier every
+// split finishes 1/S of the tile's rows. Measured on B200: a lone tile's
+// pipeline runs ~0.4 us per K block, and the exchange costs ~5 us, so a split
+// must take at least 24 K blocks off each CTA (config 0, 128 x 4096 x 1024:
+// 16.8 -> 14.5 us in 4 splits; 128 x 1024 x 4096: 54 -> 18 us in 8; K = 640
+// in 2 splits would lose 2-3 us). PQ8_LINEAR_SPLITS=<S> forces S (rounded
+// down to a power of two, within the same limits; 1 turns split K off).
 struct SplitPlan {
   int splits;
   size_t bytes;
 };
 SplitPlan plan_split(int m, int n, int k, int sms) {
-  SplitPlan sp{1, 0};
   const long long units = static_cast<long long>((m + 127) / 128) * ((n + kTileRows - 1) / kTileRows);
   const int kb = k / 32;
-  long long s = std::min<long long>({sms / units, kb / 16, 8});
-  if (units * 2 > sms || kb < 64) s = 1;
-  // PQ8_LINEAR_SPLITS=<s> in the environment forces the split count (within
-  // the same limits: one tile per CTA, at least 2 K blocks per split)
-  if (const char* force = std::getenv("PQ8_LINEAR_SPLITS"))
-    s = std::min<long long>({std::max(1, std::atoi(force)), sms / units, kb / 2, 8});
-  // every split gets K blocks: splits of ceil(kb / s) blocks, the last one shorter
-  while (s > 1 && (s - 1) * ((kb + s - 1) / s) >= kb) --s;
-  if (s < 2) return sp;
-  sp.splits = static_cast<int>(s);
-  sp.bytes = kGemvCounterBytes + round256(sizeof(float) * static_cast<size_t>(units) * s * 128 * kTileRows);
-  return sp;
+  long long s = units * 2 > sms ? 1 : std::min<long long>({sms / units, kb / 4, 8});
+  const char* force = std::getenv("PQ8_LINEAR_SPLITS");
+  if (force) s = std::min<long long>({std::max(1, std::atoi(force)), sms / units, kb / 2, 8});
+  int p2 = 1;
+  while (p2 * 2 <= s) p2 *= 2;
+  while (!force && p2 > 1 && kb - (kb + p2 - 1) / p2 < 24) p2 /= 2;
+  // every split gets K blocks: splits of ceil(kb / S) blocks, the last one shorter
+  while (p2 > 1 && (p2 - 1) * ((kb + p2 - 1) / p2) >= kb) p2 /= 2;
+  if (p2 < 2) return SplitPlan{1, 0};
+  return SplitPlan{p2, kGemvCounterBytes + round256(sizeof(float) * static_cast<size_t>(units) * p2 * 128 * kTileRows)};
 }
 
 }  // namespace
@@ -990,7 +991,6 @@ extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* 
       p.n_tiles = (n + kTileRows - 1) / kTileRows;
       p.k_blocks = k / 32;
       p.k_splits = sp.splits;
-      p.tickets = static_cast<int*>(workspace);
       p.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kGemvCounterBytes);
       return launch_gemm<128, 7, 4, 2, false, 2, 8>(ds, kG128, x, p, static_cast<cudaStream_t>(stream));
     }

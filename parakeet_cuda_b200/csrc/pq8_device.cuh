@@ -149,6 +149,13 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, 
                "r"(c1), "r"(smem_addr(src))
                : "memory");
 }
+// Shared -> global bulk copy (bytes a multiple of 16, both addresses 16-byte
+// aligned; completion tracked by bulk groups).
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_addr(src)),
+               "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N committed bulk groups are still reading their shared-memory source.
 template <int N>

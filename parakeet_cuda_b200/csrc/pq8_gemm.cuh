@@ -68,13 +68,13 @@ struct GemmParams {
   int tma_store;  // 1: epilogue stages chunks in shared memory and writes them with TMA stores
   int w_f32;      // 1: w is a dense row-major FP32 [n, k] matrix (no header), rounded to TF32 by the converters
   // Split K (single GEMMs, single-CTA tiles): each output tile's K blocks are
-  // shared by k_splits CTAs; each stores its raw accumulator to `partial`
-  // ([tile][split][BN activation rows][128 weight rows]), and the last of them
-  // (tickets[2 * tile + epilogue half], reset by that CTA) sums the partials in
-  // split order and runs the epilogue.
+  // shared by k_splits (2, 4 or 8) CTAs launched as one cluster. Each stores
+  // its raw accumulator to `partial` ([tile][split][BN activation rows][128
+  // weight rows] fp32, through L2); after a cluster barrier, CTA s pulls rows
+  // [s, s + 1) * BN / k_splits of every split's partial back and runs the
+  // epilogue on their sums, added in split order.
   int k_splits;
   float* partial;
-  int* tickets;
 };
 
 template <int BN_, int STAGES_, int ASLOTS_, int ACC_, bool PAIR_, int GROUPS_ = 2, int GROUP_WARPS_ = 4,
@@ -111,14 +111,13 @@ struct GemmCfg {
   static constexpr int kOutChunkFloats = 32 * 128;
   static constexpr int kOutOff = kWOff + WSTAGES * kRecordBytes;
   static constexpr int kBarOff = kOutOff + 4 * kOutChunkFloats * 4;
-  // Split K: the last split of a tile pulls the partial sums back with bulk
-  // copies, one [kEpiCols activation rows][128] piece per (chunk, split),
-  // into the activation ring (idle by then: a split CTA runs one tile),
-  // kRedSlots pieces in flight per epilogue half.
-  static constexpr int kRedPieceBytes = kEpiCols * 128 * 4;
-  static constexpr int kRedSlotsFit = STAGES * kXStageBytes / (2 * kRedPieceBytes);
-  static constexpr int kRedSlots = kRedSlotsFit < 4 ? kRedSlotsFit : 4;
-  static constexpr int kNumBars = 2 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1 + 8;
+  // Split K: a split CTA stages its accumulator ([BN activation rows][128
+  // weight rows] fp32), and later the rows it finishes from every split, in the
+  // activation ring, idle by then (it runs one tile).
+  static constexpr int kSplitPartialBytes = BN * 128 * 4;
+  static constexpr bool kSplitFits = !PAIR && STAGES * kXStageBytes >= kSplitPartialBytes;
+  static constexpr bool kSplitK = kSplitFits && BN == 128;  // the configuration split launches use
+  static constexpr int kNumBars = 2 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kUsedBytes = kMiscOff + 24;
   static constexpr int kAColBase = ACC * BN;
@@ -417,7 +416,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   uint64_t* acc_full = afree + ASLOTS;
   uint64_t* acc_empty = acc_full + ACC;
   uint64_t* drain = acc_empty + ACC;
-  uint64_t* red_full = drain + 1;  // [2 halves][4]: split-K partial pieces landed
+  uint64_t* red_full = drain + 1;  // [2 epilogue halves]: split-K rows pulled back
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   int* bad_flag = reinterpret_cast<int*>(smem + C::kMiscOff + 8);
@@ -469,7 +468,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       mbar_init(&acc_empty[a], C::kEpiWarps * C::kCtas);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
-    for (int b = 0; b < 8; ++b) mbar_init(&red_full[b], 1);
+    mbar_init(&red_full[0], 1);
+    mbar_init(&red_full[1], 1);
     fence_mbar_init();
   }
   if (warp == C::kTmaWarp && lane == 0 && !SEQ) {
@@ -657,10 +657,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     constexpr int E = C::kEpiCols;
     constexpr int kChunks = BN / E / 2;            // E-column chunks per half
     int chunk_seq = 0;                             // chunks issued by this half (selects the buffer)
-    // split K: this half's piece slots, and the pieces its elected thread has
-    // issued and seen land
-    float* const red_buf = reinterpret_cast<float*>(xs) + half * C::kRedSlots * (C::kRedPieceBytes / 4);
-    int red_issued = 0, red_landed = 0;
+    // Split K: this CTA's split (its rank in the cluster), the activation rows
+    // of the tile this half finishes, and whether the half has passed the
+    // cluster barrier that publishes the partials (every thread of the cluster
+    // passes it exactly once, also when giving up).
+    // (Split launches use the BN = 128 configuration only.)
+    const bool split = !SEQ && C::kSplitK && p.k_splits > 1;
+    // rows [split_off, split_off + split_rows) of the tile; derived where used
+    auto split_rows = [&]() { return BN / p.k_splits / 2; };
+    auto split_off = [&]() { return static_cast<int>(cluster_rank()) * (BN / p.k_splits) + half * split_rows(); };
+    bool published = false;
+    bool red_pending = false;  // this half's pull-back copies issued and not seen land
     int local = 0;
     griddep_wait();  // the residual and the output may be in use by the previous kernel
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
@@ -669,7 +676,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       const int m = PQ8_TP(t, m), n = PQ8_TP(t, n), out_cols = PQ8_TP(t, out_cols), layout = PQ8_TP(t, layout);
       const int epi = PQ8_TP(t, epi), flags = PQ8_TP(t, flags);
       const float alpha = PQ8_TP(t, alpha);
-      const bool tma_store = PQ8_TP(t, tma_store) != 0;
+      const bool tma_store = !split && PQ8_TP(t, tma_store) != 0;
       const float* const bias = PQ8_TP(t, bias);
       const void* ty = SEQ ? static_cast<const void*>(&t.task->tmap_y) : static_cast<const void*>(&tmap_y);
       const bool glu = epi == PQ8_EPI_GLU;
@@ -701,90 +708,79 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         for (int j = 0; j < E; ++j)
           out[j] = (store_lane && m0 + j < m) ? rcol[(size_t)(m0 + j) * out_cols] : 0.0f;
       };
-      const bool split = !SEQ && !PAIR && p.k_splits > 1;
-      if (resid && !split) load_resid(m_tile * BN + half * kChunks * E);
+      if (resid) load_resid(split ? m_tile * BN + split_off() : m_tile * BN + half * kChunks * E);
       if (!mbar_wait(&acc_full[acc], (local / ACC) & 1, abort_flag, status)) break;
       tc_fence_after();
-      // Split K: each half stores its rows of this split's raw accumulator
-      // (through L2), releases the accumulator and takes the half-tile's
-      // ticket; only the last split goes on, summing every split's partial in
-      // split order (the same order whichever CTA is last) before the epilogue.
-      const float* partials = nullptr;
-      auto issue_piece = [&](int i) {  // piece i = (chunk i / splits, split i % splits)
-        const int slot = i % C::kRedSlots;
-        const float* piece = partials + (size_t)(i % p.k_splits) * (BN * kTileRows) +
-                             (size_t)((half * kChunks + i / p.k_splits) * E) * kTileRows;
-        mbar_expect_tx(&red_full[half * 4 + slot], C::kRedPieceBytes);
-        bulk_g2s(red_buf + slot * (C::kRedPieceBytes / 4), piece, C::kRedPieceBytes, &red_full[half * 4 + slot]);
-      };
       if (split) {
-        const int out_tile = tile / p.k_splits;
-        float* mine = p.partial + ((size_t)out_tile * p.k_splits + t.split) * (BN * kTileRows);
+        // Split K: each half stages its chunks of this split's raw accumulator
+        // in the idle activation ring ([64 activation rows][128 weight rows]
+        // at half * 32 KB) and releases the accumulator; its elected thread
+        // stores them to this split's partial with one bulk copy and waits
+        // until they are written. Then the half meets the other splits of the
+        // tile at the cluster barrier (release / acquire).
+        float* const stage_h = reinterpret_cast<float*>(xs) + half * (BN / 2) * kTileRows;
 #pragma unroll 1
         for (int cc = 0; cc < kChunks; ++cc) {
-          const int c = half * kChunks + cc;
           uint32_t v[E];
-          tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
+          tmem_ld32(tmem + lane_base + acc * BN + (half * kChunks + cc) * E, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < E; ++j) __stcg(mine + (size_t)(c * E + j) * kTileRows + r, __uint_as_float(v[j]));
+          for (int j = 0; j < E; ++j) stage_h[(cc * E + j) * kTileRows + r] = __uint_as_float(v[j]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        __threadfence();
+        fence_proxy_async_smem();
         named_barrier_sync(1 + half, 128);
-        volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 12 + 4 * half);
-        partials = p.partial + (size_t)out_tile * p.k_splits * (BN * kTileRows);
         if (elected) {
-          int* ticket = p.tickets + out_tile * 2 + half;
-          const bool last = atomicAdd(ticket, 1) == p.k_splits - 1;
-          if (last) {
-            atomicExch(ticket, 0);  // every split has taken its ticket
-            __threadfence();
-            fence_proxy_async_global();  // the other splits' partials, read by the bulk-copy unit
-            const int first = min(C::kRedSlots, kChunks * p.k_splits);
-            for (int i = 0; i < first; ++i) issue_piece(i);
-            red_issued = first;
-          }
-          *last_flag = last ? 1 : 0;
+          bulk_s2g(p.partial + ((size_t)tile * BN + half * (BN / 2)) * kTileRows, stage_h, (BN / 2) * kTileRows * 4);
+          bulk_commit_group();
+          bulk_wait_group_all();
         }
-        named_barrier_sync(1 + half, 128);
-        if (!*last_flag) continue;
-        if (resid) load_resid(m_tile * BN + half * kChunks * E);
+        __syncwarp();
+        cluster_sync();
+        published = true;
       }
+      const int n_chunks = split ? 1 : kChunks;
 #pragma unroll 1
-      for (int cc = 0; cc < kChunks; ++cc, ++chunk_seq) {
+      for (int cc = 0; cc < n_chunks; ++cc, ++chunk_seq) {
         const int c = half * kChunks + cc;
-        const int m0 = m_tile * BN + c * E;
+        const int m0 = m_tile * BN + (split ? split_off() : c * E);
         if (m0 >= m) break;
         uint32_t v[E];
         if (split) {
-          // the chunk's pieces, split by split, added in split order (onto
-          // +0, which leaves the first piece's values as they are)
-          bool ok = true;
+          // this half's split_rows rows: its elected thread pulls them back
+          // from every split's partial (one bulk copy each, all in flight)
+          // into the half's staging area; they are added in split order (onto
+          // +0, which leaves the first partial's values as they are)
+          const int rows = split_rows();
+          float* const recv = reinterpret_cast<float*>(xs) + half * (BN / 2) * kTileRows;
+          if (elected) {
+            const uint32_t bytes = static_cast<uint32_t>(rows * kTileRows * 4);
+            const int first = tile - static_cast<int>(cluster_rank());  // split 0 of this output tile
+            fence_proxy_async_global();  // the other splits' partials, read by the bulk-copy unit
+            mbar_expect_tx(&red_full[half], bytes * p.k_splits);
+            for (int sp = 0; sp < p.k_splits; ++sp)
+              bulk_g2s(recv + sp * rows * kTileRows, p.partial + ((size_t)(first + sp) * BN + (m0 - m_tile * BN)) * kTileRows,
+                       bytes, &red_full[half]);
+            red_pending = true;
+          }
+          if (!mbar_wait(&red_full[half], 0, abort_flag, status)) break;
+          red_pending = false;
 #pragma unroll
           for (int j = 0; j < E; ++j) v[j] = 0u;
 #pragma unroll 1
           for (int sp = 0; sp < p.k_splits; ++sp) {
-            const int i = cc * p.k_splits + sp, slot = i % C::kRedSlots;
-            if (!mbar_wait(&red_full[half * 4 + slot], (i / C::kRedSlots) & 1, abort_flag, status)) {
-              ok = false;
-              break;
-            }
-            ++red_landed;
-            const float* piece = red_buf + slot * (C::kRedPieceBytes / 4) + r;
+            const float* src = recv + sp * rows * kTileRows + r;
 #pragma unroll
-            for (int j = 0; j < E; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + piece[j * kTileRows]);
-            named_barrier_sync(1 + half, 128);  // every thread of the half is done with the slot
-            if (elected && red_issued < kChunks * p.k_splits) issue_piece(red_issued++);
+            for (int j = 0; j < E; ++j)
+              if (j < rows) v[j] = __float_as_uint(__uint_as_float(v[j]) + src[j * kTileRows]);
           }
-          if (!ok) break;
         } else {
           tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
           tmem_wait_ld();
         }
-        const int cnt = min(E, m - m0);  // warp-uniform
+        const int cnt = min(split ? split_rows() : E, m - m0);  // warp-uniform
         if (resid) {
 #pragma unroll
           for (int j = 0; j < E; ++j) out[j] = fmaf(alpha, __uint_as_float(v[j]) + b, out[j]);
@@ -858,9 +854,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     }
     if (elected) {
       bulk_wait_group_all();
-      // after an abort: never leave pieces still landing in shared memory
-      for (int i = red_landed; i < red_issued; ++i)
-        mbar_drain(&red_full[half * 4 + i % C::kRedSlots], (i / C::kRedSlots) & 1);
+      if (red_pending) mbar_drain(&red_full[half], 0);  // never leave copies landing in shared memory
+    }
+    if (split && !published) {  // gave up before the partials were published
+      __syncwarp();
+      cluster_sync();
     }
   } else if (warp == C::kTmaWarp) {
     // ----------------------------------------------------- activation producer
@@ -1030,10 +1028,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     }
   }
 
+  // Split K: the warps other than the epilogue's take part in the cluster
+  // barrier that publishes the partials (with nothing to publish).
+  const bool split_cluster = !SEQ && C::kSplitK && p.k_splits > 1;
+  if (split_cluster && warp < C::kEpiWarp0) {
+    __syncwarp();
+    cluster_arrive_relaxed();
+  }
   __syncthreads();
   // The peer must not exit (freeing shared memory the leader's MMAs read) and the
   // tensor memory must not be freed before both CTAs are done.
   if constexpr (PAIR) cluster_sync();
+  if (split_cluster && warp < C::kEpiWarp0) cluster_wait();
   if (warp == C::kMmaWarp) {
     __syncwarp();
     tc_fence_after();

@@ -218,10 +218,10 @@ def test_linear_dispatch_gemv_matches_gemm(rt):
 
 @pytest.mark.parametrize('m,n,k,kernel', [(16, 1024, 4096, 'gemv'), (24, 640, 640, 'gemv'), (48, 8198, 640, 'gemm'),
                                           (64, 4096, 1024, 'gemm'), (9, 129, 1024, 'gemv')])
-def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
+def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel, monkeypatch):
     """pq8_linear sends 9..64 rows to whichever kernel its measured cost model
     finds faster: the result is bit for bit that kernel's (for the tensor-core
-    GEMM, its unsplit form: the workspace is withheld, which turns split K off)."""
+    GEMM, its unsplit form: PQ8_LINEAR_SPLITS=1 turns split K off)."""
     rng = np.random.default_rng(m + n)
     raw = q8_0_blocks(rng, n, k)
     w = rt.pack(raw, n, k)
@@ -230,6 +230,7 @@ def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
     if kernel == 'gemm':
         want = rt.gemm(xd, w).cpu().numpy()
         y = torch.empty(m, n, device='cuda')
+        monkeypatch.setenv('PQ8_LINEAR_SPLITS', '1')
         rt.lib.call('pq8_linear', w.pointer, xd.data_ptr(), y.data_ptr(), None, None, m, n, k, EPI_NONE, 1.0, 0,
                     None, 0, rt.stream())
         np.testing.assert_array_equal(y.cpu().numpy(), want)
@@ -249,22 +250,26 @@ def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel):
 SPLIT_CASES = [  # m, n, k, epilogue, bias, forced splits: units = M tiles x N tiles of 128
     (128, 1024, 4096, EPI_NONE, False, None),     # 8 units, 8 splits of 16 K blocks
     (441, 1024, 4096, EPI_NONE, True, None),      # reference contract shape: 32 units, 4 splits
-    (130, 1000, 2080, EPI_SILU, True, None),      # ragged M and N, 65 K blocks: splits of 17, 17, 17, 14
-    (100, 640, 2048, EPI_RESIDUAL, False, None),  # 5 units, 4 splits
+    (1024, 1024, 4096, EPI_NONE, False, None),    # 64 units, 2 splits
+    (130, 1000, 2080, EPI_SILU, True, None),      # ragged M and N, 65 K blocks: 8 splits, 7 x 9 and one of 2
+    (100, 640, 2048, EPI_RESIDUAL, False, None),  # 5 units, 8 splits
     (128, 2048, 2048, EPI_GLU, True, None),       # GLU pairs split like any row
-    (64, 4096, 2048, EPI_NONE, False, None),      # 64 rows on the GEMM side of the dispatch
-    (128, 4096, 1024, EPI_NONE, False, 4),        # config 0, forced: 4 splits of 8
-    (128, 1024, 1056, EPI_RESIDUAL, True, 8),     # forced 8 -> 7 splits: six of 5 K blocks and one of 3
+    (64, 4096, 2048, EPI_NONE, False, None),      # 64 rows on the GEMM side of the dispatch: 4 splits
+    (128, 4096, 1024, EPI_NONE, False, None),     # config 0: 4 splits of 8
+    (128, 4096, 1024, EPI_RESIDUAL, True, 2),     # config 0, forced: 2 splits of 16
+    (128, 1024, 1056, EPI_RESIDUAL, True, 8),     # forced 8 -> 4 (8 would leave the last empty): 9, 9, 9, 6
 ]
 
 
 @pytest.mark.parametrize('m,n,k,epi,with_bias,forced', SPLIT_CASES)
 def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias, forced, monkeypatch):
     """pq8_linear splits K when the GEMM's tiles would fill at most half of the
-    SMs and K is long (PQ8_LINEAR_SPLITS forces a count): the result meets the
-    north-star bar and the TF32-operand model bar, and a repeat call is bit for
-    bit the same (the last split of a tile adds the partials in split order
-    and resets the tile's tickets)."""
+    SMs (PQ8_LINEAR_SPLITS forces a count): the splits of a tile run as one
+    cluster, store their partials to the workspace and, after a cluster
+    barrier, each finishes its share of the tile's rows adding the partials in
+    split order. The result meets the north-star bar and the TF32-operand model
+    bar, and a repeat call is bit for bit the same; without a workspace the
+    GEMM runs unsplit (the bits of pq8_gemm)."""
     if forced:
         monkeypatch.setenv('PQ8_LINEAR_SPLITS', str(forced))
     assert rt.lib.linear_workspace_size(m, n, k) > (rt.lib.gemv_workspace_size(m, n, k) if m <= 64 else 0)
@@ -281,18 +286,23 @@ def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias, forced, monk
                 epilogue=epi, alpha=alpha)
     y1 = rt.linear(xd, w, **args)
     y2 = rt.linear(xd, w, **args)
+    y3 = torch.empty_like(y1)
+    rt.lib.call('pq8_linear', w.pointer, xd.data_ptr(), y3.data_ptr(),
+                args['bias'].data_ptr() if with_bias else None, args['resid'].data_ptr() if resid is not None else None,
+                m, n, k, epi, alpha, 0, None, 0, rt.stream())
     torch.cuda.synchronize()
     assert rt.device_status() == 0
     np.testing.assert_array_equal(y1.cpu().numpy(), y2.cpu().numpy())
     check_gemm(y1, x, raw, n, k, epi=epi, bias=bias, resid=resid, alpha=alpha)
-    # the tickets are back at zero: the counter area's first 2 x units words
-    units = ((m + 127) // 128) * ((n + 127) // 128)
-    assert int(rt.workspace[:8 * units].view(torch.int32).abs().sum()) == 0
+    if m > 64:  # (up to 64 rows the dispatch may pick the GEMV, which needs its workspace)
+        y4 = rt.gemm(xd, w, **args)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(y3.cpu().numpy(), y4.cpu().numpy())
 
 
 def test_linear_split_k_in_graph_repeats(rt):
-    """Twenty split launches captured in one CUDA graph and replayed: the
-    tickets of one launch are reset before the next reads them."""
+    """Twenty split launches captured in one CUDA graph and replayed three
+    times give the bits of the eager calls every time."""
     m, n, k = 128, 1024, 4096
     rng = np.random.default_rng(5)
     raw = q8_0_blocks(rng, n, k)
