@@ -629,7 +629,7 @@ constexpr int kSeqCfgId = 16;  // DeviceState::attr_set slot of the sequence ker
 constexpr size_t kSeqHeaderBytes = sizeof(SeqPlanHeader);
 
 struct SeqLayout {
-  size_t tasks_offset, counters_offset, total;
+  size_t tasks_offset, counters_offset, start_offset, order_offset, total;
   int n_counters, total_tiles;
 };
 
@@ -661,8 +661,130 @@ int seq_layout(const pq8_gemm_task* tasks, int count, SeqLayout* out) {
   out->counters_offset = round256(kSeqHeaderBytes + sizeof(SeqTask) * static_cast<size_t>(count));
   out->n_counters = static_cast<int>(counters);
   out->total_tiles = static_cast<int>(tiles);
-  out->total = round256(out->counters_offset + sizeof(int) * static_cast<size_t>(counters));
+  out->start_offset = round256(out->counters_offset + sizeof(int) * static_cast<size_t>(counters));
+  out->order_offset = round256(out->start_offset + sizeof(int) * (kSeqMaxCtas + 1));
+  out->total = round256(out->order_offset + sizeof(uint64_t) * static_cast<size_t>(tiles));
   return PQ8_OK;
+}
+
+// The tile schedule of a sequence: which CTA runs which tile, in what order.
+// List scheduling over a model of the launch: the CTA the model frees first
+// takes, among the next kLookahead tiles not yet taken (in plan order: task
+// after task, N units fastest), the first whose activation rows the model
+// has ready by then, else the one ready soonest; a tile is a candidate only
+// once every tile it depends on has been taken. The order in which tiles are
+// taken is therefore one in which each comes after every tile it depends on,
+// and every CTA's list follows it. The model: a tile occupies its CTA's
+// tensor pipe for (1 + 0.33 x K blocks) us, starting no earlier than 1 us
+// after its activation rows' producer row blocks completed; a row block
+// completes 3 us (the epilogue) after its last tile's mainloop, or after its
+// output's dependencies. Against taking every gridDim-th tile it evens out
+// CTAs that drew long-K tiles (FFN down projections: 128 K blocks against 32)
+// and fills dependency waits with tiles that have none.
+// PQ8_SEQUENCE_SCHEDULE=strided in the environment gives CTA c tiles c,
+// c + ctas, ... of the plan order instead (for comparison).
+void seq_schedule(const std::vector<SeqTask>& host, int ctas, std::vector<int>& start, std::vector<uint64_t>& order) {
+  constexpr double kTileFixed = 1.0, kPerBlock = 0.33, kEpilogue = 3.0, kLoad = 1.0;
+  constexpr int kLookahead = 64;
+  int n_counters = 0;
+  long long total = 0;
+  for (const SeqTask& t : host) {
+    n_counters = std::max(n_counters, t.counter + t.p.m_tiles);
+    total += static_cast<long long>(t.p.m_tiles) * t.n_units;
+  }
+  std::vector<double> done(n_counters, 0.0);
+  std::vector<int> left(n_counters, 0);  // tiles of each row block not yet taken
+  for (const SeqTask& t : host)
+    for (int m = 0; m < t.p.m_tiles; ++m) left[t.counter + m] = t.n_units;
+  // Latest completion of the producer row blocks a dependency list needs for
+  // row block m_tile, or -1 while any of their tiles has not been taken.
+  auto ready = [&](const SeqDep* deps, int nd, int m_tile) {
+    double r = 0.0;
+    for (int d = 0; d < nd; ++d) {
+      const SeqTask& prod = host[deps[d].task];
+      int lo = m_tile, hi = m_tile;
+      if (deps[d].window > 0) {
+        const int w = deps[d].window, r0 = m_tile * kSeqBN, r1 = r0 + kSeqBN - 1;
+        lo = (r0 / w) * w / kSeqBN;
+        hi = ((r1 / w) * w + w - 1) / kSeqBN;
+      }
+      hi = std::min(hi, prod.p.m_tiles - 1);
+      for (int row = lo; row <= hi; ++row) {
+        if (left[prod.counter + row] > 0) return -1.0;
+        r = std::max(r, done[prod.counter + row]);
+      }
+    }
+    return r;
+  };
+  // tiles in plan order: (task, row block, weight tile)
+  std::vector<uint64_t> tiles;
+  tiles.reserve(static_cast<size_t>(total));
+  for (size_t i = 0; i < host.size(); ++i)
+    for (int m = 0; m < host[i].p.m_tiles; ++m)
+      for (int n = 0; n < host[i].n_units; ++n)
+        tiles.push_back((static_cast<uint64_t>(i) << 48) | (static_cast<uint64_t>(n) << 32) |
+                        (static_cast<uint64_t>(m) << 16) | static_cast<uint64_t>(host[i].p.k_blocks));
+  const char* mode = std::getenv("PQ8_SEQUENCE_SCHEDULE");
+  const bool strided = mode != nullptr && std::strcmp(mode, "strided") == 0;
+  std::vector<std::vector<uint64_t>> lists(ctas);
+  std::vector<char> taken(tiles.size(), 0);
+  std::vector<std::pair<double, int>> heap;  // (time the CTA's tensor pipe is free, CTA), min-heap
+  for (int c = 0; c < ctas; ++c) heap.push_back({0.0, c});
+  auto later = [](const std::pair<double, int>& a, const std::pair<double, int>& b) { return a > b; };
+  std::make_heap(heap.begin(), heap.end(), later);
+  size_t first = 0;  // lowest tile not yet taken
+  for (size_t k = 0; k < tiles.size(); ++k) {
+    std::pop_heap(heap.begin(), heap.end(), later);
+    auto [free_at, c] = heap.back();
+    while (taken[first]) ++first;
+    size_t pick = first;
+    double pick_ready = 0.0;
+    if (strided) {
+      c = static_cast<int>(k % ctas);
+      pick_ready = std::max(0.0, ready(host[tiles[k] >> 48].x_dep, host[tiles[k] >> 48].n_x_deps,
+                                       static_cast<int>((tiles[k] >> 16) & 0xFFFF)));
+      pick = k;
+    } else {
+      pick_ready = -1.0;
+      int seen = 0;
+      for (size_t j = first; j < tiles.size() && seen < kLookahead; ++j) {
+        if (taken[j]) continue;
+        ++seen;
+        const SeqTask& t = host[tiles[j] >> 48];
+        const int m = static_cast<int>((tiles[j] >> 16) & 0xFFFF);
+        const double xr = ready(t.x_dep, t.n_x_deps, m);
+        if (xr < 0.0 || ready(t.out_dep, t.n_out_deps, m) < 0.0) continue;  // a dependency not taken yet
+        if (xr + kLoad <= free_at) {
+          pick = j;
+          pick_ready = xr;
+          break;
+        }
+        if (pick_ready < 0.0 || xr < pick_ready) {
+          pick = j;
+          pick_ready = xr;
+        }
+      }
+      if (pick_ready < 0.0) pick_ready = 0.0;  // (the first tile not taken always qualifies)
+    }
+    const uint64_t e = tiles[pick];
+    const SeqTask& t = host[e >> 48];
+    const int m = static_cast<int>((e >> 16) & 0xFFFF);
+    const double end = std::max(free_at, pick_ready + kLoad) + kTileFixed + kPerBlock * t.p.k_blocks;
+    const double out_ready = std::max(0.0, ready(t.out_dep, t.n_out_deps, m));
+    heap.back() = {end, c};
+    std::push_heap(heap.begin(), heap.end(), later);
+    done[t.counter + m] = std::max(done[t.counter + m], std::max(end, out_ready) + kEpilogue);
+    --left[t.counter + m];
+    taken[pick] = 1;
+    lists[c].push_back(e);
+  }
+  start.assign(ctas + 1, 0);
+  order.clear();
+  for (int c = 0; c < ctas; ++c) {
+    start[c] = static_cast<int>(order.size());
+    order.insert(order.end(), lists[c].begin(), lists[c].end());
+  }
+  start[ctas] = static_cast<int>(order.size());
 }
 
 // A buffer as the sequence sees it: rows of `width` floats starting at `base`.
@@ -816,6 +938,10 @@ extern "C" int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* pl
         return PQ8_ERR_DRIVER;
     }
   }
+  if (ds->sms > kSeqMaxCtas) return PQ8_ERR_UNSUPPORTED_SHAPE;
+  std::vector<int> start;
+  std::vector<uint64_t> order;
+  seq_schedule(host, ds->sms, start, order);
   std::vector<uint8_t> blob(L.total, 0);
   SeqPlanHeader hdr{};
   hdr.magic = kSeqMagic;
@@ -826,8 +952,13 @@ extern "C" int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* pl
   hdr.finished = 0;
   hdr.tasks_offset = static_cast<long long>(L.tasks_offset);
   hdr.counters_offset = static_cast<long long>(L.counters_offset);
+  hdr.ctas = ds->sms;
+  hdr.start_offset = static_cast<long long>(L.start_offset);
+  hdr.order_offset = static_cast<long long>(L.order_offset);
   std::memcpy(blob.data(), &hdr, sizeof(hdr));
   std::memcpy(blob.data() + L.tasks_offset, host.data(), sizeof(SeqTask) * host.size());
+  std::memcpy(blob.data() + L.start_offset, start.data(), sizeof(int) * start.size());
+  std::memcpy(blob.data() + L.order_offset, order.data(), sizeof(uint64_t) * order.size());
   cudaError_t e = cudaMemcpyAsync(plan, blob.data(), blob.size(), cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   return to_code(e);

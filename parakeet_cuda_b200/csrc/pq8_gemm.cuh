@@ -197,16 +197,16 @@ __device__ __forceinline__ void expand16_tf32(const uint4 q, uint32_t sbits, boo
 //
 // The host lays a plan out in device memory (pq8_sequence_plan): a header,
 // one SeqTask per GEMM (its parameters, tensor maps and dependencies) and one
-// completion counter per (task, 192-row block). Tiles are numbered task after
-// task, and within a task N-unit fastest, so a task's row blocks complete in
-// order. CTA c runs tiles c, c + grid, c + 2 grid, ... Before a tile's
+// completion counter per (task, 192-row block). The plan's schedule gives
+// each CTA its list of tiles, all lists following one global order in which
+// every tile comes after the tiles it depends on. Before a tile's
 // activations are loaded, its X dependencies must have completed the row
 // blocks the tile reads; before its epilogue reads the residual or writes the
 // output, its output dependencies must have (write-after-read,
-// write-after-write, and the residual's read-after-write). Every dependency
-// points to an earlier task and every CTA runs its tiles in order, so the
-// lowest unfinished tile can always make progress while all CTAs are
-// resident (one per SM). Counters are reset by the last CTA to finish.
+// write-after-write, and the residual's read-after-write). As every CTA runs
+// its list in order, the earliest unfinished tile of the global order can
+// always make progress while all CTAs are resident (one per SM). Counters
+// are reset by the last CTA to finish.
 constexpr uint32_t kSeqMagic = 0x51455350u;  // "PSEQ"
 constexpr int kSeqMaxDeps = 4;
 
@@ -228,6 +228,12 @@ struct alignas(128) SeqTask {
   SeqDep out_dep[kSeqMaxDeps];
 };
 
+// Tile schedule: CTA c runs tiles order[start[c]] ... order[start[c + 1] - 1],
+// each entry (task << 48 | weight tile << 32 | row block << 16 | K blocks).
+// Every CTA's list follows one global order in which each tile comes after
+// every tile it depends on.
+constexpr int kSeqMaxCtas = 1024;
+
 struct alignas(128) SeqPlanHeader {
   uint32_t magic;
   int count;        // tasks
@@ -236,6 +242,8 @@ struct alignas(128) SeqPlanHeader {
   int bn;           // rows per tile (all tasks)
   int finished;     // CTAs done with this run (the last one resets the counters)
   long long tasks_offset, counters_offset;
+  int ctas;         // CTAs the schedule is made for (the device's SM count)
+  long long start_offset, order_offset;  // int start[ctas + 1]; uint64_t order[total_tiles]
 };
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -335,33 +343,25 @@ struct TileWindow<kCtas, false> {
 // Looks up the tile of lane (threadIdx & 31) of the window starting at local
 // index `local`; out of line, so that its temporaries do not add to the
 // register pressure of the role loops it is called from (once per 32 tiles).
-__device__ __noinline__ void seq_window_entry(const uint8_t* plan, int local, int* cur, uint32_t* task_n,
-                                              uint32_t* m_kb) {
+__device__ __noinline__ void seq_window_entry(const uint8_t* plan, int local, uint32_t* task_n, uint32_t* m_kb) {
   const SeqPlanHeader* hdr = reinterpret_cast<const SeqPlanHeader*>(plan);
-  const SeqTask* tasks = reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader));
-  const int tile =
-      static_cast<int>(blockIdx.x) + (local + static_cast<int>(threadIdx.x & 31)) * static_cast<int>(gridDim.x);
-  if (tile >= hdr->total_tiles) return;
-  const int count = hdr->count;
-  int c = *cur;
-  while (c + 1 < count && tasks[c + 1].tile0 <= tile) ++c;
-  *cur = c;
-  const SeqTask* t = tasks + c;
-  const int u = tile - t->tile0, nu = t->n_units;
-  *task_n = (static_cast<uint32_t>(c) << 16) | static_cast<uint32_t>(u % nu);
-  *m_kb = (static_cast<uint32_t>(u / nu) << 16) | static_cast<uint32_t>(t->p.k_blocks);
+  const int* start = reinterpret_cast<const int*>(plan + hdr->start_offset);
+  const int tile = start[blockIdx.x] + local + static_cast<int>(threadIdx.x & 31);
+  if (tile >= start[blockIdx.x + 1]) return;
+  const uint64_t e = reinterpret_cast<const uint64_t*>(plan + hdr->order_offset)[tile];
+  *task_n = static_cast<uint32_t>(e >> 32);
+  *m_kb = static_cast<uint32_t>(e);
 }
 
 template <int kCtas>
 struct TileWindow<kCtas, true> {
-  int cur = 0;     // task of this lane's latest lookup
   int base = -64;  // local index of lane 0's entry
   uint32_t e_task_n = 0, e_m_kb = 0;  // this lane's entry, two 16-bit fields each
   __device__ __forceinline__ TileRef get(int local, uint32_t, const uint8_t* plan) {
     const SeqTask* tasks = reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader));
     if (local - base >= 32) {
       base = local;
-      seq_window_entry(plan, local, &cur, &e_task_n, &e_m_kb);
+      seq_window_entry(plan, local, &e_task_n, &e_m_kb);
     }
     const int i = local - base;
     const uint32_t tn = __shfl_sync(0xffffffffu, e_task_n, i), mk = __shfl_sync(0xffffffffu, e_m_kb, i);
@@ -375,16 +375,13 @@ struct TileWindow<kCtas, true> {
 template <int kCtas, bool SEQ>
 struct TileCursor {
   int m_tiles, k_blocks, splits;  // single GEMM
-  int cur = 0;            // sequence: task of the latest lookup
+  const uint64_t* order;          // sequence: the schedule's tile entries
   __device__ __forceinline__ TileRef at(int tile, uint32_t rank, const uint8_t* plan) {
     if constexpr (SEQ) {
-      const SeqPlanHeader* hdr = reinterpret_cast<const SeqPlanHeader*>(plan);
       const SeqTask* tasks = reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader));
-      const int count = hdr->count;
-      while (cur + 1 < count && tasks[cur + 1].tile0 <= tile) ++cur;
-      const SeqTask* t = tasks + cur;
-      const int u = tile - t->tile0, nu = t->n_units;
-      return {t, u % nu, u / nu, t->p.k_blocks};
+      const uint64_t e = __ldg(reinterpret_cast<const unsigned long long*>(order) + tile);
+      return {tasks + static_cast<int>(e >> 48), static_cast<int>((e >> 32) & 0xFFFFu),
+              static_cast<int>((e >> 16) & 0xFFFFu), static_cast<int>(e & 0xFFFFu)};
     } else {
       return single_tile<kCtas>(tile, rank, m_tiles, k_blocks, splits);
     }
@@ -428,16 +425,18 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   griddep_launch();
   const uint32_t rank = PAIR ? cluster_rank() : 0;  // 0 = leader (issues the MMAs)
   const bool leader = rank == 0;
-  const int unit0 = blockIdx.x / C::kCtas;          // first work unit of this CTA (pair)
-  const int unit_stride = gridDim.x / C::kCtas;
-
   // Tiles of this launch: one GEMM (p), or every task of a sequence plan.
+  // A single GEMM's CTA (pair) runs units blockIdx, blockIdx + grid, ...; a
+  // sequence CTA runs its list of the plan's schedule, entries start[c] on.
   const SeqPlanHeader* hdr = SEQ ? reinterpret_cast<const SeqPlanHeader*>(plan) : nullptr;
   const SeqTask* tasks = SEQ ? reinterpret_cast<const SeqTask*>(plan + sizeof(SeqPlanHeader)) : nullptr;
   int* counters = SEQ ? reinterpret_cast<int*>(const_cast<uint8_t*>(plan) + hdr->counters_offset) : nullptr;
+  const int* seq_start = SEQ ? reinterpret_cast<const int*>(plan + hdr->start_offset) : nullptr;
   const int task_count = SEQ ? hdr->count : 1;
   const int n_units = PAIR ? (p.n_tiles + 1) / 2 : p.n_tiles;
-  const int num_tiles = SEQ ? hdr->total_tiles : n_units * p.m_tiles * p.k_splits;
+  const int unit0 = SEQ ? seq_start[blockIdx.x] : static_cast<int>(blockIdx.x) / C::kCtas;
+  const int unit_stride = SEQ ? 1 : static_cast<int>(gridDim.x) / C::kCtas;
+  const int num_tiles = SEQ ? seq_start[blockIdx.x + 1] : n_units * p.m_tiles * p.k_splits;
   int* const status = p.status;
 
   if (threadIdx.x == 0) {
@@ -447,6 +446,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         const PackedHeader* h = reinterpret_cast<const PackedHeader*>(p.w);
         ok = h->magic == kMagic && h->n == p.n && h->k == p.k && h->layout == p.layout && h->n_tiles == p.n_tiles;
       }
+    } else {
+      ok = hdr->ctas == static_cast<int>(gridDim.x);  // the schedule is made for this many CTAs
     }
     *bad_flag = ok ? 0 : 1;
     *abort_flag = 0;
@@ -496,7 +497,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   // Arrivals that the leader's MMA waits for go to the leader's barriers.
   const uint32_t conv_remote = PAIR ? map_to_rank(conv, 0) : 0;
   const uint32_t acc_empty_remote = PAIR ? map_to_rank(acc_empty, 0) : 0;
-  TileCursor<C::kCtas, SEQ> src{p.m_tiles, p.k_blocks, p.k_splits};
+  TileCursor<C::kCtas, SEQ> src{p.m_tiles, p.k_blocks, p.k_splits,
+                                SEQ ? reinterpret_cast<const uint64_t*>(plan + hdr->order_offset) : nullptr};
   const int x_flags = SEQ ? (task_count > 0 ? tasks[0].p.flags : 0) : p.flags;
   bool mma_issued = false;
 

@@ -346,8 +346,15 @@ class EncoderStackHost:
             for entry in LAYER_PLAN:
                 self.launch(l, entry)
 
-    def sequence_tasks(self, dependencies: str = 'model', window: int = FRAMES_PER_WINDOW) -> list:
-        """Every linear of every layer as ``pq8_gemm_task``s, in launch order.
+    # Order of a layer's linears in a sequence plan: the layer's order with
+    # linear_pos, which depends on nothing in the layer, ahead of QKV, so that
+    # its tiles are there to take while QKV waits for the rows of the FFN1
+    # residual (the plan's schedule hands tiles out in plan order).
+    SEQUENCE_ORDER = ('ffn1_up', 'ffn1_down', 'pos', 'qkv', 'out', 'pw1_glu', 'pw2', 'ffn2_up', 'ffn2_down')
+
+    def sequence_tasks(self, dependencies: str = 'model', window: int = FRAMES_PER_WINDOW, order=None) -> list:
+        """Every linear of every layer as ``pq8_gemm_task``s, in plan order
+        (``order``: names of a layer's linears, default ``SEQUENCE_ORDER``).
 
         Dependencies the buffers show (the FFN hidden state, the GLU output, the
         residual stream, and every rewrite of a buffer) are found by the library.
@@ -361,10 +368,14 @@ class EncoderStackHost:
         if dependencies not in ('model', 'buffers'):
             raise ValueError(dependencies)
         b = self.buffers
+        plan = {entry[0]: entry for entry in LAYER_PLAN}
+        names = self.SEQUENCE_ORDER if order is None else tuple(order)
+        if sorted(names) != sorted(plan):
+            raise ValueError(f'order must name each of {sorted(plan)} once')
         tasks, index = [], {}
         last_residual = -1
         for l in range(self.layers):
-            for name, _, n, k, epi, alpha, src, dst, flags in LAYER_PLAN:
+            for name, _, n, k, epi, alpha, src, dst, flags in (plan[nm] for nm in names):
                 after, after_window = -1, 0
                 if dependencies == 'model':
                     if name in ('ffn1_up', 'qkv', 'pw1_glu', 'ffn2_up'):
@@ -380,10 +391,10 @@ class EncoderStackHost:
                     last_residual = len(tasks) - 1
         return tasks
 
-    def make_sequence(self, dependencies: str = 'model') -> Buffer:
+    def make_sequence(self, dependencies: str = 'model', order=None) -> Buffer:
         """Plan every linear of a step as one persistent launch (``pq8_sequence_plan``);
         ``step_sequence`` runs it."""
-        tasks = self.sequence_tasks(dependencies)
+        tasks = self.sequence_tasks(dependencies, order=order)
         nbytes = self.rt.lib.sequence_plan_size(tasks)
         if getattr(self, '_plan', None) is None or self._plan.nbytes < nbytes:
             self._plan = Buffer(self.rt.drv.alloc(nbytes), nbytes, (nbytes,), np.uint8)
