@@ -176,12 +176,13 @@ PQ8_API int pq8_gemv(const void* w, const float* x, float* y, const float* bias,
  * tensor-core GEMM's fixed cost (a measured cost model of both); the
  * tensor-core GEMM otherwise, with split K when its tiles would fill at most
  * half of the SMs (each tile's K blocks shared by 2, 4 or 8 CTAs of one
- * cluster; their partial sums go through the workspace, and after a cluster
- * barrier each CTA adds 1/S of the tile's rows in split order, so results are
- * deterministic). The workspace (zeroed once by pq8_workspace_init) must hold
- * pq8_linear_workspace_size(m, n, k) bytes; with less, the GEMM runs
- * unsplit. PQ8_LINEAR_SPLITS=<s> in the environment forces the split count
- * (1 turns split K off). The drop-in for Blas.linear (gpu.py:87-90). */
+ * cluster, which exchange their partial sums between their shared memories;
+ * each CTA adds 1/S of the tile's rows in split order, so results are
+ * deterministic; no workspace is involved). The workspace (zeroed once by
+ * pq8_workspace_init) is the GEMV's and must hold
+ * pq8_linear_workspace_size(m, n, k) bytes. PQ8_LINEAR_SPLITS=<s> in the
+ * environment forces the split count (1 turns split K off). The drop-in for
+ * Blas.linear (gpu.py:87-90). */
 PQ8_API int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid,
                int m, int n, int k, int epilogue, float alpha, int flags, void* workspace,
                size_t workspace_bytes, void* stream);

@@ -93,8 +93,7 @@ template <int BN, int STAGES, int ASLOTS, int ACC, bool PAIR, int GROUPS, int WS
 int launch_gemm(DeviceState* ds, int cfg_id, const float* x, GemmParams p, cudaStream_t st) {
   using C = GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS, 4, 32, WSTAGES>;
   if (p.k_splits < 1) p.k_splits = 1;
-  if (p.k_splits > 1 &&
-      (!C::kSplitK || p.partial == nullptr || (p.k_splits != 2 && p.k_splits != 4 && p.k_splits != 8)))
+  if (p.k_splits > 1 && (!C::kSplitK || (p.k_splits != 2 && p.k_splits != 4 && p.k_splits != 8)))
     return PQ8_ERR_INVALID_ARGUMENT;
   EncodeTiledFn enc;
   int rc = encode_fn(&enc);
@@ -1061,19 +1060,15 @@ bool gemv_faster(int m, int n, int k) {
 // Split K for pq8_linear's GEMM path: when BN = 128 tiles would fill at most
 // half of the SMs, each tile's K blocks are shared by S = 2, 4 or 8 CTAs (S x
 // tiles within the SM count, at least 4 K blocks each) launched as clusters
-// of S. Each split stores its partial sums to the workspace, after its 64 KB
-// counter area ([tile][split][128][128] fp32); after a cluster barrier every
-// split finishes 1/S of the tile's rows. Measured on B200: a lone tile's
-// pipeline runs ~0.4 us per K block, and the exchange costs ~5 us, so a split
-// must take at least 24 K blocks off each CTA (config 0, 128 x 4096 x 1024:
-// 16.8 -> 14.5 us in 4 splits; 128 x 1024 x 4096: 54 -> 18 us in 8; K = 640
-// in 2 splits would lose 2-3 us). PQ8_LINEAR_SPLITS=<S> forces S (rounded
-// down to a power of two, within the same limits; 1 turns split K off).
-struct SplitPlan {
-  int splits;
-  size_t bytes;
-};
-SplitPlan plan_split(int m, int n, int k, int sms) {
+// of S, which exchange their partial sums through shared memory (no
+// workspace). Measured on B200: a lone tile's pipeline runs ~0.4 us per K
+// block and the exchange costs ~4 us, so a split must take at least 16 K
+// blocks off each CTA (config 0, 128 x 4096 x 1024: 16.8 -> 14.3 us in 4
+// splits; 128 x 1024 x 4096: 54 -> 17.6 us in 8; 256 x 4096 x 1024: 18.0 ->
+// 17.0 us in 2; K = 640 in 2 splits would lose 0.8-1.6 us).
+// PQ8_LINEAR_SPLITS=<S> forces S (rounded down to a power of two, within the
+// same limits; 1 turns split K off).
+int plan_split(int m, int n, int k, int sms) {
   const long long units = static_cast<long long>((m + 127) / 128) * ((n + kTileRows - 1) / kTileRows);
   const int kb = k / 32;
   long long s = units * 2 > sms ? 1 : std::min<long long>({sms / units, kb / 4, 8});
@@ -1081,11 +1076,10 @@ SplitPlan plan_split(int m, int n, int k, int sms) {
   if (force) s = std::min<long long>({std::max(1, std::atoi(force)), sms / units, kb / 2, 8});
   int p2 = 1;
   while (p2 * 2 <= s) p2 *= 2;
-  while (!force && p2 > 1 && kb - (kb + p2 - 1) / p2 < 24) p2 /= 2;
+  while (!force && p2 > 1 && kb - (kb + p2 - 1) / p2 < 16) p2 /= 2;
   // every split gets K blocks: splits of ceil(kb / S) blocks, the last one shorter
   while (p2 > 1 && (p2 - 1) * ((kb + p2 - 1) / p2) >= kb) p2 /= 2;
-  if (p2 < 2) return SplitPlan{1, 0};
-  return SplitPlan{p2, kGemvCounterBytes + round256(sizeof(float) * static_cast<size_t>(units) * p2 * 128 * kTileRows)};
+  return p2;
 }
 
 }  // namespace
@@ -1100,8 +1094,8 @@ extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* 
     DeviceState* ds;
     int rc = device_state(&ds);
     if (rc) return rc;
-    const SplitPlan sp = plan_split(m, n, k, ds->sms);
-    if (sp.splits > 1 && workspace != nullptr && workspace_bytes >= sp.bytes && aligned(workspace, 256)) {
+    const int splits = plan_split(m, n, k, ds->sms);
+    if (splits > 1) {
       if ((rc = check_linear_args(w, x, y, resid, m, n, k, epilogue))) return rc;
       if (!aligned(x, 16)) return PQ8_ERR_MISALIGNED;
       if (flags & ~(PQ8_FLAG_X_TF32 | PQ8_FLAG_OUT_TF32)) return PQ8_ERR_INVALID_ARGUMENT;
@@ -1121,8 +1115,7 @@ extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* 
       p.out_cols = epilogue == PQ8_EPI_GLU ? n / 2 : n;
       p.n_tiles = (n + kTileRows - 1) / kTileRows;
       p.k_blocks = k / 32;
-      p.k_splits = sp.splits;
-      p.partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kGemvCounterBytes);
+      p.k_splits = splits;
       return launch_gemm<128, 7, 4, 2, false, 2, 8>(ds, kG128, x, p, static_cast<cudaStream_t>(stream));
     }
   }
@@ -1141,8 +1134,6 @@ extern "C" int pq8_linear_workspace_size(int m, int n, int k, size_t* bytes) {
     const GemvPlan g = plan_gemv(m, n, k, ds->sms);
     if (g.ok) *bytes = g.total;
   }
-  const SplitPlan sp = plan_split(m, n, k, ds->sms);
-  if (sp.splits > 1 && sp.bytes > *bytes) *bytes = sp.bytes;
   return PQ8_OK;
 }
 

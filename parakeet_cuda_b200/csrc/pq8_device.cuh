@@ -156,6 +156,16 @@ __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t by
                "r"(bytes)
                : "memory");
 }
+// Shared -> shared bulk copy into a CTA of the cluster: dst and mbar are that
+// CTA's addresses (from map_to_rank), src this CTA's; bytes a multiple of 16,
+// both addresses 16-byte aligned. Completion is counted on the destination's
+// mbarrier (complete_tx).
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(smem_addr(src)), "r"(bytes), "r"(mbar)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until at most N committed bulk groups are still reading their shared-memory source.
 template <int N>

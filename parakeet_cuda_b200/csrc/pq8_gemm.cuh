@@ -68,13 +68,13 @@ struct GemmParams {
   int tma_store;  // 1: epilogue stages chunks in shared memory and writes them with TMA stores
   int w_f32;      // 1: w is a dense row-major FP32 [n, k] matrix (no header), rounded to TF32 by the converters
   // Split K (single GEMMs, single-CTA tiles): each output tile's K blocks are
-  // shared by k_splits (2, 4 or 8) CTAs launched as one cluster. Each stores
-  // its raw accumulator to `partial` ([tile][split][BN activation rows][128
-  // weight rows] fp32, through L2); after a cluster barrier, CTA s pulls rows
-  // [s, s + 1) * BN / k_splits of every split's partial back and runs the
-  // epilogue on their sums, added in split order.
+  // shared by k_splits (2, 4 or 8) CTAs launched as one cluster. Each stages
+  // its raw accumulator in shared memory; after a cluster barrier every split
+  // pushes each other split the rows that one finishes (CTA s: rows
+  // [s, s + 1) * BN / k_splits of the tile) with bulk copies between the
+  // CTAs' shared memories, and runs the epilogue on its rows' sums, added in
+  // split order.
   int k_splits;
-  float* partial;
 };
 
 template <int BN_, int STAGES_, int ASLOTS_, int ACC_, bool PAIR_, int GROUPS_ = 2, int GROUP_WARPS_ = 4,
@@ -112,10 +112,11 @@ struct GemmCfg {
   static constexpr int kOutOff = kWOff + WSTAGES * kRecordBytes;
   static constexpr int kBarOff = kOutOff + 4 * kOutChunkFloats * 4;
   // Split K: a split CTA stages its accumulator ([BN activation rows][128
-  // weight rows] fp32), and later the rows it finishes from every split, in the
-  // activation ring, idle by then (it runs one tile).
+  // weight rows] fp32) and receives the other splits' partials of the rows it
+  // finishes (as much again) in the activation and weight rings, idle by then
+  // (it runs one tile).
   static constexpr int kSplitPartialBytes = BN * 128 * 4;
-  static constexpr bool kSplitFits = !PAIR && STAGES * kXStageBytes >= kSplitPartialBytes;
+  static constexpr bool kSplitFits = !PAIR && kOutOff >= 2 * kSplitPartialBytes;
   static constexpr bool kSplitK = kSplitFits && BN == 128;  // the configuration split launches use
   static constexpr int kNumBars = 2 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
@@ -413,7 +414,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   uint64_t* acc_full = afree + ASLOTS;
   uint64_t* acc_empty = acc_full + ACC;
   uint64_t* drain = acc_empty + ACC;
-  uint64_t* red_full = drain + 1;  // [2 epilogue halves]: split-K rows pulled back
+  uint64_t* red_full = drain + 1;  // [2 epilogue halves]: split K, the other splits' rows received
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   int* bad_flag = reinterpret_cast<int*>(smem + C::kMiscOff + 8);
@@ -669,7 +670,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     auto split_rows = [&]() { return BN / p.k_splits / 2; };
     auto split_off = [&]() { return static_cast<int>(cluster_rank()) * (BN / p.k_splits) + half * split_rows(); };
     bool published = false;
-    bool red_pending = false;  // this half's pull-back copies issued and not seen land
+    bool received = false;  // this half's receive barrier waited for (it must be, before the CTA exits)
     int local = 0;
     griddep_wait();  // the residual and the output may be in use by the previous kernel
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
@@ -715,33 +716,45 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
       tc_fence_after();
       if (split) {
         // Split K: each half stages its chunks of this split's raw accumulator
-        // in the idle activation ring ([64 activation rows][128 weight rows]
-        // at half * 32 KB) and releases the accumulator; its elected thread
-        // stores them to this split's partial with one bulk copy and waits
-        // until they are written. Then the half meets the other splits of the
-        // tile at the cluster barrier (release / acquire).
-        float* const stage_h = reinterpret_cast<float*>(xs) + half * (BN / 2) * kTileRows;
+        // at the start of the idle activation ring ([BN activation rows][128
+        // weight rows]), releases the accumulator, and its elected thread sets
+        // the bytes its receive area expects. Then all splits of the tile meet
+        // at the cluster barrier: every mainloop is done, so every receive area
+        // is free, and every expectation is set.
+        float* const stage = reinterpret_cast<float*>(xs);
 #pragma unroll 1
         for (int cc = 0; cc < kChunks; ++cc) {
+          const int c = half * kChunks + cc;
           uint32_t v[E];
-          tmem_ld32(tmem + lane_base + acc * BN + (half * kChunks + cc) * E, v);
+          tmem_ld32(tmem + lane_base + acc * BN + c * E, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < E; ++j) stage_h[(cc * E + j) * kTileRows + r] = __uint_as_float(v[j]);
+          for (int j = 0; j < E; ++j) stage[(c * E + j) * kTileRows + r] = __uint_as_float(v[j]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[acc]);
-        fence_proxy_async_smem();
-        named_barrier_sync(1 + half, 128);
-        if (elected) {
-          bulk_s2g(p.partial + ((size_t)tile * BN + half * (BN / 2)) * kTileRows, stage_h, (BN / 2) * kTileRows * 4);
-          bulk_commit_group();
-          bulk_wait_group_all();
-        }
+        fence_proxy_async_smem();  // the staged values, read by the bulk-copy unit
+        if (elected)
+          mbar_expect_tx(&red_full[half], static_cast<uint32_t>((p.k_splits - 1) * split_rows() * kTileRows * 4));
         __syncwarp();
         cluster_sync();
         published = true;
+        // The first epilogue warp pushes every other split (d) the rows it
+        // finishes, one bulk copy per (d, epilogue half of d), into d's receive
+        // area ([half][source split][rows][128], after the staging area).
+        if (half == 0 && q == 0) {
+          const int S = p.k_splits, R = split_rows();
+          const int me = static_cast<int>(cluster_rank());
+          for (int i = lane; i < 2 * (S - 1); i += 32) {
+            const int d = (me + 1 + (i >> 1)) % S, h2 = i & 1;
+            const float* src = stage + (d * (BN / S) + h2 * R) * kTileRows;
+            const uint32_t dst = map_to_rank(stage + BN * kTileRows, static_cast<uint32_t>(d)) +
+                                 static_cast<uint32_t>((h2 * S + me) * R * kTileRows * 4);
+            bulk_s2s_cluster(dst, src, static_cast<uint32_t>(R * kTileRows * 4),
+                             map_to_rank(&red_full[h2], static_cast<uint32_t>(d)));
+          }
+        }
       }
       const int n_chunks = split ? 1 : kChunks;
 #pragma unroll 1
@@ -751,29 +764,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         if (m0 >= m) break;
         uint32_t v[E];
         if (split) {
-          // this half's split_rows rows: its elected thread pulls them back
-          // from every split's partial (one bulk copy each, all in flight)
-          // into the half's staging area; they are added in split order (onto
-          // +0, which leaves the first partial's values as they are)
-          const int rows = split_rows();
-          float* const recv = reinterpret_cast<float*>(xs) + half * (BN / 2) * kTileRows;
-          if (elected) {
-            const uint32_t bytes = static_cast<uint32_t>(rows * kTileRows * 4);
-            const int first = tile - static_cast<int>(cluster_rank());  // split 0 of this output tile
-            fence_proxy_async_global();  // the other splits' partials, read by the bulk-copy unit
-            mbar_expect_tx(&red_full[half], bytes * p.k_splits);
-            for (int sp = 0; sp < p.k_splits; ++sp)
-              bulk_g2s(recv + sp * rows * kTileRows, p.partial + ((size_t)(first + sp) * BN + (m0 - m_tile * BN)) * kTileRows,
-                       bytes, &red_full[half]);
-            red_pending = true;
-          }
+          // this half's split_rows rows, summed over the splits' partials in
+          // split order (onto +0, which leaves the first partial's values as
+          // they are): this split's from its staging area, the others' from
+          // the receive area once they have landed
+          const int rows = split_rows(), me = static_cast<int>(cluster_rank());
           if (!mbar_wait(&red_full[half], 0, abort_flag, status)) break;
-          red_pending = false;
+          received = true;
+          const float* const own = reinterpret_cast<const float*>(xs) + (m0 - m_tile * BN) * kTileRows + r;
+          const float* const recv = reinterpret_cast<const float*>(xs) + BN * kTileRows +
+                                    half * p.k_splits * rows * kTileRows + r;
 #pragma unroll
           for (int j = 0; j < E; ++j) v[j] = 0u;
 #pragma unroll 1
           for (int sp = 0; sp < p.k_splits; ++sp) {
-            const float* src = recv + sp * rows * kTileRows + r;
+            const float* src = sp == me ? own : recv + sp * rows * kTileRows;
 #pragma unroll
             for (int j = 0; j < E; ++j)
               if (j < rows) v[j] = __float_as_uint(__uint_as_float(v[j]) + src[j * kTileRows]);
@@ -854,14 +859,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
         }
       }
     }
-    if (elected) {
-      bulk_wait_group_all();
-      if (red_pending) mbar_drain(&red_full[half], 0);  // never leave copies landing in shared memory
-    }
+    if (elected) bulk_wait_group_all();
     if (split && !published) {  // gave up before the partials were published
       __syncwarp();
       cluster_sync();
     }
+    // never leave the other splits' copies landing in this CTA's shared memory
+    if (split && published && !received) mbar_drain(&red_full[half], 0);
   } else if (warp == C::kTmaWarp) {
     // ----------------------------------------------------- activation producer
     if (lane == 0) {
@@ -1031,7 +1035,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   }
 
   // Split K: the warps other than the epilogue's take part in the cluster
-  // barrier that publishes the partials (with nothing to publish).
+  // barrier that publishes the partials (with nothing to publish) ...
   const bool split_cluster = !SEQ && C::kSplitK && p.k_splits > 1;
   if (split_cluster && warp < C::kEpiWarp0) {
     __syncwarp();
@@ -1041,7 +1045,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   // The peer must not exit (freeing shared memory the leader's MMAs read) and the
   // tensor memory must not be freed before both CTAs are done.
   if constexpr (PAIR) cluster_sync();
-  if (split_cluster && warp < C::kEpiWarp0) cluster_wait();
+  if (split_cluster) {
+    // ... and no split leaves (the bulk copies out of its shared memory still
+    // running) before every split has received all of its rows.
+    if (warp < C::kEpiWarp0) cluster_wait();
+    cluster_sync();
+  }
   if (warp == C::kMmaWarp) {
     __syncwarp();
     tc_fence_after();

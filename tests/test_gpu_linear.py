@@ -265,14 +265,14 @@ SPLIT_CASES = [  # m, n, k, epilogue, bias, forced splits: units = M tiles x N t
 def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias, forced, monkeypatch):
     """pq8_linear splits K when the GEMM's tiles would fill at most half of the
     SMs (PQ8_LINEAR_SPLITS forces a count): the splits of a tile run as one
-    cluster, store their partials to the workspace and, after a cluster
-    barrier, each finishes its share of the tile's rows adding the partials in
-    split order. The result meets the north-star bar and the TF32-operand model
-    bar, and a repeat call is bit for bit the same; without a workspace the
-    GEMM runs unsplit (the bits of pq8_gemm)."""
+    cluster and, after a cluster barrier, push each other the rows each
+    finishes (bulk copies between their shared memories); each adds its rows'
+    partials in split order. The result meets the north-star bar and the
+    TF32-operand model bar, a repeat call is bit for bit the same, and so is a
+    call without any workspace (split K needs none)."""
     if forced:
         monkeypatch.setenv('PQ8_LINEAR_SPLITS', str(forced))
-    assert rt.lib.linear_workspace_size(m, n, k) > (rt.lib.gemv_workspace_size(m, n, k) if m <= 64 else 0)
+    assert rt.lib.linear_workspace_size(m, n, k) == (rt.lib.gemv_workspace_size(m, n, k) if m <= 64 else 0)
     rng = np.random.default_rng(1000 + m + n + k)
     raw = q8_0_blocks(rng, n, k)
     w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
@@ -295,9 +295,7 @@ def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias, forced, monk
     np.testing.assert_array_equal(y1.cpu().numpy(), y2.cpu().numpy())
     check_gemm(y1, x, raw, n, k, epi=epi, bias=bias, resid=resid, alpha=alpha)
     if m > 64:  # (up to 64 rows the dispatch may pick the GEMV, which needs its workspace)
-        y4 = rt.gemm(xd, w, **args)
-        torch.cuda.synchronize()
-        np.testing.assert_array_equal(y3.cpu().numpy(), y4.cpu().numpy())
+        np.testing.assert_array_equal(y1.cpu().numpy(), y3.cpu().numpy())
 
 
 def test_linear_split_k_in_graph_repeats(rt):
