@@ -883,7 +883,7 @@ extern "C" int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* pl
   std::vector<SeqTask> host(count);
   std::memset(host.data(), 0, sizeof(SeqTask) * host.size());
   if ((rc = seq_dependencies(tasks, count, host))) return rc;
-  int tile0 = 0, counter = 0;
+  int counter = 0;
   for (int i = 0; i < count; ++i) {
     const pq8_gemm_task& t = tasks[i];
     SeqTask& q = host[i];
@@ -914,10 +914,8 @@ extern "C" int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* pl
     p.m_tiles = (t.m + kSeqBN - 1) / kSeqBN;
     p.k_splits = 1;
     p.tma_store = (p.out_cols % 4 == 0) && aligned(t.y, 16);
-    q.tile0 = tile0;
     q.n_units = n_tiles;
     q.counter = counter;
-    tile0 += p.m_tiles * n_tiles;
     counter += p.m_tiles;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(t.k), static_cast<cuuint64_t>(t.m)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(t.k) * sizeof(float)};

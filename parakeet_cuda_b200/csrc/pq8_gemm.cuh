@@ -221,7 +221,6 @@ struct alignas(128) SeqTask {
   CUtensorMap tmap_x;  // activations [m, k], box 32 x BN rows
   CUtensorMap tmap_y;  // output [m, out_cols] (when p.tma_store)
   GemmParams p;
-  int tile0;     // first tile of this task in the sequence
   int n_units;   // tiles along N
   int counter;   // index of this task's first row-block counter
   int n_x_deps, n_out_deps;
