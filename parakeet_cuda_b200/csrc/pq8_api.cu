@@ -673,8 +673,9 @@ int seq_layout(const pq8_gemm_task* tasks, int count, SeqLayout* out) {
 // has ready by then, else the one ready soonest; a tile is a candidate only
 // once every tile it depends on has been taken. The order in which tiles are
 // taken is therefore one in which each comes after every tile it depends on,
-// and every CTA's list follows it. The model: a tile occupies its CTA's
-// tensor pipe for (1 + 0.33 x K blocks) us, starting no earlier than 1 us
+// and every CTA's list follows it. The model (per-tile times measured in the
+// sequence kernel): a tile occupies its CTA's tensor pipe for
+// (2 + 0.41 x K blocks) us, starting no earlier than 1 us
 // after its activation rows' producer row blocks completed; a row block
 // completes 3 us (the epilogue) after its last tile's mainloop, or after its
 // output's dependencies. Against taking every gridDim-th tile it evens out
@@ -683,7 +684,7 @@ int seq_layout(const pq8_gemm_task* tasks, int count, SeqLayout* out) {
 // PQ8_SEQUENCE_SCHEDULE=strided in the environment gives CTA c tiles c,
 // c + ctas, ... of the plan order instead (for comparison).
 void seq_schedule(const std::vector<SeqTask>& host, int ctas, std::vector<int>& start, std::vector<uint64_t>& order) {
-  constexpr double kTileFixed = 1.0, kPerBlock = 0.33, kEpilogue = 3.0, kLoad = 1.0;
+  constexpr double kTileFixed = 2.0, kPerBlock = 0.41, kEpilogue = 3.0, kLoad = 1.0;
   constexpr int kLookahead = 64;
   int n_counters = 0;
   long long total = 0;
