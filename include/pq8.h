@@ -386,9 +386,14 @@ PQ8_API int pq8_sequence_plan_size(const pq8_gemm_task* tasks, int count, size_t
  * earlier tasks that wrote or read those rows. Buffers are identified by
  * their start address and row width; two that overlap otherwise are refused
  * (PQ8_ERR_UNSUPPORTED_SHAPE), as is a task with more than 4 dependencies of
- * either kind. Reads each weight's packed header (PQ8_ERR_LAYOUT on a
- * mismatch) and synchronizes `stream`; not for stream capture. The plan stays
- * valid while the buffers and weights it names do. */
+ * either kind. The plan also holds the tile schedule for this device's SM
+ * count: tiles handed out in task order to the CTA a model of the launch frees
+ * first (list scheduling with a short lookahead; PQ8_SEQUENCE_SCHEDULE=strided
+ * in the environment gives CTA c tiles c, c + SMs, ... instead). Reads each
+ * weight's packed header (PQ8_ERR_LAYOUT on a mismatch) and synchronizes
+ * `stream`; not for stream capture. The plan stays valid while the buffers
+ * and weights it names do, on devices with the same SM count (a run on
+ * another records PQ8_ERR_LAYOUT). */
 PQ8_API int pq8_sequence_plan(const pq8_gemm_task* tasks, int count, void* plan, size_t plan_bytes, void* stream);
 /* Run a plan: one launch (one CTA per SM) that computes every task. Runs of
  * one plan must not overlap on the GPU (its completion counters are shared and
