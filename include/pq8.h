@@ -178,11 +178,16 @@ PQ8_API int pq8_gemv(const void* w, const float* x, float* y, const float* bias,
  * half of the SMs (each tile's K blocks shared by 2, 4 or 8 CTAs of one
  * cluster, which exchange their partial sums between their shared memories;
  * each CTA adds 1/S of the tile's rows in split order, so results are
- * deterministic; no workspace is involved). The workspace (zeroed once by
- * pq8_workspace_init) is the GEMV's and must hold
- * pq8_linear_workspace_size(m, n, k) bytes. PQ8_LINEAR_SPLITS=<s> in the
- * environment forces the split count (1 turns split K off). The drop-in for
- * Blas.linear (gpu.py:87-90). */
+ * deterministic; no workspace is involved). Activations not flagged
+ * PQ8_FLAG_X_TF32, 256 rows or more, are rounded to TF32 once into the
+ * workspace (one streaming pass, the same bits as rounding inside the GEMM)
+ * and the GEMM reads that copy; x itself is not written. The workspace
+ * (zeroed once by pq8_workspace_init) must hold
+ * pq8_linear_workspace_size(m, n, k) bytes (the GEMV's scratch, and m x k
+ * floats after its 64 KiB counter area for that copy); with less, the GEMM
+ * rounds the activations itself. PQ8_LINEAR_SPLITS=<s> in the environment
+ * forces the split count (1 turns split K off). The drop-in for Blas.linear
+ * (gpu.py:87-90). */
 PQ8_API int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid,
                int m, int n, int k, int epilogue, float alpha, int flags, void* workspace,
                size_t workspace_bytes, void* stream);

@@ -455,6 +455,23 @@ __global__ void round_tf32_kernel(uint32_t* __restrict__ x, long long n) {
     x[i] = tf32_round_bits(x[i]);
 }
 
+// x rounded to TF32 (as the GEMM's converters would round it) into y: one
+// streaming pass; n4 float4s, both 16-byte aligned. Launched with
+// programmatic dependent launch: x may be the previous kernel's output, and
+// the GEMM that reads y may start its set-up while this pass runs.
+__global__ void round_tf32_copy_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, long long n4) {
+  griddep_launch();
+  griddep_wait();
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    uint4 v = x[i];
+    v.x = tf32_round_bits(v.x);
+    v.y = tf32_round_bits(v.y);
+    v.z = tf32_round_bits(v.z);
+    v.w = tf32_round_bits(v.w);
+    y[i] = v;
+  }
+}
+
 int check_linear_args(const void* w, const float* x, const float* y, const float* resid, int m, int n, int k,
                       int epi) {
   if (m < 0 || n < 1) return PQ8_ERR_UNSUPPORTED_SHAPE;
@@ -1084,6 +1101,22 @@ int plan_split(int m, int n, int k, int sms) {
 }  // namespace
 }  // namespace pq8
 
+namespace pq8 {
+namespace {
+// Raw (not yet TF32-rounded) activations of at least this many rows are
+// rounded once into pq8_linear's workspace before the GEMM instead of by
+// every CTA's converter warps, which are the mainloop's bottleneck. Measured
+// on B200 (graph replay): M = 3000, N = 4096, K = 1024 takes 82 us rounding
+// in the GEMM against 48 us on rounded input; 3000 x 1024 x 4096 105 against
+// 50 us; 441 x 1024 x 4096 25.6 against 20.6 us; config 0 (M = 128) 14.2
+// against 12.8 us, about what a separate pass costs there.
+constexpr int kPreRoundRows = 256;
+size_t preround_bytes(int m, int k) {
+  return m >= kPreRoundRows ? kGemvCounterBytes + round256(sizeof(float) * static_cast<size_t>(m) * k) : 0;
+}
+}  // namespace
+}  // namespace pq8
+
 extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid, int m,
                           int n, int k, int epilogue, float alpha, int flags, void* workspace, size_t workspace_bytes,
                           void* stream) {
@@ -1093,11 +1126,25 @@ extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* 
     DeviceState* ds;
     int rc = device_state(&ds);
     if (rc) return rc;
+    if ((rc = check_linear_args(w, x, y, resid, m, n, k, epilogue))) return rc;
+    if (!aligned(x, 16)) return PQ8_ERR_MISALIGNED;
+    if (flags & ~(PQ8_FLAG_X_TF32 | PQ8_FLAG_OUT_TF32)) return PQ8_ERR_INVALID_ARGUMENT;
+    const size_t pre = preround_bytes(m, k);
+    if (!(flags & PQ8_FLAG_X_TF32) && pre > 0 && workspace != nullptr && workspace_bytes >= pre &&
+        aligned(workspace, 256)) {
+      // the activations, rounded once into the workspace (after its counter area)
+      float* xr = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kGemvCounterBytes);
+      const long long n4 = static_cast<long long>(m) * k / 4;
+      const long long blocks = std::min<long long>((n4 + 255) / 256, 8LL * ds->sms);
+      cudaError_t e = launch_pdl(round_tf32_copy_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                                 static_cast<cudaStream_t>(stream), reinterpret_cast<const uint4*>(x),
+                                 reinterpret_cast<uint4*>(xr), n4);
+      if (e != cudaSuccess) return to_code(e);
+      x = xr;
+      flags |= PQ8_FLAG_X_TF32;
+    }
     const int splits = plan_split(m, n, k, ds->sms);
     if (splits > 1) {
-      if ((rc = check_linear_args(w, x, y, resid, m, n, k, epilogue))) return rc;
-      if (!aligned(x, 16)) return PQ8_ERR_MISALIGNED;
-      if (flags & ~(PQ8_FLAG_X_TF32 | PQ8_FLAG_OUT_TF32)) return PQ8_ERR_INVALID_ARGUMENT;
       GemmParams p{};
       p.w = static_cast<const uint8_t*>(w);
       p.y = y;
@@ -1133,6 +1180,7 @@ extern "C" int pq8_linear_workspace_size(int m, int n, int k, size_t* bytes) {
     const GemvPlan g = plan_gemv(m, n, k, ds->sms);
     if (g.ok) *bytes = g.total;
   }
+  *bytes = std::max(*bytes, preround_bytes(m, k));  // raw activations rounded once (large M)
   return PQ8_OK;
 }
 

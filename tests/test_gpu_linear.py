@@ -272,7 +272,9 @@ def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias, forced, monk
     call without any workspace (split K needs none)."""
     if forced:
         monkeypatch.setenv('PQ8_LINEAR_SPLITS', str(forced))
-    assert rt.lib.linear_workspace_size(m, n, k) == (rt.lib.gemv_workspace_size(m, n, k) if m <= 64 else 0)
+    # the GEMV's scratch, or (256 rows and more) the once-rounded activations after the 64 KiB counter area
+    copy = (64 << 10) + ((4 * m * k + 255) // 256) * 256 if m >= 256 else 0
+    assert rt.lib.linear_workspace_size(m, n, k) == max(rt.lib.gemv_workspace_size(m, n, k) if m <= 64 else 0, copy)
     rng = np.random.default_rng(1000 + m + n + k)
     raw = q8_0_blocks(rng, n, k)
     w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
@@ -296,6 +298,42 @@ def test_linear_split_k_matches_oracle(rt, m, n, k, epi, with_bias, forced, monk
     check_gemm(y1, x, raw, n, k, epi=epi, bias=bias, resid=resid, alpha=alpha)
     if m > 64:  # (up to 64 rows the dispatch may pick the GEMV, which needs its workspace)
         np.testing.assert_array_equal(y1.cpu().numpy(), y3.cpu().numpy())
+
+
+@pytest.mark.parametrize('m,n,k,epi', [(300, 1024, 2048, EPI_RESIDUAL), (3000, 1024, 4096, EPI_NONE),
+                                      (256, 2048, 1024, EPI_GLU)])
+def test_linear_rounds_raw_activations_once(rt, m, n, k, epi):
+    """Raw activations of 256 or more rows: pq8_linear rounds them into its
+    workspace with one streaming pass and runs the GEMM on the rounded copy.
+    The result is bit for bit what rounding inside the GEMM gives (pq8_linear
+    without the workspace room, the same split decision; and pq8_gemm when
+    the shape is not split), and the caller's activations are left as they
+    were."""
+    rng = np.random.default_rng(m + k)
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k, LAYOUT_GLU if epi == EPI_GLU else LAYOUT_ROWS)
+    x = rng.normal(size=(m, k)).astype(np.float32)
+    bias = rng.normal(size=n).astype(np.float32)
+    n_out = n // 2 if epi == EPI_GLU else n
+    resid = rng.normal(size=(m, n_out)).astype(np.float32) if epi == EPI_RESIDUAL else None
+    xd = dev(x)
+    args = dict(bias=dev(bias), resid=dev(resid) if resid is not None else None, epilogue=epi,
+                alpha=0.5 if epi == EPI_RESIDUAL else 1.0)
+    assert rt.lib.linear_workspace_size(m, n, k) >= (64 << 10) + 4 * m * k
+    got = rt.linear(xd, w, **args)
+    want = rt.gemm(xd, w, **args)
+    small = torch.empty_like(got)
+    rt.lib.call('pq8_linear', w.pointer, xd.data_ptr(), small.data_ptr(), args['bias'].data_ptr(),
+                args['resid'].data_ptr() if resid is not None else None, m, n, k, epi, args['alpha'], 0,
+                rt.workspace.data_ptr(), 64 << 10, rt.stream())
+    torch.cuda.synchronize()
+    assert rt.device_status() == 0
+    np.testing.assert_array_equal(xd.cpu().numpy(), x)
+    np.testing.assert_array_equal(got.cpu().numpy(), small.cpu().numpy())
+    units = ((m + 127) // 128) * ((n + 127) // 128)
+    if 2 * units > 148:  # not split: the launch pq8_gemm makes
+        np.testing.assert_array_equal(got.cpu().numpy(), want.cpu().numpy())
+    check_gemm(got, x, raw, n, k, epi=epi, bias=bias, resid=resid, alpha=args['alpha'])
 
 
 def test_linear_split_k_in_graph_repeats(rt):
