@@ -1,6 +1,6 @@
 """GEMM sequences (pq8_sequence_plan / pq8_sequence_run): many GEMMs as one
-persistent launch, tiles ordered task after task, each tile waiting only for
-the row blocks it depends on.
+persistent launch, each CTA running its list of the plan's tile schedule and
+each tile waiting only for the row blocks it depends on.
 
 Every tile runs the same single-CTA BN = 192 kernel configuration as
 pq8_gemm with PQ8_GEMM_CONFIG=1, so a sequence must reproduce those launches
@@ -13,6 +13,7 @@ import pytest
 from parakeet_cuda_b200 import pq8
 from parakeet_cuda_b200.cuda_driver import Event
 from parakeet_cuda_b200.host import EncoderStackHost, HostRuntime
+from parakeet_cuda_b200.layers import LAYER_PLAN
 from parakeet_cuda_b200.synthetic import SyntheticParakeet, q8_0_blocks
 
 pytestmark = pytest.mark.gpu
@@ -42,15 +43,21 @@ def test_stack_sequence_equals_per_linear_launches(hrt, rows, monkeypatch):
     hrt.synchronize()
     want = snapshot(hrt, stack)
     monkeypatch.delenv('PQ8_GEMM_CONFIG')
-    for deps in ('model', 'buffers'):
-        stack.make_sequence(deps)
+    layer_order = tuple(entry[0] for entry in LAYER_PLAN)
+    # the plan's list schedule (default), and the strided assignment in the layer's own order
+    for deps, schedule, order in (('model', None, None), ('buffers', None, None), ('model', 'strided', layer_order)):
+        if schedule:
+            monkeypatch.setenv('PQ8_SEQUENCE_SCHEDULE', schedule)
+        stack.make_sequence(deps, order=order)
+        monkeypatch.delenv('PQ8_SEQUENCE_SCHEDULE', raising=False)
         for _ in range(2):  # the second run finds the counters reset by the first
             hrt.drv.memset(resid.pointer, 0, resid.nbytes, hrt.stream)
             stack.step_sequence()
             hrt.synchronize()
             got = snapshot(hrt, stack)
             for name in want:
-                np.testing.assert_array_equal(got[name], want[name], err_msg=f'{deps} {name}')
+                np.testing.assert_array_equal(got[name], want[name], err_msg=f'{deps} {schedule} {name}')
+    stack.make_sequence('model')
     graph = stack.capture(sequence=True)
     for _ in range(3):
         hrt.drv.memset(resid.pointer, 0, resid.nbytes, hrt.stream)
