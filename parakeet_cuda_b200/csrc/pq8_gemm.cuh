@@ -118,7 +118,7 @@ struct GemmCfg {
   static constexpr int kSplitPartialBytes = BN * 128 * 4;
   static constexpr bool kSplitFits = !PAIR && kOutOff >= 2 * kSplitPartialBytes;
   static constexpr bool kSplitK = kSplitFits && BN == 128;  // the configuration split launches use
-  static constexpr int kNumBars = 2 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1 + 2;
+  static constexpr int kNumBars = 3 * STAGES + 2 * WSTAGES + 2 * ASLOTS + 2 * ACC + 1 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kUsedBytes = kMiscOff + 24;
   static constexpr int kAColBase = ACC * BN;
@@ -414,6 +414,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   uint64_t* acc_empty = acc_full + ACC;
   uint64_t* drain = acc_empty + ACC;
   uint64_t* red_full = drain + 1;  // [2 epilogue halves]: split K, the other splits' rows received
+  uint64_t* xround = red_full + 2;  // activation stage rounded by the epilogue warps (epi_round_x)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kMiscOff + 4);
   int* bad_flag = reinterpret_cast<int*>(smem + C::kMiscOff + 8);
@@ -471,6 +472,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     mbar_init(drain, 1);
     mbar_init(&red_full[0], 1);
     mbar_init(&red_full[1], 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&xround[s], C::kEpiWarps);  // one arrival per epilogue warp
     fence_mbar_init();
   }
   if (warp == C::kTmaWarp && lane == 0 && !SEQ) {
@@ -500,6 +502,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
   TileCursor<C::kCtas, SEQ> src{p.m_tiles, p.k_blocks, p.k_splits,
                                 SEQ ? reinterpret_cast<const uint64_t*>(plan + hdr->order_offset) : nullptr};
   const int x_flags = SEQ ? (task_count > 0 ? tasks[0].p.flags : 0) : p.flags;
+  // Activations not yet rounded to TF32 are rounded in shared memory as each
+  // stage lands: by the epilogue warps when every CTA of a single-CTA launch
+  // runs one tile (they have nothing to do before its epilogue, and the
+  // converters are the mainloop's bottleneck), otherwise by the converters.
+  // (All tasks of a sequence share the X rounding flag.)
+  const bool round_x = !(x_flags & PQ8_FLAG_X_TF32);
+  const bool epi_round_x = !SEQ && !PAIR && round_x && num_tiles <= unit_stride;
   bool mma_issued = false;
 
   if (warp >= C::kConvWarp0 && warp < C::kConvWarp0 + C::kConvWarps) {
@@ -523,10 +532,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     ar.advance(grp);
     // Who vouches for this CTA's activation stage before the MMA: the
     // converters when they round it in place or when they are the pair peer's
-    // (whose barriers the leader cannot see); otherwise the scheduler. (All
-    // tasks of a sequence share the X rounding flag.)
-    const bool round_x = !(x_flags & PQ8_FLAG_X_TF32);
-    const bool vouch_x = round_x || (PAIR && !leader);
+    // (whose barriers the leader cannot see); otherwise the scheduler.
+    const bool vouch_x = (round_x && !epi_round_x) || (PAIR && !leader);
     bool w_ready = false;
     int tile = unit0, local = 0;
     uint32_t tile_first = 0;  // index of the current tile's first K block
@@ -672,6 +679,34 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     bool received = false;  // this half's receive barrier waited for (it must be, before the CTA exits)
     int local = 0;
     griddep_wait();  // the residual and the output may be in use by the previous kernel
+    if (epi_round_x && unit0 < num_tiles) {
+      // This CTA's one tile: round each activation stage to TF32 as it lands
+      // (the scheduler waits for xround before the MMA reads the stage).
+      constexpr int kEpiThreads = C::kEpiWarps * 32;
+      constexpr int kPer = C::kXStageBytes / 16 / kEpiThreads;
+      static_assert(C::kXStageBytes / 16 % kEpiThreads == 0, "X stage must split evenly over the epilogue");
+      const int et = static_cast<int>(threadIdx.x) - C::kEpiWarp0 * 32;
+      const int KB = src.at(unit0, rank, plan).kb;
+      Ring<STAGES> xr;
+      for (int kb = 0; kb < KB; ++kb, xr.advance(1)) {
+        if (!mbar_wait(&xfull[xr.idx], xr.phase, abort_flag, status)) break;
+        uint4* xv = reinterpret_cast<uint4*>(xs + xr.idx * C::kXStageBytes);
+        uint4 v[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) v[i] = xv[et + kEpiThreads * i];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          v[i].x = tf32_round_bits(v[i].x);
+          v[i].y = tf32_round_bits(v[i].y);
+          v[i].z = tf32_round_bits(v[i].z);
+          v[i].w = tf32_round_bits(v[i].w);
+          xv[et + kEpiThreads * i] = v[i];
+        }
+        fence_proxy_async_smem();  // the rounded values, read by the tensor cores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xround[xr.idx]);
+      }
+    }
     for (int tile = unit0; tile < num_tiles; tile += unit_stride, ++local) {
       const TileRef t = src.at(tile, rank, plan);
       const int n_tile = t.n_tile, m_tile = t.m_tile;
@@ -932,8 +967,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
     if (leader) {
       constexpr int RK = C::kRendezvousBlocks;
       // The leader's activation stages are vouched for here unless its
-      // converters round them in place.
-      const bool sched_x = (x_flags & PQ8_FLAG_X_TF32) != 0;
+      // converters round them in place (landed, or rounded by the epilogue
+      // warps).
+      const bool sched_x = !round_x || epi_round_x;
+      uint64_t* const xready = epi_round_x ? xround : xfull;
       Ring<ASLOTS> ar;
       Ring<STAGES> xr;
       bool bad = false;
@@ -947,7 +984,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, ASLOTS, ACC, PAIR, GROUPS,
           if (lane == 0)
             for (int b = 0; b < nb && !bad; ++b) {
               bad = !mbar_wait(&conv[ar.idx], ar.phase, abort_flag, status);
-              if (sched_x) bad = bad || !mbar_wait(&xfull[xr.idx], xr.phase, abort_flag, status);
+              if (sched_x) bad = bad || !mbar_wait(&xready[xr.idx], xr.phase, abort_flag, status);
               ar.advance(1);
               xr.advance(1);
             }
