@@ -194,7 +194,9 @@ __device__ __forceinline__ void slice_matvec(uint8_t* smem, const SmemQ8& s, con
     const uint4* q1 = reinterpret_cast<const uint4*>(smem + s.q1);
     const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem + s.sc);
     const int kb1 = min(KB, (sl + 1) * per);
-#pragma unroll 1
+    // narrow passes unroll two K blocks so the next block's shared-memory loads
+    // overlap this block's arithmetic (same order of additions)
+#pragma unroll(MT <= 4 ? 2 : 1)
     for (int kb = sl * per; kb < kb1; ++kb)
       gemv_block<MT>(q0[kb * R + r], q1[kb * R + r], sc[kb * R + r], xs + kb * 32, K, acc);
 #pragma unroll
@@ -203,8 +205,19 @@ __device__ __forceinline__ void slice_matvec(uint8_t* smem, const SmemQ8& s, con
   __syncthreads();
   for (int i = t; i < R * MT; i += kDecodeThreads) {
     const int idx = (i / MT) * kDecodeGroup + i % MT;
+    // partials added in range order; four loads in flight per group of adds
+    const float* pp = part + idx;
+    const int step = R * kDecodeGroup;
     float z = 0.0f;
-    for (int q = 0; q < S; ++q) z += part[q * R * kDecodeGroup + idx];
+    int q = 0;
+    for (; q + 4 <= S; q += 4) {
+      const float a = pp[q * step], b = pp[(q + 1) * step], c = pp[(q + 2) * step], d = pp[(q + 3) * step];
+      z += a;
+      z += b;
+      z += c;
+      z += d;
+    }
+    for (; q < S; ++q) z += pp[q * step];
     zs[idx] = z;
   }
   __syncthreads();
@@ -228,7 +241,7 @@ __device__ __forceinline__ void slice_matvec_rows(uint8_t* smem, const SmemQ8& s
 // with the largest share (ceil(n / grid) rows of each matrix).
 struct DecodeLayout {
   SmemQ8 joint, lstm[2], pred;
-  uint32_t xs, part, zs, ctl, total;
+  uint32_t xs, part, zs, ctl, bias, total;
 };
 
 __host__ __device__ inline uint32_t decode_align16(uint32_t v) { return (v + 15u) & ~15u; }
@@ -261,6 +274,8 @@ __host__ __device__ inline DecodeLayout decode_layout(int rows_joint, int units,
   off = decode_align16(off + 4u * kDecodeGroup * rmax);
   L.ctl = off;
   off = decode_align16(off + 4u * (kTdtStateWords * m + 2 * kDecodeMaxStreams + 8));
+  L.bias = off;  // the biases of the CTA's rows: joint, LSTM 0 and 1 (gate-major), pred
+  off = decode_align16(off + 4u * (rows_joint + 8 * units + rows_pred));
   L.total = off;
   return L;
 }
@@ -385,6 +400,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) tdt_decode_kernel(const Dec
       return (u >> 5) * 128 + g * 32 + (u & 31);
     });
   }
+  // The biases of the CTA's rows, read once (the phases' epilogues read them
+  // right after their products, where a global load would be a round trip).
+  float* bj = reinterpret_cast<float*>(smem + L.bias);  // [j1 - j0]
+  float* bl = bj + (j1 - j0);                           // [2][4][U]: gate g of unit u0 + ul
+  float* bp = bl + 8 * U;                               // [p1 - p0]
+  for (int i = t; i < j1 - j0; i += kDecodeThreads) bj[i] = p.b_joint[j0 + i];
+  for (int i = t; i < 8 * U; i += kDecodeThreads) bl[i] = p.b_lstm[i / (4 * U)][(i / U) % 4 * H + u0 + i % U];
+  for (int i = t; i < p1 - p0; i += kDecodeThreads) bp[i] = p.b_pred[p0 + i];
   for (int i = t; i < m * kTdtStateWords; i += kDecodeThreads) ctl[i] = p.state[i];
   __syncthreads();
   if (!p.resume && t < m) ctl[t * kTdtStateWords + 7] = 0;  // committed slot of a fresh decode
@@ -426,11 +449,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) tdt_decode_kernel(const Dec
         for (int i = t; i < U * mc; i += kDecodeThreads) {
           const int ul = i % U, j = i / U, u = u0 + ul;
           const int b = list[g0 + j], cm = ctl[b * kTdtStateWords + 7];
-          const float* bias = p.b_lstm[l];
-          const float gi = zs[(0 * U + ul) * kDecodeGroup + j] + bias[0 * H + u];
-          const float gf = zs[(1 * U + ul) * kDecodeGroup + j] + bias[1 * H + u];
-          const float gg = zs[(2 * U + ul) * kDecodeGroup + j] + bias[2 * H + u];
-          const float go = zs[(3 * U + ul) * kDecodeGroup + j] + bias[3 * H + u];
+          const float* bias = bl + l * 4 * U + ul;
+          const float gi = zs[(0 * U + ul) * kDecodeGroup + j] + bias[0 * U];
+          const float gf = zs[(1 * U + ul) * kDecodeGroup + j] + bias[1 * U];
+          const float gg = zs[(2 * U + ul) * kDecodeGroup + j] + bias[2 * U];
+          const float go = zs[(3 * U + ul) * kDecodeGroup + j] + bias[3 * U];
           const float si = 1.0f / (1.0f + expf(-gi)), sf = 1.0f / (1.0f + expf(-gf));
           const float so = 1.0f / (1.0f + expf(-go));
           const float cn = sf * (i == t ? c_pre : __ldcg(cbuf(l, cm, b) + u)) + si * tanhf(gg);
@@ -453,7 +476,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) tdt_decode_kernel(const Dec
         slice_matvec_rows(smem, sp, xs, part, zs, mc);
         for (int i = t; i < sp.rows * mc; i += kDecodeThreads) {
           const int r = i % sp.rows, j = i / sp.rows;
-          p.pred[(size_t)list[g0 + j] * KJ + p0 + r] = zs[r * kDecodeGroup + j] + p.b_pred[p0 + r];
+          p.pred[(size_t)list[g0 + j] * KJ + p0 + r] = zs[r * kDecodeGroup + j] + bp[r];
         }
       }
     }
@@ -496,7 +519,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) tdt_decode_kernel(const Dec
         int i0 = INT_MAX, i1 = INT_MAX;
         for (int r = lane; r < sj.rows; r += 32) {
           const int row = j0 + r;
-          const float z = zs[r * kDecodeGroup + jw] + p.b_joint[row];
+          const float z = zs[r * kDecodeGroup + jw] + bj[r];
           if (row < p.vocab) argmax_merge(v0, i0, z, row);
           else argmax_merge(v1, i1, z, row);
         }
