@@ -1062,17 +1062,6 @@ extern "C" int pq8_gemv(const void* w, const float* x, float* y, const float* bi
 namespace pq8 {
 namespace {
 
-// pq8_linear's choice for PQ8_LINEAR_GEMV_MAX_M < m <= PQ8_GEMV_MAX_M, from
-// B200 measurements of both kernels at 9-64 rows (N 65-8198, K 640-4096, CUDA
-// graphs of back-to-back calls): the GEMV costs ~4 us plus ~0.1 ns per
-// multiply-add of its 8-row groups (FP32 FMA), the GEMM (one wave of tiles at
-// these sizes) ~3.3 us plus ~0.4 us per 32-wide K block. Within 6 % of the
-// faster kernel at every measured point.
-bool gemv_faster(int m, int n, int k) {
-  const double macs = static_cast<double>((m + 7) / 8 * 8) * n * k;
-  return 4.0 + 1.0e-7 * macs < 3.3 + 0.4 * (k / 32);
-}
-
 // Split K for pq8_linear's GEMM path: when BN = 128 tiles would fill at most
 // half of the SMs, each tile's K blocks are shared by S = 2, 4 or 8 CTAs (S x
 // tiles within the SM count, at least 4 K blocks each) launched as clusters
@@ -1084,11 +1073,11 @@ bool gemv_faster(int m, int n, int k) {
 // 17.0 us in 2; K = 640 in 2 splits would lose 0.8-1.6 us).
 // PQ8_LINEAR_SPLITS=<S> forces S (rounded down to a power of two, within the
 // same limits; 1 turns split K off).
-int plan_split(int m, int n, int k, int sms) {
+int plan_split(int m, int n, int k, int sms, bool allow_force = true) {
   const long long units = static_cast<long long>((m + 127) / 128) * ((n + kTileRows - 1) / kTileRows);
   const int kb = k / 32;
   long long s = units * 2 > sms ? 1 : std::min<long long>({sms / units, kb / 4, 8});
-  const char* force = std::getenv("PQ8_LINEAR_SPLITS");
+  const char* force = allow_force ? std::getenv("PQ8_LINEAR_SPLITS") : nullptr;
   if (force) s = std::min<long long>({std::max(1, std::atoi(force)), sms / units, kb / 2, 8});
   int p2 = 1;
   while (p2 * 2 <= s) p2 *= 2;
@@ -1096,6 +1085,24 @@ int plan_split(int m, int n, int k, int sms) {
   // every split gets K blocks: splits of ceil(kb / S) blocks, the last one shorter
   while (p2 > 1 && (p2 - 1) * ((kb + p2 - 1) / p2) >= kb) p2 /= 2;
   return p2;
+}
+
+// pq8_linear's choice for PQ8_LINEAR_GEMV_MAX_M < m <= PQ8_GEMV_MAX_M, from
+// B200 measurements of both kernels at 9-64 rows (N 1024-8197, K 640-4096,
+// CUDA graphs of back-to-back calls, weights streamed from HBM): the GEMV
+// costs ~4 us plus ~0.1 ns per multiply-add of its 8-row groups (FP32 FMA),
+// twice that per multiply-add at K = 4096 (its K splits run long); the GEMM
+// ~3.3 us plus ~0.4 us per 32-wide K block unsplit (one wave of tiles at
+// these sizes), or ~9.5 us plus ~0.42 us per K block of one split when
+// plan_split shares the K blocks among a cluster. Within ~1.3 us of the
+// faster kernel at every measured point.
+bool gemv_faster(int m, int n, int k, int sms) {
+  const int kb = k / 32;
+  const double macs = static_cast<double>((m + 7) / 8 * 8) * n * k;
+  const double gemv = 4.0 + 1.0e-7 * macs * (1.0 + std::max(0, kb - 32) / 96.0);
+  const int s = plan_split(m, n, k, sms, false);  // the policy's splits (PQ8_LINEAR_SPLITS does not steer this)
+  const double gemm = s > 1 ? 9.5 + 0.42 * ((kb + s - 1) / s) : 3.3 + 0.4 * kb;
+  return gemv < gemm;
 }
 
 }  // namespace
@@ -1120,8 +1127,18 @@ size_t preround_bytes(int m, int k) {
 extern "C" int pq8_linear(const void* w, const float* x, float* y, const float* bias, const float* resid, int m,
                           int n, int k, int epilogue, float alpha, int flags, void* workspace, size_t workspace_bytes,
                           void* stream) {
-  if (m >= 1 && (m <= PQ8_LINEAR_GEMV_MAX_M || (m <= PQ8_GEMV_MAX_M && gemv_faster(m, n, k))))
+  if (m >= 1 && m <= PQ8_GEMV_MAX_M && k > 0 && k % 32 == 0 && n >= 1) {
+    bool gemv = m <= PQ8_LINEAR_GEMV_MAX_M;
+    if (!gemv) {
+      DeviceState* ds;
+      int rc = device_state(&ds);
+      if (rc) return rc;
+      gemv = gemv_faster(m, n, k, ds->sms);
+    }
+    if (gemv) return pq8_gemv(w, x, y, bias, resid, m, n, k, epilogue, alpha, workspace, workspace_bytes, stream);
+  } else if (m >= 1 && m <= PQ8_LINEAR_GEMV_MAX_M) {
     return pq8_gemv(w, x, y, bias, resid, m, n, k, epilogue, alpha, workspace, workspace_bytes, stream);
+  }
   if (m >= 1 && k > 0 && k % 32 == 0 && n >= 1) {
     DeviceState* ds;
     int rc = device_state(&ds);

@@ -216,8 +216,9 @@ def test_linear_dispatch_gemv_matches_gemm(rt):
         np.testing.assert_allclose(y, gold, atol=2e-4, rtol=2e-4)
 
 
-@pytest.mark.parametrize('m,n,k,kernel', [(16, 1024, 4096, 'gemv'), (24, 640, 640, 'gemv'), (48, 8198, 640, 'gemm'),
-                                          (64, 4096, 1024, 'gemm'), (9, 129, 1024, 'gemv')])
+@pytest.mark.parametrize('m,n,k,kernel', [(16, 1024, 4096, 'gemm'), (24, 640, 640, 'gemv'), (48, 8198, 640, 'gemm'),
+                                          (64, 4096, 1024, 'gemm'), (9, 129, 1024, 'gemv'), (16, 4096, 1024, 'gemv'),
+                                          (24, 4096, 1024, 'gemm')])
 def test_linear_dispatch_9_to_64_rows(rt, m, n, k, kernel, monkeypatch):
     """pq8_linear sends 9..64 rows to whichever kernel its measured cost model
     finds faster: the result is bit for bit that kernel's (for the tensor-core
