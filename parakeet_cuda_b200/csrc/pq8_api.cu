@@ -639,7 +639,7 @@ extern "C" int pq8_gemm(const void* w, const float* x, float* y, const float* bi
 namespace pq8 {
 namespace {
 
-constexpr int kSeqBN = 192, kSeqStages = 5, kSeqSlots = 4, kSeqAcc = 2, kSeqWStages = 8;
+constexpr int kSeqBN = 192, kSeqStages = 6, kSeqSlots = 4, kSeqAcc = 2, kSeqWStages = 4;
 using SeqCfg = GemmCfg<kSeqBN, kSeqStages, kSeqSlots, kSeqAcc, false, 2, 4, 32, kSeqWStages>;
 constexpr int kSeqCfgId = 16;  // DeviceState::attr_set slot of the sequence kernel
 constexpr size_t kSeqHeaderBytes = sizeof(SeqPlanHeader);
