@@ -318,24 +318,34 @@ int gemv_cluster_fit(DeviceState* ds, const GemvParams& p, const GemvPlan& g, in
   }
   const int max_smem = static_cast<int>(sizeof(float) * kGemvXSmemFloats + 128 +
                                         sizeof(float) * kGemvMaxClusterSplits * kGemvThreads * MT);
+  // The query enqueues nothing; relaxed capture mode lets it run while the
+  // caller's stream is being captured into a graph (a shape's first call).
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e != cudaSuccess) return to_code(e);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.n_tiles * g.splits, g.groups);
-  cfg.blockDim = dim3(kGemvThreads);
-  cfg.dynamicSmemBytes = ((sizeof(float) * MT * g.kbps * 32 + 127) & ~size_t(127)) +
-                         sizeof(float) * g.splits * kGemvThreads * MT;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = g.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   int n = 0;
-  e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
-  if (e != cudaSuccess) return to_code(e);
+  if (e == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.n_tiles * g.splits, g.groups);
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = ((sizeof(float) * MT * g.kbps * 32 + 127) & ~size_t(127)) +
+                           sizeof(float) * g.splits * kGemvThreads * MT;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = g.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+  }
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (e != cudaSuccess) {  // no answer: keep the plan as it is (not cached)
+    cudaGetLastError();
+    *fit = 1 << 30;
+    return PQ8_OK;
+  }
   std::lock_guard<std::mutex> lock(g_mutex);
   ds->gemv_cluster_fit[key] = n;
   *fit = n;

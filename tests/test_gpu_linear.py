@@ -576,3 +576,37 @@ def test_gemv_batch_matches_oracle(rt):
     for (y, *_), f in zip(golds, first):
         assert torch.equal(y, f)
     assert rt.device_status() == 0
+
+
+def test_gemv_first_call_in_graph_matches_eager(rt):
+    """A GEMV shape whose K splits would form clusters of more than 8 CTAs
+    asks, on its first call, how many such clusters the GPU holds (an
+    occupancy query, which may fall on a stream being captured into a graph):
+    the captured launch must run the same plan as an eager call, bit for bit.
+    (N = 4096, K = 1024 at 3 rows: 32 clusters of 16, which do not all fit.)"""
+    rng = np.random.default_rng(31)
+    m, n, k = 3, 4096, 1024
+    raw = q8_0_blocks(rng, n, k)
+    w = rt.pack(raw, n, k)
+    xh = rng.normal(size=(m, k)).astype(np.float32)
+    x = dev(xh)
+    rt.ensure_workspace(m, n, k)
+    ws = rt.workspace
+    y_graph = torch.empty(m, n, device='cuda')
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            rt.lib.call('pq8_gemv', w.pointer, x.data_ptr(), y_graph.data_ptr(), None, None, m, n, k, EPI_NONE,
+                        1.0, ws.data_ptr(), ws.numel(), s.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    y = torch.empty(m, n, device='cuda')
+    rt.lib.call('pq8_gemv', w.pointer, x.data_ptr(), y.data_ptr(), None, None, m, n, k, EPI_NONE, 1.0,
+                ws.data_ptr(), ws.numel(), rt.stream())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(y_graph.cpu().numpy(), y.cpu().numpy())
+    np.testing.assert_allclose(y.cpu().numpy(), q8.gemm(xh, raw, n, k), atol=2e-4, rtol=2e-4)
+    del g
+    assert rt.device_status() == 0
