@@ -39,7 +39,7 @@ struct DeviceState {
   bool attr_set[24] = {};
   // GEMV launches with clusters of 9-16 CTAs: how many such clusters the GPU
   // holds at once, per (rows per group, splits, K blocks per split); guarded by g_mutex
-  std::map<int, int> gemv_cluster_fit;
+  std::map<long long, int> gemv_cluster_fit;
   cublasHandle_t blas = nullptr;  // attention GEMMs; created on first use, guarded by blas_mutex
   std::mutex blas_mutex;
 };
@@ -307,7 +307,7 @@ GemvPlan plan_gemv(int m, int n, int k, int sms) {
 template <int MT>
 int gemv_cluster_fit(DeviceState* ds, const GemvParams& p, const GemvPlan& g, int* fit) {
   auto kernel = gemv_kernel<MT, false>;
-  const int key = (MT << 16) | (g.splits << 8) | g.kbps;
+  const long long key = (static_cast<long long>(MT) << 40) | (static_cast<long long>(g.splits) << 20) | g.kbps;
   {
     std::lock_guard<std::mutex> lock(g_mutex);
     auto it = ds->gemv_cluster_fit.find(key);
